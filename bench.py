@@ -1,0 +1,560 @@
+"""Benchmark of the quantized-KV decode hot path on B200.
+
+Default workload: KIVI INT4 long-context decode,
+32 requests at context 32768, 64 query / 8 KV heads, head 128, group 128,
+residual 128, sharded by KV head across N GPUs (GPU i owns KV heads
+[8i/N, 8(i+1)/N) and their query heads) with one NCCL all-gather of the
+attention outputs per step. The cache of every request is built the way the
+reference builds it — bulk prefill of L-1 tokens (floor(n/r)*r straight to
+int4, the rest to the bf16 window) plus one decode write — with K/V ~ N(0,1)
+in bf16 and x10 key outliers on 2% of (head, channel) pairs.
+
+One step = one decode-attention pass of every request over its int4 pages and
+bf16 windows (``qkv_kivi_paged_decode``: split-KV kernel + combine) followed,
+for N > 1, by the all-gather. The caches (1.22 GB / N per GPU) exceed the
+126 MB L2, so no L2 flush is needed between steps.
+
+Reported on one JSON line (rank 0):
+  value     tokens/s/layer over all GPUs, inputs resident in HBM, device-timed
+            with CUDA events, max over ranks;
+  roofline  algorithmic bytes per decode call / its CUDA-event time vs the
+            measured HBM copy bandwidth (MEASURED_PEAKS.json);
+  pack      KIVI pack GB/s (config 2 definition, 5248 B/token);
+  e2e       the same metric through the plugin API — the KIVI mixin's
+            ``forward()`` in DecodeOnly state with pinned host q/k/v copied in
+            and the output copied out every step;
+  cpu_baseline  the reference's CPU path (numpy port in oracle/) on a bounded
+            sample of the workload, rank 0, N = 1 only.
+
+``--impl reference`` times that CPU path alone (rank 0) on the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+from types import SimpleNamespace
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "vllm-ascend-quantized-kv-cache-hust_b200"))
+
+METRIC = "quantized-KV decode attn tokens/s/layer"
+UNIT = "tokens/s/layer"
+
+CONFIG5 = dict(batch=32, context=32768, num_heads=64, num_kv_heads=8, head_size=128, group_size=128,
+               residual=128, block_size=128)
+CONFIG2_PACK = dict(tokens=8192, num_kv_heads=8, head_size=128, group_size=128, block_size=128)
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=30)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# CPU path (the reference's algorithm, numpy port in oracle/)
+# ---------------------------------------------------------------------------
+
+
+def cpu_reference_sample(cfg, seed=0):
+    """Builds one request of the workload on the host and returns a closure
+    running the reference's CPU decode path on it: gather + dequantise the
+    int4 history (kivi_dequant_gather_cache), overwrite the residual tail,
+    fp32 attention (_forward_kivi_dense_attention)."""
+    import numpy as np
+
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import qkv_oracle as O
+
+    rng = np.random.default_rng(seed)
+    L, H, D, g, blk, r = (cfg[k] for k in ("context", "num_kv_heads", "head_size", "group_size", "block_size",
+                                           "residual"))
+    Hq = cfg["num_heads"]
+    pages = (L + blk - 1) // blk
+    hist = ((L - 1) // r) * r  # bulk prefill of L-1 tokens flushes floor((L-1)/r)*r
+    nbp = pages
+    views = [
+        np.zeros((nbp, H, D, blk // 8), np.int32), np.ones((nbp, H, D, blk // g), np.float32),
+        np.zeros((nbp, H, D, blk // g), np.float32), np.zeros((nbp, blk, H, D // 8), np.int32),
+        np.ones((nbp, blk, H, D // g), np.float32), np.zeros((nbp, blk, H, D // g), np.float32),
+    ]
+    # packed words / scales drawn directly (the CPU timing does not depend on
+    # how they were produced)
+    views[0][:] = rng.integers(-(2 ** 31), 2 ** 31 - 1, size=views[0].shape, dtype=np.int64).astype(np.int32)
+    views[3][:] = rng.integers(-(2 ** 31), 2 ** 31 - 1, size=views[3].shape, dtype=np.int64).astype(np.int32)
+    views[1][:] = rng.uniform(0.05, 0.5, views[1].shape)
+    views[4][:] = rng.uniform(0.05, 0.5, views[4].shape)
+    views[2][:] = rng.uniform(-3, 0, views[2].shape)
+    views[5][:] = rng.uniform(-3, 0, views[5].shape)
+    bt = rng.permutation(nbp).reshape(1, nbp)
+    res = L - hist
+    kwin = [O.bf16_round(rng.standard_normal((res, H, D)).astype(np.float32))]
+    vwin = [O.bf16_round(rng.standard_normal((res, H, D)).astype(np.float32))]
+    q = O.bf16_round(rng.standard_normal((1, Hq, D)).astype(np.float32))
+
+    def run():
+        dk, dv = O.kivi_dequant_gather(*views, bt, [L], g, target_bf16=True)
+        dk, dv = O.overwrite_residual_tail(dk, dv, [L], kwin, vwin)
+        return O.dense_attention(q, dk, dv, [1], [L], D ** -0.5, causal=True)
+
+    return run
+
+
+def cpu_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+
+        n = [i.get("num_threads", 1) for i in threadpool_info()]
+        return max(n) if n else 1
+    except Exception:
+        return 1
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg = CONFIG5
+    run = cpu_reference_sample(cfg)
+    for _ in range(max(args.warmup, 0)):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        run()
+    dt = (time.perf_counter() - t0) / max(args.steps, 1)
+    value = 1.0 / dt  # one decode token of one request per step
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dt * 1e3,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "int4/bf16->fp32",
+        "data": "synthetic",
+        "config": workload_config(cfg, args.gpus),
+        "cpu_baseline": {
+            "value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+            "sample": "one request of the workload per step (context 32768, 64 q / 8 kv heads); the CPU path is "
+                      "linear in requests, so tokens/s/layer of the sample is that of the full batch",
+        },
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(cfg, n):
+    return {
+        "workload": "BASELINE config 5: KIVI INT4 long-context decode, KV-head sharded",
+        "batch": cfg["batch"], "context": cfg["context"], "num_heads": cfg["num_heads"],
+        "num_kv_heads": cfg["num_kv_heads"], "head_size": cfg["head_size"], "group_size": cfg["group_size"],
+        "residual": cfg["residual"], "block_size": cfg["block_size"],
+        "parallelism": f"kv-head shard x{n}" + (" + NCCL all-gather" if n > 1 else ""),
+        "l2": "inputs larger than L2 (KIVI cache 1.22 GB / N per GPU), no flush",
+    }
+
+
+# ---------------------------------------------------------------------------
+# GPU build of the workload
+# ---------------------------------------------------------------------------
+
+
+def build_workload(cfg, rank, world, device, seed=1234):
+    """Per-rank KIVI caches + windows of config 5, built with the pack kernels
+    following the reference's bulk-prefill + one-decode-write semantics."""
+    import torch
+
+    from qkv_b200.methods.kivi_int4.byte_cache import KiviByteCacheLayout, kivi_caches_from_byte_tensors
+    from qkv_b200.ops import kivi_pack_key_cache, kivi_pack_value_cache
+
+    B, L, Hq, H, D, g, r, blk = (cfg[k] for k in ("batch", "context", "num_heads", "num_kv_heads", "head_size",
+                                                 "group_size", "residual", "block_size"))
+    assert H % world == 0 and Hq % world == 0
+    Hl, Hql = H // world, Hq // world
+    pages = (L + blk - 1) // blk
+    spare = 2  # pages per request for e2e steps beyond the context
+    nb = B * (pages + spare)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    cpu_gen = torch.Generator().manual_seed(seed)
+    lay = KiviByteCacheLayout(num_blocks=nb, block_size=blk, num_kv_heads=Hl, head_size=D, group_size=g)
+    kbuf = torch.zeros(nb, blk, Hl, lay.bytes_per_token_head, dtype=torch.uint8, device=device)
+    vbuf = torch.zeros_like(kbuf)
+    views = kivi_caches_from_byte_tensors(kbuf, vbuf, lay)
+    perm = torch.randperm(nb, generator=cpu_gen)
+    bt = perm.view(B, pages + spare).to(torch.int32)
+    # key outliers: x10 on 2% of (head, channel) pairs of the FULL model; this
+    # rank keeps its heads' share
+    n_out = max(1, int(0.02 * H * D))
+    out_idx = torch.randperm(H * D, generator=cpu_gen)[:n_out]
+    kscale = torch.ones(H * D)
+    kscale[out_idx] = 10.0
+    kscale = kscale.view(H, D)[rank * Hl:(rank + 1) * Hl].to(device)
+    hist = ((L - 1) // r) * r
+    res = L - hist
+    rk = torch.zeros(B + 1, r, Hl, D, dtype=torch.bfloat16, device=device)
+    rv = torch.zeros_like(rk)
+    pos = torch.arange(L, device=device)
+    for b in range(B):
+        k = (torch.randn(L, Hl, D, generator=gen, device=device) * kscale).to(torch.bfloat16)
+        v = torch.randn(L, Hl, D, generator=gen, device=device).to(torch.bfloat16)
+        slots = bt[b].to(device).long()[pos // blk] * blk + pos % blk
+        kivi_pack_key_cache(k[:hist].contiguous(), slots[:hist].contiguous(), *views[:3], g, validate_slots=False)
+        kivi_pack_value_cache(v[:hist].contiguous(), slots[:hist].contiguous(), *views[3:], g)
+        rk[b, :res] = k[hist:]
+        rv[b, :res] = v[hist:]
+    torch.cuda.synchronize(device)
+    q = torch.randn(B, Hql, D, generator=gen, device=device).to(torch.bfloat16)
+    # window state of request b: row b, start 0, both windows = the last `res` positions
+    state = torch.tensor([[b, 0, res, 0, res, L] for b in range(B)], dtype=torch.int32, device=device)
+    return SimpleNamespace(
+        views=views, kbuf=kbuf, vbuf=vbuf, layout=lay, bt=bt, bt_dev=bt.to(device), rk=rk, rv=rv, q=q,
+        state=state, seq_lens=torch.full((B,), L, dtype=torch.int32, device=device), hist=hist, res=res,
+        B=B, L=L, Hl=Hl, Hql=Hql, D=D, g=g, r=r, blk=blk, nb=nb, pages=pages,
+    )
+
+
+def algorithmic_bytes(w) -> int:
+    """Bytes one decode call must move: int4 codes + per-group scale/min of
+    the history (keys: per channel per token group; values: per token per
+    dim group), the bf16 windows, q, out and the block table."""
+    B, L, H, Hq, D, g = w.B, w.L, w.Hl, w.Hql, w.D, w.g
+    hk = hv = w.hist
+    per_head = hk * D // 2 + (hk // g) * D * 8 + hv * D // 2 + hv * (D // g) * 8 + 2 * w.res * D * 2
+    return B * (H * per_head + 2 * Hq * D * 2 + 4 * ((L + w.blk - 1) // w.blk))
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons of one GPU during a region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.rows: list[list[str]] = []
+        self._stop = threading.Event()
+        self._thread: threading.Thread | None = None
+
+    def _query(self):
+        try:
+            out = subprocess.run(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-i", str(self.index)],
+                capture_output=True, text=True, timeout=5,
+            ).stdout.strip()
+            if out:
+                self.rows.append([c.strip() for c in out.split(",")])
+        except Exception:
+            pass
+
+    def _loop(self):
+        while not self._stop.is_set():
+            self._query()
+            self._stop.wait(0.05)
+
+    def __enter__(self):
+        self._thread = threading.Thread(target=self._loop, daemon=True)
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join(timeout=10)
+        if not self.rows:
+            self._query()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for row in self.rows:
+            try:
+                sm.append(float(row[0]))
+                mx = float(row[1])
+            except (ValueError, IndexError):
+                continue
+            for name, val in zip(names, row[4:8]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text())
+    return {}
+
+
+def bench_pack(device):
+    """Pack GB/s (config 2's definition: 5248 B/token = 4096 bf16 in + 1152
+    out at KVH 8, D 128, g 128): keys and values of 8192 tokens."""
+    import torch
+
+    from qkv_b200.ops import kivi_pack_key_cache, kivi_pack_value_cache
+
+    c = CONFIG2_PACK
+    T, H, D, g, blk = c["tokens"], c["num_kv_heads"], c["head_size"], c["group_size"], c["block_size"]
+    nb = T // blk
+    k = torch.randn(T, H, D, device=device).to(torch.bfloat16)
+    v = torch.randn(T, H, D, device=device).to(torch.bfloat16)
+    slots = torch.randperm(nb, device=device).repeat_interleave(blk) * blk + torch.arange(T, device=device) % blk
+    f = lambda *s, dt=torch.float32: torch.zeros(s, dtype=dt, device=device)
+    views = (f(nb, H, D, blk // 8, dt=torch.int32), f(nb, H, D, blk // g), f(nb, H, D, blk // g),
+             f(nb, blk, H, D // 8, dt=torch.int32), f(nb, blk, H, D // g), f(nb, blk, H, D // g))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+
+    def once():
+        kivi_pack_key_cache(k, slots, *views[:3], g, validate_slots=False)
+        kivi_pack_value_cache(v, slots, *views[3:], g)
+
+    for _ in range(3):
+        once()
+    times = []
+    for _ in range(20):
+        flush.zero_()  # inputs (33 MB) fit in L2: flush between runs
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        once()
+        e.record()
+        e.synchronize()
+        times.append(s.elapsed_time(e) / 1e3)
+    t = statistics.median(times)
+    by = T * (H * D * 2 * 2 + H * (D // 2 + 8 * D // g) * 2)
+    return {"gbs": by / t / 1e9, "bytes_per_call": by, "us_per_call": t * 1e6, "tokens": T,
+            "bytes_per_token": by // T, "launches_per_call": 2}
+
+
+def e2e_impl(w, device):
+    """A KIVI mixin bound to the workload's buffers, with its window state
+    set to what the reference's writes leave (rows b = request b)."""
+    import torch
+
+    from qkv_b200.methods.kivi_int4.attention_backend import AscendKiviInt4AttentionBackendMixin
+
+    class Host:
+        pass
+
+    class Impl(AscendKiviInt4AttentionBackendMixin, Host):
+        pass
+
+    impl = Impl()
+    impl.num_heads, impl.num_kv_heads, impl.head_size = w.Hql, w.Hl, w.D
+    impl.num_queries_per_kv = w.Hql // w.Hl
+    impl.scale = w.D ** -0.5
+    impl._init_kivi_state("kivi_int4", SimpleNamespace(
+        cache_config=SimpleNamespace(kivi_group_size=w.g, kivi_residual_length=w.r),
+        scheduler_config=SimpleNamespace(max_num_seqs=w.B + 1)))
+    impl._bind_kivi_cache((w.kbuf, w.vbuf))
+    impl.kivi_residual_key_cache.copy_(w.rk)
+    impl.kivi_residual_value_cache.copy_(w.rv)
+    bt = w.bt.numpy()
+    for b in range(w.B):
+        row = impl._get_kivi_residual_row(f"req{b}", create=True)
+        assert row == b
+        for side in (impl._kivi_planner.key, impl._kivi_planner.value):
+            for i in range(w.res):
+                p = w.hist + i
+                side.slots[row, i] = int(bt[b, p // w.blk]) * w.blk + p % w.blk
+            side.start[row] = 0
+            side.length[row] = w.res
+    return impl
+
+
+def run_e2e(w, device, steps, warmup):
+    """tokens/s/layer through the plugin API with host buffers in the loop."""
+    import torch
+
+    impl = e2e_impl(w, device)
+    B, Hq, H, D = w.B, w.Hql, w.Hl, w.D
+    bt_host = w.bt.numpy()
+    total = steps + warmup
+    gen = torch.Generator().manual_seed(7)
+    q_h = torch.randn(total, B, Hq, D, generator=gen).to(torch.bfloat16).pin_memory()
+    k_h = torch.randn(total, B, H, D, generator=gen).to(torch.bfloat16).pin_memory()
+    v_h = torch.randn(total, B, H, D, generator=gen).to(torch.bfloat16).pin_memory()
+    out_h = torch.empty(B, Hq, D, dtype=torch.bfloat16).pin_memory()
+    bt_pinned = w.bt.clone().pin_memory()
+    lens = [w.L] * B
+    names = [f"req{b}" for b in range(B)]
+
+    def step(i):
+        for b in range(B):
+            lens[b] += 1
+        slots = [int(bt_host[b, (lens[b] - 1) // w.blk]) * w.blk + (lens[b] - 1) % w.blk for b in range(B)]
+        q = q_h[i].to(device, non_blocking=True)
+        k = k_h[i].to(device, non_blocking=True)
+        v = v_h[i].to(device, non_blocking=True)
+        md = SimpleNamespace(
+            attn_state=SimpleNamespace(name="DecodeOnly"), actual_seq_lengths_q=list(range(1, B + 1)),
+            seq_lens_list=list(lens), slot_mapping=torch.tensor(slots, dtype=torch.int64).pin_memory(),
+            block_tables=bt_pinned, req_ids=names, num_actual_tokens=B, causal=True, finished_req_ids=None,
+        )
+        md.slot_mapping = md.slot_mapping.to(device, non_blocking=True)
+        out = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=device)
+        impl.forward(None, q, k, v, (w.kbuf, w.vbuf), md, out)
+        out_h.copy_(out, non_blocking=True)
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    for i in range(warmup, total):
+        step(i)
+    torch.cuda.synchronize(device)
+    dt = (time.perf_counter() - t0) / max(steps, 1)
+    h2d = B * (Hq + 2 * H) * D * 2 + B * 8 + B * 5 * 4 + B * 4 + w.bt.numel() * 4
+    d2h = B * Hq * D * 2
+    return dt, h2d, d2h
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    from qkv_b200.ops import kivi_paged_decode
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    cfg = CONFIG5
+    w = build_workload(cfg, rank, world, device)
+    out = torch.empty(w.B, w.Hql, w.D, dtype=torch.bfloat16, device=device)
+    gathered = torch.empty(world, w.B, w.Hql, w.D, dtype=torch.bfloat16, device=device) if world > 1 else None
+    full = torch.empty(w.B, cfg["num_heads"], w.D, dtype=torch.bfloat16, device=device)
+
+    def decode():
+        kivi_paged_decode(w.q, w.views, w.rk, w.rv, w.bt_dev, w.seq_lens, w.state, w.g, w.D ** -0.5, out, w.L)
+
+    def step():
+        decode()
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, out)
+            full.view(w.B, world, w.Hql, w.D).copy_(gathered.permute(1, 0, 2, 3))
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with sampler:
+        torch.cuda.synchronize(device)
+        start.record()
+        for _ in range(args.steps):
+            step()
+        end.record()
+        torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end) / args.steps
+    # the decode call alone (dominant kernel), for the roofline
+    ks, ke = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    ks.record()
+    for _ in range(args.steps):
+        decode()
+    ke.record()
+    torch.cuda.synchronize(device)
+    decode_ms = ks.elapsed_time(ke) / args.steps
+    t = torch.tensor([ms, decode_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, decode_ms = t.tolist()
+
+    from qkv_b200.ops import _lib
+
+    workspace_splits = _lib.load().qkv_kivi_paged_decode_workspace(w.B, w.Hql, w.Hl, w.D, w.g, w.blk, w.L)
+    launches_per_step = 2 if workspace_splits > 0 else 1
+
+    pack = bench_pack(device) if rank == 0 else None
+    e2e_dt, h2d, d2h = run_e2e(w, device, args.e2e_steps, 3)
+    t = torch.tensor([e2e_dt], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_dt = float(t.item())
+
+    if rank == 0:
+        peaks = measured_peaks()
+        peak = peaks.get("hbm_gbs")
+        peak_src = "measured" if peak else "fallback"
+        peak = peak or 6650.0
+        by = algorithmic_bytes(w)
+        achieved = by / (decode_ms * 1e-3) / 1e9
+        value = w.B / (ms * 1e-3)
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            run = cpu_reference_sample(cfg)
+            run()
+            n = 3
+            t0 = time.perf_counter()
+            for _ in range(n):
+                run()
+            cdt = (time.perf_counter() - t0) / n
+            cpu = {"value": 1.0 / cdt, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+                   "sample": "one request of the workload (context 32768, 64 q / 8 kv heads) per step, median of "
+                             f"{n}; linear in requests"}
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "int4/bf16->fp32",
+            "data": "synthetic",
+            "config": workload_config(cfg, world),
+            "hbm_gbs": achieved,
+            "hbm_frac_of_8tbs": achieved / 8000.0,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
+                         "bytes_per_launch": by, "kernel_ms": decode_ms},
+            "pack": pack,
+            "e2e": {"value": w.B / e2e_dt, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_dt * 1e3, "api": "AscendKiviInt4AttentionBackendMixin.forward (DecodeOnly)"},
+            "cpu_baseline": cpu,
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": sampler.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,233 @@
+/*
+ * qkv_sm100.h — C ABI of libqkv_sm100.so, the B200 (sm_100a) kernels behind the
+ * quantized-KV attention path of vllm-ascend-quantized-kv-cache
+ * (dtype literals "int8" and "kivi_int4").
+ *
+ * Conventions shared by every entry point:
+ *   - All tensor arguments are DEVICE pointers to contiguous memory in the
+ *     layouts written next to each function; sizes are element counts.
+ *   - `stream` is a cudaStream_t (0 = legacy default stream). Launches are
+ *     asynchronous on that stream; no entry point synchronises the device.
+ *   - Return value: QKV_OK (0) or a negative qkv_status. On error nothing was
+ *     launched and qkv_last_error() returns the message (thread-local).
+ *   - Kernels bounds-check every index they read from device memory (slots,
+ *     block ids, residual rows). An out-of-range index is skipped, never
+ *     dereferenced, and recorded in a device error word that
+ *     qkv_device_error() reads back.
+ *   - Floating-point element types are selected with qkv_dtype; index arrays
+ *     (slot_mapping) with qkv_index.
+ *
+ * Every entry point names the reference interface it replaces (paths are
+ * relative to src/vllm_ascend_quantized_kv_cache/ of the reference project).
+ */
+#ifndef QKV_SM100_H
+#define QKV_SM100_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define QKV_API __attribute__((visibility("default")))
+#else
+#define QKV_API
+#endif
+
+typedef struct CUstream_st* qkv_stream_t; /* identical to cudaStream_t */
+
+enum qkv_status {
+  QKV_OK = 0,
+  QKV_ERR_INVALID = -1,     /* bad argument: shape, alignment, geometry */
+  QKV_ERR_UNSUPPORTED = -2, /* valid for the reference, not built here */
+  QKV_ERR_CUDA = -3,        /* a CUDA runtime call failed */
+  QKV_ERR_WORKSPACE = -4,   /* caller workspace too small */
+  QKV_ERR_DEVICE = -5       /* a kernel recorded a bad index */
+};
+
+enum qkv_dtype { QKV_F32 = 0, QKV_BF16 = 1, QKV_F16 = 2 };
+enum qkv_index { QKV_I32 = 0, QKV_I64 = 1 };
+
+/* Library version string, e.g. "qkv_sm100 0.1.0 (sm_100a)". */
+QKV_API const char* qkv_version(void);
+
+/* Copies the calling thread's last error message into buf (NUL-terminated,
+ * truncated to len). Returns the status of the failed call (0 if none). */
+QKV_API int qkv_last_error(char* buf, int len);
+
+/* Synchronises `stream`, then reads and clears the device error word of the
+ * current device. *code receives 0 or the first recorded kernel error
+ * (1 = slot out of range, 2 = block id out of range, 3 = residual row out of
+ * range, 4 = block-table entry negative for a live token). Returns QKV_OK or
+ * QKV_ERR_CUDA. */
+QKV_API int qkv_device_error(int* code, qkv_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * INT8 dynamic per-channel
+ * ---------------------------------------------------------------------- */
+
+/* Per-(kv_head, channel) scales from the first K/V batch of a layer.
+ * Replaces AscendInt8AttentionBackendMixin._prepare_int8_scales
+ * (methods/int8_dynamic/attention_backend.py:130-150; the same math as
+ * Int8DynamicSemantics.calc_scales, methods/int8_dynamic/semantics.py:49-70).
+ *   key, value        bf16 [num_tokens, num_kv_heads, head_size]
+ *   k_inv_scale, ...  bf16 [num_kv_heads, head_size]
+ * inv = bf16(bf16(1 / max(amax_t |x|, bf16(1e-12))) * 127), aq = bf16(1 / inv),
+ * i.e. torch's bf16 `127.0 / amax` and `1.0 / inv` rounding sequence. */
+QKV_API int qkv_int8_scales(const void* key, const void* value, int64_t num_tokens,
+                    int num_kv_heads, int head_size, void* k_inv_scale,
+                    void* v_inv_scale, void* k_aq_scale, void* v_aq_scale,
+                    qkv_stream_t stream);
+
+/* Quantise K/V and scatter them into the paged int8 caches.
+ * Replaces AscendInt8AttentionBackendMixin._quantize_kv_to_runtime_int8
+ * (methods/int8_dynamic/attention_backend.py:152-171) followed by the host's
+ * reshape_and_cache (attention_backend.py:86-88).
+ *   key, value            bf16 [num_tokens, num_kv_heads, head_size]
+ *   slot_mapping          int32/int64 [num_tokens]; slot < 0 = padding, skipped
+ *   k_inv_scale, v_inv..  bf16 [num_kv_heads, head_size]
+ *   key_cache, value_c.   int8 [num_blocks, block_size, num_kv_heads, head_size]
+ * code = clamp(rint(bf16(x * inv)), -128, 127). */
+QKV_API int qkv_int8_quant_store(const void* key, const void* value,
+                         const void* slot_mapping, int slot_dtype,
+                         int64_t num_tokens, int num_kv_heads, int head_size,
+                         int block_size, int64_t num_blocks,
+                         const void* k_inv_scale, const void* v_inv_scale,
+                         int8_t* key_cache, int8_t* value_cache,
+                         qkv_stream_t stream);
+
+/* Bytes of workspace qkv_int8_paged_decode needs for this batch shape. */
+QKV_API size_t qkv_int8_paged_decode_workspace(int batch, int num_heads,
+                                       int num_kv_heads, int head_size,
+                                       int block_size, int max_seq_len);
+
+/* GQA decode attention, one query token per request, over the paged int8
+ * caches with per-channel antiquant folded into the kernel. Replaces the FIA
+ * call of AscendInt8AttentionBackendMixin._forward_int8_decode
+ * (methods/int8_dynamic/attention_backend.py:173-205); numerically it follows
+ * the dequantise-then-attend path of _dequant_int8_paged_kv_to_dense
+ * (attention_backend.py:370-404) + fp32 softmax attention.
+ *   query        bf16, row b at query + b*q_stride, heads contiguous [Hq, D]
+ *   key_cache..  int8 [num_blocks, block_size, num_kv_heads, head_size]
+ *   k_aq_scale.. bf16 [num_kv_heads, head_size]
+ *   block_table  int32, row b at block_table + b*bt_stride (>= max_blocks)
+ *   seq_lens     int32 [batch]
+ *   out          bf16, row b at out + b*out_stride, [Hq, D]
+ * max_seq_len bounds seq_lens (used to plan the split-KV grid only). */
+QKV_API int qkv_int8_paged_decode(const void* query, int64_t q_stride,
+                          const int8_t* key_cache, const int8_t* value_cache,
+                          const void* k_aq_scale, const void* v_aq_scale,
+                          const int32_t* block_table, int64_t bt_stride,
+                          const int32_t* seq_lens, int batch, int num_heads,
+                          int num_kv_heads, int head_size, int block_size,
+                          int64_t num_blocks, int max_seq_len, float scale,
+                          void* workspace, size_t workspace_bytes, void* out,
+                          int64_t out_stride, qkv_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * KIVI INT4 (int4 history + full-precision residual window)
+ * ---------------------------------------------------------------------- */
+
+/* Pack whole token groups of keys into the paged int4 key cache.
+ * Replaces kivi_pack_key_cache / _kivi_pack_key_cache_kernel
+ * (ops/triton/kivi_pack.py:287-348, :134-226).
+ *   key       key_dtype [num_tokens, num_kv_heads, head_size], num_tokens % g == 0
+ *   slot_map  [num_tokens]; each group of g slots contiguous, g-aligned and
+ *             inside one block (validated by the host before the call)
+ *   k_quant   int32 [num_blocks, num_kv_heads, head_size, block_size/8]
+ *   k_scale   f32   [num_blocks, num_kv_heads, head_size, block_size/g]
+ *   k_mn      f32   same shape as k_scale
+ * scale = max((mx - mn) / 15, 1e-6); code = clamp(floor((x - mn)/scale + 0.5), 0, 15),
+ * token offset o of the block goes to nibble o % 8 of word o / 8. */
+QKV_API int qkv_kivi_pack_key(const void* key, int key_dtype, const void* slot_mapping,
+                      int slot_dtype, int64_t num_tokens, int num_kv_heads,
+                      int head_size, int group_size, int block_size,
+                      int64_t num_blocks, int32_t* k_quant, float* k_scale,
+                      float* k_mn, qkv_stream_t stream);
+
+/* Pack values, one token at a time, grouped along head_size.
+ * Replaces kivi_pack_value_cache / _kivi_pack_value_cache_kernel
+ * (ops/triton/kivi_pack.py:229-284, :61-131).
+ *   value     value_dtype [num_tokens, num_kv_heads, head_size]
+ *   slot_map  [num_tokens]; slot < 0 skipped
+ *   v_quant   int32 [num_blocks, block_size, num_kv_heads, head_size/8]
+ *   v_scale   f32   [num_blocks, block_size, num_kv_heads, head_size/g]
+ *   v_mn      f32   same shape as v_scale */
+QKV_API int qkv_kivi_pack_value(const void* value, int value_dtype,
+                        const void* slot_mapping, int slot_dtype,
+                        int64_t num_tokens, int num_kv_heads, int head_size,
+                        int group_size, int block_size, int64_t num_blocks,
+                        int32_t* v_quant, float* v_scale, float* v_mn,
+                        qkv_stream_t stream);
+
+/* Bytes of workspace qkv_kivi_paged_decode needs for this batch shape. */
+QKV_API size_t qkv_kivi_paged_decode_workspace(int batch, int num_heads,
+                                       int num_kv_heads, int head_size,
+                                       int group_size, int block_size,
+                                       int max_seq_len);
+
+/* Fused KIVI decode attention: streams the int4 pages of each request,
+ * dequantises in registers and merges the bf16 residual window into the same
+ * online softmax; no dense K/V copy is materialised. Replaces
+ * _forward_kivi_paged_decode_attention (methods/kivi_int4/attention_backend.py:1193-1230),
+ * i.e. _gather_dequant_kivi_paged_cache (:849-935) = kivi_dequant_gather_cache
+ * (ops/kivi_gather.py:36-156) + residual tail overwrite, then FIA TND.
+ *   query, out           as for qkv_int8_paged_decode
+ *   k_quant..v_mn        the six KIVI views (see qkv_kivi_pack_key/value)
+ *   res_key, res_value   bf16 [res_rows, res_capacity, num_kv_heads, head_size]
+ *   seq_lens             int32 [batch]: row b attends to positions [0, seq_lens[b])
+ *                        (the new token included; a prefill query row passes its
+ *                        causal length, with the request's table row repeated)
+ *   res_state            int32 [batch, 6] = row, k_start, k_len, v_start, v_len, end
+ *                        (row < 0 or NULL: no residual). The key window holds
+ *                        positions [end - k_len, end): position p in it reads
+ *                        residual lane (k_start + p - (end - k_len)) % res_capacity,
+ *                        every other position reads its int4 page
+ *                        block_table[b][p / block_size]; values likewise. */
+QKV_API int qkv_kivi_paged_decode(
+    const void* query, int64_t q_stride, const int32_t* k_quant,
+    const float* k_scale, const float* k_mn, const int32_t* v_quant,
+    const float* v_scale, const float* v_mn, const void* res_key,
+    const void* res_value, int res_rows, int res_capacity,
+    const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
+    const int32_t* res_state, int batch, int num_heads, int num_kv_heads,
+    int head_size, int group_size, int block_size, int64_t num_blocks,
+    int max_seq_len, float scale, void* workspace, size_t workspace_bytes,
+    void* out, int64_t out_stride, qkv_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Dense prefill attention (TND)
+ * ---------------------------------------------------------------------- */
+
+/* Bytes of workspace qkv_dense_prefill needs. */
+QKV_API size_t qkv_dense_prefill_workspace(int total_q, int num_heads,
+                                   int num_kv_heads, int head_size,
+                                   int max_kv_len);
+
+/* Prompt attention over full-precision K/V in the TND layout, one request per
+ * [cu_seqlens_q[b], cu_seqlens_q[b+1]) query range. Replaces the FIA calls of
+ * the all-new prefill branches: _forward_kivi_prefill_fia and the prompt rows
+ * of _forward_kivi_chunked_prefill (methods/kivi_int4/attention_backend.py:
+ * 1232-1266, :1315-1338), and the PrefillNoCache / all-new rows of
+ * _forward_int8_prefill / _forward_int8_chunked_prefill
+ * (methods/int8_dynamic/attention_backend.py:246-368). With causal != 0 query
+ * i of a request with q_len queries over kv_len keys sees keys
+ * j <= kv_len - q_len + i (FIA sparse_mode 3, the mask of build_causal_mask,
+ * methods/kivi_int4/semantics.py:285-299).
+ *   query, out     bf16 [total_q, num_heads, head_size]
+ *   key, value     bf16 [cu_seqlens_k[num_reqs], num_kv_heads, head_size]
+ *   cu_seqlens_*   int32 [num_reqs + 1], cu[0] = 0 */
+QKV_API int qkv_dense_prefill(const void* query, const void* key, const void* value,
+                      const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
+                      int num_reqs, int total_q, int num_heads,
+                      int num_kv_heads, int head_size, int causal,
+                      int max_kv_len, float scale, void* workspace,
+                      size_t workspace_bytes, void* out, qkv_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QKV_SM100_H */

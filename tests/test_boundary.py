@@ -1,0 +1,205 @@
+"""The reference-facing surface: dtype contract, method registry, dispatcher,
+bootstrap and the KIVI byte budget / six-view split — the behaviour the
+reference's tests/test_plugin.py and tests/test_kivi_int4.py:1205-1400 pin."""
+
+from __future__ import annotations
+
+import subprocess
+import sys
+from types import SimpleNamespace
+
+import pytest
+import torch
+
+from qkv_b200 import KVQuantMode, bootstrap, kv_methods, resolve_layout
+from qkv_b200.methods.kivi_int4.byte_cache import (
+    KiviByteCacheLayout,
+    kivi_byte_cache_layout,
+    kivi_caches_from_byte_tensors,
+)
+from qkv_b200.methods.kivi_int4.geometry import validate_kivi_config
+from qkv_b200.methods.base import MethodConfig
+
+
+def test_methods_and_dtypes():
+    assert kv_methods.list() == ["int8_dynamic", "kivi_int4"]
+    assert kv_methods.describe("int8_dynamic")["dtype"] == "int8"
+    assert kv_methods.describe("kivi_int4")["dtype"] == "kivi_int4"
+    with pytest.raises(ValueError, match="unknown quantized KV method"):
+        kv_methods.get("fp8_e4m3")
+
+
+def test_layout_contract():
+    assert resolve_layout("int8", 128).storage_dtype == "int8"
+    lay = resolve_layout("kivi_int4", 128)
+    assert lay.storage_dtype == "uint8" and lay.packed_last_dim == 64
+    assert lay.quant_mode is KVQuantMode.KIVI_INT4
+    with pytest.raises(ValueError, match="positive even"):
+        resolve_layout("kivi_int4", 127)
+    with pytest.raises(ValueError, match="not a registered"):
+        resolve_layout("int4", 128)
+
+
+@pytest.mark.parametrize(
+    "overrides, match",
+    [
+        ({"group_size": 7}, "divisible by 8"),
+        ({"residual_length": 4, "group_size": 8}, "residual_length"),
+        ({"head_size": 12}, "head_size"),
+        ({"head_size": 8, "group_size": 16}, "head_size"),
+        ({"block_size": 8, "group_size": 16}, "block_size"),
+    ],
+)
+def test_geometry_rejects(overrides, match):
+    kw = dict(head_size=32, group_size=8, residual_length=16, block_size=16)
+    kw.update(overrides)
+    with pytest.raises(ValueError, match=match):
+        validate_kivi_config(MethodConfig(**kw))
+    with pytest.raises(ValueError, match=match):
+        kv_methods.get("kivi_int4", **kw)
+
+
+def test_import_needs_no_torch():
+    code = "import sys; import qkv_b200; qkv_b200.kv_methods.list(); print('torch' in sys.modules)"
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                         env={"PYTHONPATH": ":".join(sys.path)})
+    assert out.stdout.strip() == "False", out.stderr
+
+
+def test_bootstrap_noop_without_host(monkeypatch):
+    monkeypatch.setattr(bootstrap, "detect_host", lambda: None)
+    assert bootstrap.register_plugins() == []
+
+
+def test_bootstrap_registers_both(monkeypatch):
+    calls = []
+    monkeypatch.setattr(bootstrap, "detect_host", lambda: bootstrap.VLLM_ASCEND_HUST)
+    import qkv_b200.core.activation as activation
+
+    monkeypatch.setattr(activation, "activate", lambda name, host: calls.append((name, host)) or {})
+    assert bootstrap.register_plugins() == ["int8_dynamic", "kivi_int4"]
+    assert calls == [("int8_dynamic", "vllm_ascend_hust"), ("kivi_int4", "vllm_ascend_hust")]
+
+
+@pytest.fixture
+def host_stack(monkeypatch):
+    import importlib.machinery
+    import types
+
+    def stub(name):
+        m = types.ModuleType(name)
+        m.__spec__ = importlib.machinery.ModuleSpec(name, None)
+        monkeypatch.setitem(sys.modules, name, m)
+        return m
+
+    for n in ("vllm", "vllm_ascend", "vllm_ascend.attention", "vllm_ascend.ops"):
+        stub(n)
+    vcfg = stub("vllm.config")
+    av1 = stub("vllm_ascend.attention.attention_v1")
+    utils = stub("vllm_ascend.attention.utils")
+
+    class HostImpl:
+        def __init__(self, *a, **k):
+            self.num_heads = 4
+            self.num_kv_heads = 2
+            self.head_size = 32
+            self.num_queries_per_kv = 2
+            self.scale = 0.125
+            self.vllm_config = SimpleNamespace(
+                cache_config=SimpleNamespace(kivi_group_size=8, kivi_residual_length=16),
+                scheduler_config=SimpleNamespace(max_num_seqs=3),
+            )
+
+    class HostBackend:
+        @staticmethod
+        def get_impl_cls():
+            return HostImpl
+
+    av1.AscendAttentionBackend = HostBackend
+    av1.AscendAttentionBackendImpl = HostImpl
+    cc = SimpleNamespace(cache_dtype="auto")
+    vcfg.get_current_vllm_config = lambda: SimpleNamespace(cache_config=cc)
+    utils.enable_cp = lambda: False
+    from qkv_b200.adapters.vllm_ascend_hust import backend
+
+    backend._build_kivi_impl_cls.cache_clear()
+    backend._build_int8_impl_cls.cache_clear()
+    yield SimpleNamespace(backend=HostBackend, impl=HostImpl, cc=cc, utils=utils)
+    backend._build_kivi_impl_cls.cache_clear()
+    backend._build_int8_impl_cls.cache_clear()
+
+
+def test_dispatch_selects_plugin_only_for_quantized_dtypes(host_stack):
+    info = kv_methods.activate("kivi_int4", host="vllm_ascend_hust")
+    assert info["integration"] == "host_get_impl_cls_dispatch"
+    assert "--kv-cache-dtype kivi_int4" in info["usage"]
+    be = host_stack.backend
+    assert be.get_impl_cls() is host_stack.impl
+    host_stack.cc.cache_dtype = "kivi_int4"
+    cls = be.get_impl_cls()
+    from qkv_b200.methods.kivi_int4.attention_backend import AscendKiviInt4AttentionBackendMixin
+
+    assert issubclass(cls, AscendKiviInt4AttentionBackendMixin) and issubclass(cls, host_stack.impl)
+    impl = cls()
+    assert impl.enable_kivi and impl.kivi_group_size == 8 and impl.kivi_residual_length == 16
+    assert impl.kivi_max_num_seqs == 3
+    host_stack.cc.cache_dtype = "int8"
+    from qkv_b200.methods.int8_dynamic.attention_backend import AscendInt8AttentionBackendMixin
+
+    assert issubclass(be.get_impl_cls(), AscendInt8AttentionBackendMixin)
+    # idempotent install
+    kv_methods.activate("int8_dynamic", host="vllm_ascend_hust")
+    host_stack.cc.cache_dtype = "auto"
+    assert be.get_impl_cls() is host_stack.impl
+
+
+def test_dispatch_refuses_context_parallel(host_stack):
+    kv_methods.activate("kivi_int4", host="vllm_ascend_hust")
+    host_stack.utils.enable_cp = lambda: True
+    host_stack.cc.cache_dtype = "kivi_int4"
+    with pytest.raises(NotImplementedError, match="does not support context parallel"):
+        host_stack.backend.get_impl_cls()
+    host_stack.cc.cache_dtype = "auto"
+    assert host_stack.backend.get_impl_cls() is host_stack.impl
+
+
+# ---------------------------------------------------------------- byte cache
+
+
+def test_byte_budget_and_compression():
+    lay = KiviByteCacheLayout(num_blocks=1, block_size=128, num_kv_heads=8, head_size=128, group_size=128)
+    assert lay.bytes_per_token_head == 72
+    assert lay.compression_vs_fp16() == pytest.approx(256 / 72)
+    assert lay.page_size_bytes() == 2 * 128 * 8 * 72
+    assert KiviByteCacheLayout(num_blocks=1, block_size=128, num_kv_heads=8, head_size=128,
+                               group_size=64).bytes_per_token_head == 80
+
+
+@pytest.mark.parametrize("head,group,block,kvh,nb", [(128, 128, 128, 8, 7), (32, 8, 16, 2, 3), (64, 32, 256, 4, 2)])
+def test_host_buffers_rebuild_the_layout_and_alias(head, group, block, kvh, nb):
+    lay = KiviByteCacheLayout(num_blocks=nb, block_size=block, num_kv_heads=kvh, head_size=head, group_size=group)
+    raw = torch.zeros((2, nb, block, kvh, lay.bytes_per_token_head), dtype=torch.uint8)
+    assert lay.page_size_bytes() * nb == 2 * lay.region_bytes
+    assert kivi_byte_cache_layout(raw[0], raw[1], num_kv_heads=kvh, head_size=head, group_size=group) == lay
+    kq, ks, km, vq, vs, vm = kivi_caches_from_byte_tensors(raw[0], raw[1], lay)
+    assert kq.shape == (nb, kvh, head, block // 8) and kq.dtype == torch.int32
+    assert vq.shape == (nb, block, kvh, head // 8)
+    ks[0, 0, 0, 0] = 3.5
+    assert float(raw[0].reshape(-1).view(torch.float32)[kq.numel()]) == 3.5
+    kq[0, 0, 0, 0] = 0x04030201
+    assert raw[0].reshape(-1)[:4].tolist() == [1, 2, 3, 4]
+
+
+def test_byte_cache_rejects_bad_buffers():
+    lay = KiviByteCacheLayout(num_blocks=4, block_size=16, num_kv_heads=2, head_size=32, group_size=8)
+    k = torch.zeros(4, 16, 2, lay.bytes_per_token_head, dtype=torch.uint8)
+    v = torch.zeros_like(k)
+    with pytest.raises(RuntimeError, match="equal regions"):
+        kivi_byte_cache_layout(k, v[:1], num_kv_heads=2, head_size=32, group_size=8)
+    with pytest.raises(RuntimeError, match="must be contiguous"):
+        kivi_byte_cache_layout(k.transpose(0, 1), v, num_kv_heads=2, head_size=32, group_size=8)
+    with pytest.raises(RuntimeError, match="value cache must hold"):
+        kivi_caches_from_byte_tensors(k, v[:-1], lay)
+    dense = torch.zeros(4, 16, 2, 32, dtype=torch.float16)
+    with pytest.raises(RuntimeError, match="must hold|whole number of pages"):
+        kivi_byte_cache_layout(dense, dense.clone(), num_kv_heads=2, head_size=32, group_size=8)

@@ -1,0 +1,340 @@
+"""CUDA kernels vs the oracle through the C ABI (libqkv_sm100.so).
+
+Bit-exact: INT8 scales / codes / pages, KIVI packed words / scales / mins.
+Attention: max-abs 1e-2 against the oracle's dequantise-then-attend result in
+fp32 (the tolerance the north-star sets for bf16 outputs)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import qkv_oracle as O
+from conftest import bf16_to_f32
+
+pytestmark = pytest.mark.gpu
+
+ATOL = 1e-2  # attention outputs vs the fp32 dequantise-then-attend oracle
+
+
+def dev():
+    return torch.device("cuda", 0)
+
+
+def bf16_tensor(x: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(O.bf16_round(x))).to(dev()).to(torch.bfloat16)
+
+
+def to_np(t: torch.Tensor) -> np.ndarray:
+    return t.detach().float().cpu().numpy() if t.dtype == torch.bfloat16 else t.detach().cpu().numpy()
+
+
+def assert_no_device_error():
+    from qkv_b200.ops import _lib
+
+    code = _lib.device_error(torch.cuda.current_stream().cuda_stream)
+    assert code == 0, _lib.DEVICE_ERRORS.get(code, code)
+
+
+def kv_data(rng, T, H, D, outlier_frac=0.02, factor=10.0):
+    x = rng.standard_normal((T, H, D)).astype(np.float32)
+    n = max(1, int(outlier_frac * H * D))
+    flat = rng.choice(H * D, size=n, replace=False)
+    for f in flat:
+        x[:, f // D, f % D] *= factor
+    return O.bf16_round(x)
+
+
+# ---------------------------------------------------------------- INT8
+
+
+def test_int8_scales_and_store_match_golden(golden):
+    from qkv_b200.ops import int8_calc_scales, int8_quant_store
+
+    g = golden("int8")
+    key = torch.from_numpy(g["key"].view(np.int16)).view(torch.bfloat16).to(dev())
+    value = torch.from_numpy(g["value"].view(np.int16)).view(torch.bfloat16).to(dev())
+    k_inv, v_inv, k_aq, v_aq = int8_calc_scales(key, value)
+    for t, name in ((k_inv, "k_inv"), (v_inv, "v_inv"), (k_aq, "k_aq"), (v_aq, "v_aq")):
+        assert np.array_equal(t.cpu().view(torch.int16).numpy().view(np.uint16), g[name]), name
+    n = int(g["n_actual"])
+    kc = torch.zeros(g["key_cache"].shape, dtype=torch.int8, device=dev())
+    vc = torch.zeros_like(kc)
+    slots = torch.from_numpy(g["slots"]).to(dev())
+    int8_quant_store(key[:n], value[:n], slots, k_inv, v_inv, kc, vc)
+    assert np.array_equal(kc.cpu().numpy(), g["key_cache"])
+    assert np.array_equal(vc.cpu().numpy(), g["value_cache"])
+    assert_no_device_error()
+
+
+@pytest.mark.parametrize("T", [1, 7, 300, 4096])
+def test_int8_scales_and_codes_bit_exact_random(T):
+    from qkv_b200.ops import int8_calc_scales, int8_quant_store
+
+    rng = np.random.default_rng(T)
+    H, D, blk = 8, 128, 128
+    key, value = kv_data(rng, T, H, D, 0.01, 16.0), kv_data(rng, T, H, D, 0.01, 16.0)
+    key[:, 2, 5] = 0.0
+    kt, vt = bf16_tensor(key), bf16_tensor(value)
+    k_inv, v_inv, k_aq, v_aq = int8_calc_scales(kt, vt)
+    ok_inv, ov_inv, ok_aq, ov_aq = O.int8_calc_scales(key, value)
+    assert np.array_equal(to_np(k_inv), ok_inv) and np.array_equal(to_np(v_inv), ov_inv)
+    assert np.array_equal(to_np(k_aq), ok_aq) and np.array_equal(to_np(v_aq), ov_aq)
+    nb = (T + blk - 1) // blk + 1
+    perm = rng.permutation(nb * blk)[:T]
+    slots = perm.copy()
+    slots[::13] = -1  # padding tokens are skipped
+    kc = torch.zeros(nb, blk, H, D, dtype=torch.int8, device=dev())
+    vc = torch.zeros_like(kc)
+    int8_quant_store(kt, vt, torch.from_numpy(slots).to(dev()), k_inv, v_inv, kc, vc)
+    okc = np.zeros((nb, blk, H, D), np.int8)
+    ovc = np.zeros_like(okc)
+    O.int8_quant_store(key, value, slots, ok_inv, ov_inv, okc, ovc)
+    assert np.array_equal(kc.cpu().numpy(), okc) and np.array_equal(vc.cpu().numpy(), ovc)
+    assert_no_device_error()
+
+
+def _int8_decode_case(rng, B, lens, Hq, H, D, blk, shuffle=True):
+    nb = sum((L + blk - 1) // blk for L in lens) + 2
+    maxb = max((L + blk - 1) // blk for L in lens)
+    perm = rng.permutation(nb) if shuffle else np.arange(nb)
+    bt = np.zeros((B, maxb), np.int32)
+    cur = 0
+    for b, L in enumerate(lens):
+        n = (L + blk - 1) // blk
+        bt[b, :n] = perm[cur:cur + n]
+        cur += n
+    kc = rng.integers(-128, 128, size=(nb, blk, H, D), dtype=np.int8)
+    vc = rng.integers(-128, 128, size=(nb, blk, H, D), dtype=np.int8)
+    k_aq = O.bf16_round(rng.uniform(0.005, 0.2, size=(H, D)).astype(np.float32))
+    v_aq = O.bf16_round(rng.uniform(0.005, 0.2, size=(H, D)).astype(np.float32))
+    q = O.bf16_round(rng.standard_normal((B, Hq, D)).astype(np.float32))
+    return q, kc, vc, k_aq, v_aq, bt
+
+
+@pytest.mark.parametrize(
+    "B,lens,Hq,H,D,blk",
+    [
+        (4, [512, 1024, 1536, 2048], 32, 8, 128, 128),  # config 1
+        (3, [1, 129, 300], 32, 8, 128, 128),  # ragged, partial pages
+        (2, [40, 17], 8, 2, 64, 16),  # small geometry, small blocks
+        (2, [100, 260], 16, 2, 256, 32),  # head 256, GQA 8
+        (1, [5000], 40, 8, 128, 128),  # GQA 5
+    ],
+)
+def test_int8_paged_decode_vs_oracle(B, lens, Hq, H, D, blk):
+    from qkv_b200.ops import int8_paged_decode
+
+    rng = np.random.default_rng(B * 1000 + D)
+    q, kc, vc, k_aq, v_aq, bt = _int8_decode_case(rng, B, lens, Hq, H, D, blk)
+    scale = D ** -0.5
+    out = torch.zeros(B, Hq, D, dtype=torch.bfloat16, device=dev())
+    int8_paged_decode(
+        bf16_tensor(q), torch.from_numpy(kc).to(dev()), torch.from_numpy(vc).to(dev()),
+        bf16_tensor(k_aq), bf16_tensor(v_aq), torch.from_numpy(bt).to(dev()),
+        torch.tensor(lens, dtype=torch.int32, device=dev()), scale, out, max(lens),
+    )
+    dk, dv = O.int8_dequant_gather(kc, vc, k_aq, v_aq, bt, lens)
+    want = O.dense_attention(q, dk, dv, [1] * B, lens, scale, causal=True)
+    got = to_np(out)
+    assert np.isfinite(got).all()
+    assert np.max(np.abs(got - want)) <= ATOL
+    assert_no_device_error()
+
+
+# ---------------------------------------------------------------- KIVI pack
+
+
+def _empty_views(nb, blk, H, D, g, fill_scale=1.0):
+    t = lambda *s, dt=torch.float32, v=0.0: torch.full(s, v, dtype=dt, device=dev())
+    return (
+        t(nb, H, D, blk // 8, dt=torch.int32), t(nb, H, D, blk // g, v=fill_scale), t(nb, H, D, blk // g),
+        t(nb, blk, H, D // 8, dt=torch.int32), t(nb, blk, H, D // g, v=fill_scale), t(nb, blk, H, D // g),
+    )
+
+
+def test_kivi_pack_matches_golden_at_reference_geometries(golden):
+    from qkv_b200.ops import kivi_pack_key_cache, kivi_pack_value_cache
+
+    g = golden("kivi_pack")
+    names = ("k_quant", "k_scale", "k_mn", "v_quant", "v_scale", "v_mn")
+    for p in sorted({k.split("_")[0] for k in g if k.endswith("_geometry")}):
+        head, kvh, group, block, residual, nb = g[p + "_geometry"].tolist()
+        views = _empty_views(nb, block, kvh, head, group)
+        slots = torch.from_numpy(g[p + "_slots"]).to(dev())
+        for dtype in (torch.float32, torch.bfloat16):
+            key = torch.from_numpy(bf16_to_f32(g[p + "_key"])).to(dev()).to(dtype)
+            value = torch.from_numpy(bf16_to_f32(g[p + "_value"])).to(dev()).to(dtype)
+            kivi_pack_key_cache(key, slots, *views[:3], group)
+            kivi_pack_value_cache(value, slots, *views[3:], group)
+            for v, n in zip(views, names):
+                assert np.array_equal(v.cpu().numpy().view(np.uint32), g[f"{p}_{n}"].view(np.uint32)), (p, n, dtype)
+    assert_no_device_error()
+
+
+@pytest.mark.parametrize("group", [64, 128])
+def test_kivi_pack_bit_exact_config2_scale(group):
+    """Config-2 shapes (KVH 8, D 128, block 128): 16 whole pages packed at once."""
+    from qkv_b200.ops import kivi_pack_key_cache, kivi_pack_value_cache
+
+    rng = np.random.default_rng(group)
+    H, D, blk, pages = 8, 128, 128, 16
+    T = pages * blk
+    key, value = kv_data(rng, T, H, D, 0.02, 10.0), kv_data(rng, T, H, D, 0.0, 1.0)
+    key[:group, 1, 3] = 0.25  # constant group: scale floor
+    value[5, 2, :] = np.arange(D, dtype=np.float32) * 0.5  # exact ties
+    nb = pages + 3
+    page_ids = rng.permutation(nb)[:pages]
+    slots = (page_ids[np.arange(T) // blk] * blk + np.arange(T) % blk).astype(np.int64)
+    views = _empty_views(nb, blk, H, D, group)
+    kivi_pack_key_cache(bf16_tensor(key), torch.from_numpy(slots).to(dev()), *views[:3], group)
+    kivi_pack_value_cache(bf16_tensor(value), torch.from_numpy(slots).to(dev()), *views[3:], group)
+    ov = [v.cpu().numpy().copy() for v in _empty_views(nb, blk, H, D, group)]
+    O.kivi_pack_key(key, slots, ov[0], ov[1], ov[2], group)
+    O.kivi_pack_value(value, slots, ov[3], ov[4], ov[5], group)
+    for v, o in zip(views, ov):
+        assert np.array_equal(v.cpu().numpy().view(np.uint32), o.view(np.uint32))
+    assert_no_device_error()
+
+
+def test_kivi_pack_value_skips_padding_and_rejects_misaligned_keys():
+    from qkv_b200.ops import kivi_pack_key_cache, kivi_pack_value_cache
+
+    H, D, blk, g = 2, 32, 16, 8
+    views = _empty_views(4, blk, H, D, g, fill_scale=7.0)
+    value = torch.randn(3, H, D, device=dev())
+    kivi_pack_value_cache(value, torch.tensor([-1, -1, -1], device=dev()), *views[3:], g)
+    assert torch.equal(views[4], torch.full_like(views[4], 7.0))  # nothing written
+    key = torch.randn(g, H, D, device=dev())
+    with pytest.raises(RuntimeError, match="group-size aligned|contiguous"):
+        kivi_pack_key_cache(key, torch.arange(1, 1 + g, device=dev()), *views[:3], g)
+    with pytest.raises(RuntimeError, match="must be contiguous"):
+        kivi_pack_value_cache(value.transpose(0, 1), torch.arange(3, device=dev()), *views[3:], g)
+
+
+# ---------------------------------------------------------------- KIVI decode
+
+
+def _kivi_decode_case(rng, lens, k_res, v_res, Hq, H, D, g, blk, cap):
+    """Packs each request's history through the oracle and builds bf16
+    residual windows holding its last positions (ring rotated by a random
+    start)."""
+    B = len(lens)
+    maxb = max((L + blk - 1) // blk for L in lens)
+    nb = sum((L + blk - 1) // blk for L in lens) + 1
+    perm = rng.permutation(nb)
+    bt = np.zeros((B, maxb), np.int32)
+    views = [
+        np.zeros((nb, H, D, blk // 8), np.int32), np.ones((nb, H, D, blk // g), np.float32),
+        np.zeros((nb, H, D, blk // g), np.float32), np.zeros((nb, blk, H, D // 8), np.int32),
+        np.ones((nb, blk, H, D // g), np.float32), np.zeros((nb, blk, H, D // g), np.float32),
+    ]
+    res_k = np.zeros((B + 1, cap, H, D), np.float32)
+    res_v = np.zeros_like(res_k)
+    state = np.zeros((B, 6), np.int32)
+    k_win, v_win, full_k, full_v = [], [], [], []
+    cur = 0
+    for b, L in enumerate(lens):
+        n = (L + blk - 1) // blk
+        bt[b, :n] = perm[cur:cur + n]
+        cur += n
+        K = kv_data(rng, L, H, D, 0.02, 10.0)
+        V = kv_data(rng, L, H, D, 0.0, 1.0)
+        full_k.append(K)
+        full_v.append(V)
+        pos = np.arange(L)
+        slots = bt[b, pos // blk].astype(np.int64) * blk + pos % blk
+        kh = ((L - k_res[b]) // g) * g  # whole groups of history (pages of garbage after)
+        O.kivi_pack_key(K[:kh], slots[:kh], *views[:3], g)
+        O.kivi_pack_value(V[: L - v_res[b]], slots[: L - v_res[b]], *views[3:], g)
+        row = B - b  # rows shuffled
+        ks, vs = int(rng.integers(0, cap)), int(rng.integers(0, cap))
+        for i in range(k_res[b]):
+            res_k[row, (ks + i) % cap] = K[L - k_res[b] + i]
+        for i in range(v_res[b]):
+            res_v[row, (vs + i) % cap] = V[L - v_res[b] + i]
+        state[b] = [row, ks, k_res[b], vs, v_res[b], L]
+    return views, bt, res_k, res_v, state
+
+
+@pytest.mark.parametrize(
+    "lens,k_res,v_res,Hq,H,D,g,blk,cap",
+    [
+        ([1024, 3000, 5000, 8192], [128, 1, 64, 0], [128, 128, 128, 0], 40, 8, 128, 128, 128, 128),  # config 2
+        ([6144, 2100], [16, 128], [128, 37], 32, 8, 128, 64, 128, 128),  # group 64
+        ([3, 100, 129], [3, 100, 1], [3, 100, 128], 32, 8, 128, 128, 128, 128),  # window covers everything
+        ([40, 77], [8, 5], [16, 16], 4, 2, 32, 8, 16, 16),  # reference toy geometry
+        ([300, 1000], [64, 100], [128, 128], 8, 1, 256, 128, 128, 128),  # head 256 / 1 kv head
+        ([2000], [32], [32], 64, 8, 128, 128, 128, 128),  # GQA 8
+    ],
+)
+def test_kivi_paged_decode_vs_oracle(lens, k_res, v_res, Hq, H, D, g, blk, cap):
+    from qkv_b200.ops import kivi_paged_decode
+
+    rng = np.random.default_rng(sum(lens) + D)
+    views, bt, res_k, res_v, state = _kivi_decode_case(rng, lens, k_res, v_res, Hq, H, D, g, blk, cap)
+    B = len(lens)
+    q = O.bf16_round(rng.standard_normal((B, Hq, D)).astype(np.float32))
+    scale = D ** -0.5
+    out = torch.zeros(B, Hq, D, dtype=torch.bfloat16, device=dev())
+    tv = tuple(torch.from_numpy(v).to(dev()) for v in views)
+    kivi_paged_decode(
+        bf16_tensor(q), tv, bf16_tensor(res_k), bf16_tensor(res_v), torch.from_numpy(bt).to(dev()),
+        torch.tensor(lens, dtype=torch.int32, device=dev()), torch.from_numpy(state).to(dev()), g, scale, out,
+        max(lens),
+    )
+    dk, dv = O.kivi_dequant_gather(*views, bt, lens, g, target_bf16=True)
+    kw = [[res_k[state[b, 0], (state[b, 1] + i) % cap] for i in range(k_res[b])] or None for b in range(B)]
+    vw = [[res_v[state[b, 0], (state[b, 3] + i) % cap] for i in range(v_res[b])] or None for b in range(B)]
+    dk, dv = O.overwrite_residual_tail(dk, dv, lens, kw, vw)
+    want = O.dense_attention(q, dk, dv, [1] * B, lens, scale, causal=True)
+    got = to_np(out)
+    assert np.isfinite(got).all()
+    err = np.max(np.abs(got - want))
+    assert err <= ATOL, err
+    assert_no_device_error()
+
+
+def test_kivi_decode_records_bad_block_ids_without_faulting():
+    """A block id beyond the cache is skipped and reported, never read."""
+    from qkv_b200.ops import kivi_paged_decode
+
+    H, D, g, blk = 2, 64, 64, 64
+    views = tuple(torch.from_numpy(v).to(dev()) for v in (
+        np.zeros((2, H, D, blk // 8), np.int32), np.ones((2, H, D, 1), np.float32), np.zeros((2, H, D, 1), np.float32),
+        np.zeros((2, blk, H, D // 8), np.int32), np.ones((2, blk, H, 1), np.float32), np.zeros((2, blk, H, 1), np.float32),
+    ))
+    bt = torch.tensor([[0, 5]], dtype=torch.int32, device=dev())  # 5 >= num_blocks
+    out = torch.zeros(1, 4, D, dtype=torch.bfloat16, device=dev())
+    q = torch.randn(1, 4, D, device=dev()).to(torch.bfloat16)
+    kivi_paged_decode(q, views, None, None, bt, torch.tensor([100], dtype=torch.int32, device=dev()), None, g,
+                      0.1, out, 100)
+    from qkv_b200.ops import _lib
+
+    code = _lib.device_error(torch.cuda.current_stream().cuda_stream)
+    assert code == 2  # block id out of range
+    assert torch.isfinite(out.float()).all()
+
+
+# ---------------------------------------------------------------- dense prefill
+
+
+@pytest.mark.parametrize("q_lens,kv_lens,Hq,H,D,causal", [
+    ([5, 33], [5, 33], 32, 8, 128, True),
+    ([1, 64, 7], [1, 64, 7], 4, 2, 64, True),
+    ([16], [16], 8, 8, 128, False),
+    ([200], [200], 40, 8, 128, True),
+])
+def test_dense_prefill_vs_oracle(q_lens, kv_lens, Hq, H, D, causal):
+    from qkv_b200.ops import dense_prefill
+
+    rng = np.random.default_rng(sum(q_lens))
+    q = O.bf16_round(rng.standard_normal((sum(q_lens), Hq, D)).astype(np.float32))
+    k = kv_data(rng, sum(kv_lens), H, D, 0.02, 5.0)
+    v = kv_data(rng, sum(kv_lens), H, D, 0.0, 1.0)
+    scale = D ** -0.5
+    out = torch.zeros(sum(q_lens), Hq, D, dtype=torch.bfloat16, device=dev())
+    dense_prefill(bf16_tensor(q), bf16_tensor(k), bf16_tensor(v), q_lens, kv_lens, scale, out, causal=causal)
+    want = O.dense_attention(q, k, v, q_lens, kv_lens, scale, causal=causal)
+    assert np.max(np.abs(to_np(out) - want)) <= ATOL

@@ -1,0 +1,281 @@
+// C ABI of the paged decode kernels: argument validation, split planning and
+// dispatch between the tensor-core kernels (production geometries) and the
+// geometry-general CUDA-core kernels.
+#include <cmath>
+
+#include "decode_common.cuh"
+
+namespace qkv {
+
+int launch_decode_generic(const DecodeParams& p, int mode, cudaStream_t stream);
+// Returns QKV_ERR_UNSUPPORTED (without recording an error) when the geometry
+// has no tensor-core kernel; the caller then runs the generic kernel.
+int launch_decode_mma(const DecodeParams& p, bool kivi, cudaStream_t stream);
+bool decode_mma_supported(const DecodeParams& p, bool kivi);
+SplitPlan plan_for(const DecodeParams& p, bool kivi, int max_seq_len);
+
+namespace {
+
+int check_decode_args(const char* fn, int batch, int num_heads, int kvh,
+                      int head_size, int block_size, int64_t num_blocks,
+                      int max_seq_len) {
+  const std::string f(fn);
+  QKV_CHECK_ARG(batch >= 0 && kvh > 0 && num_heads > 0 && num_blocks > 0,
+                f + ": bad sizes");
+  QKV_CHECK_ARG(num_heads % kvh == 0,
+                f + ": num_heads must be a multiple of num_kv_heads");
+  QKV_CHECK_ARG(head_size > 0 && head_size % 8 == 0 && head_size <= 256,
+                f + ": head_size must be a multiple of 8 and <= 256");
+  QKV_CHECK_ARG(block_size > 0 && block_size % 8 == 0,
+                f + ": block_size must be a multiple of 8");
+  QKV_CHECK_ARG(max_seq_len >= 0, f + ": max_seq_len must be >= 0");
+  return QKV_OK;
+}
+
+}  // namespace
+
+SplitPlan plan_for(const DecodeParams& p, bool kivi, int max_seq_len) {
+  if (decode_mma_supported(p, kivi))
+    return plan_splits(p.batch, p.kvh, p.blk, max_seq_len, kivi, sm_count(), 2,
+                       1024);
+  return plan_splits(p.batch, p.kvh, p.blk, max_seq_len, kivi, sm_count(), 4,
+                     256);
+}
+
+}  // namespace qkv
+
+extern "C" {
+
+size_t qkv_int8_paged_decode_workspace(int batch, int num_heads,
+                                       int num_kv_heads, int head_size,
+                                       int block_size, int max_seq_len) {
+  using namespace qkv;
+  if (batch <= 0 || num_kv_heads <= 0 || block_size <= 0) return 0;
+  DecodeParams p{};
+  p.batch = batch;
+  p.num_heads = num_heads;
+  p.kvh = num_kv_heads;
+  p.head_size = head_size;
+  p.gqa = num_heads / num_kv_heads;
+  p.blk = block_size;
+  p.group = head_size;
+  const SplitPlan plan = plan_for(p, false, max_seq_len);
+  return workspace_bytes(batch, num_heads, head_size, plan.total);
+}
+
+size_t qkv_kivi_paged_decode_workspace(int batch, int num_heads,
+                                       int num_kv_heads, int head_size,
+                                       int group_size, int block_size,
+                                       int max_seq_len) {
+  using namespace qkv;
+  if (batch <= 0 || num_kv_heads <= 0 || block_size <= 0) return 0;
+  DecodeParams p{};
+  p.batch = batch;
+  p.num_heads = num_heads;
+  p.kvh = num_kv_heads;
+  p.head_size = head_size;
+  p.gqa = num_heads / num_kv_heads;
+  p.blk = block_size;
+  p.group = group_size;
+  const SplitPlan plan = plan_for(p, true, max_seq_len);
+  return workspace_bytes(batch, num_heads, head_size, plan.total);
+}
+
+int qkv_int8_paged_decode(const void* query, int64_t q_stride,
+                          const int8_t* key_cache, const int8_t* value_cache,
+                          const void* k_aq_scale, const void* v_aq_scale,
+                          const int32_t* block_table, int64_t bt_stride,
+                          const int32_t* seq_lens, int batch, int num_heads,
+                          int num_kv_heads, int head_size, int block_size,
+                          int64_t num_blocks, int max_seq_len, float scale,
+                          void* workspace, size_t workspace_bytes_, void* out,
+                          int64_t out_stride, qkv_stream_t stream) {
+  using namespace qkv;
+  int rc = check_decode_args("qkv_int8_paged_decode", batch, num_heads,
+                             num_kv_heads, head_size, block_size, num_blocks,
+                             max_seq_len);
+  if (rc != QKV_OK) return rc;
+  if (batch == 0) return QKV_OK;
+  QKV_CHECK_ARG(query && key_cache && value_cache && k_aq_scale && v_aq_scale &&
+                    block_table && seq_lens && out,
+                "qkv_int8_paged_decode: null pointer");
+  DecodeParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(query);
+  p.q_stride = q_stride;
+  p.kc = key_cache;
+  p.vc = value_cache;
+  p.k_aq = static_cast<const __nv_bfloat16*>(k_aq_scale);
+  p.v_aq = static_cast<const __nv_bfloat16*>(v_aq_scale);
+  p.bt = block_table;
+  p.bt_stride = bt_stride;
+  p.seq_lens = seq_lens;
+  p.batch = batch;
+  p.num_heads = num_heads;
+  p.kvh = num_kv_heads;
+  p.head_size = head_size;
+  p.gqa = num_heads / num_kv_heads;
+  p.group = head_size;
+  p.blk = block_size;
+  p.num_blocks = num_blocks;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_stride = out_stride;
+  p.err = device_error_ptr();
+  const SplitPlan plan = plan_for(p, false, max_seq_len);
+  p.num_hist_splits = plan.hist_splits;
+  p.split_tokens = plan.split_tokens;
+  p.splits_total = plan.total;
+  const size_t need = workspace_bytes(batch, num_heads, head_size, plan.total);
+  if (need > 0) {
+    if (workspace == nullptr || workspace_bytes_ < need)
+      return set_error(QKV_ERR_WORKSPACE,
+                       "qkv_int8_paged_decode: workspace needs " +
+                           std::to_string(need) + " bytes");
+    p.ws_acc = static_cast<float*>(workspace);
+    p.ws_ml = p.ws_acc + static_cast<size_t>(batch) * num_heads * plan.total *
+                             head_size;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (decode_mma_supported(p, false)) return launch_decode_mma(p, false, s);
+  return launch_decode_generic(p, kInt8Pages, s);
+}
+
+int qkv_kivi_paged_decode(
+    const void* query, int64_t q_stride, const int32_t* k_quant,
+    const float* k_scale, const float* k_mn, const int32_t* v_quant,
+    const float* v_scale, const float* v_mn, const void* res_key,
+    const void* res_value, int res_rows, int res_capacity,
+    const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
+    const int32_t* res_state, int batch, int num_heads, int num_kv_heads,
+    int head_size, int group_size, int block_size, int64_t num_blocks,
+    int max_seq_len, float scale, void* workspace, size_t workspace_bytes_,
+    void* out, int64_t out_stride, qkv_stream_t stream) {
+  using namespace qkv;
+  int rc = check_decode_args("qkv_kivi_paged_decode", batch, num_heads,
+                             num_kv_heads, head_size, block_size, num_blocks,
+                             max_seq_len);
+  if (rc != QKV_OK) return rc;
+  QKV_CHECK_ARG(group_size > 0 && group_size % 8 == 0 &&
+                    head_size % group_size == 0 && block_size % group_size == 0,
+                "qkv_kivi_paged_decode: group_size must be a multiple of 8 "
+                "dividing head_size and block_size");
+  QKV_CHECK_ARG(res_state == nullptr || (res_rows > 0 && res_capacity > 0),
+                "qkv_kivi_paged_decode: residual window needs rows and capacity");
+  if (batch == 0) return QKV_OK;
+  QKV_CHECK_ARG(query && k_quant && k_scale && k_mn && v_quant && v_scale &&
+                    v_mn && block_table && seq_lens && out,
+                "qkv_kivi_paged_decode: null pointer");
+  QKV_CHECK_ARG(res_state == nullptr || (res_key && res_value),
+                "qkv_kivi_paged_decode: residual buffers are NULL");
+  DecodeParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(query);
+  p.q_stride = q_stride;
+  p.kq = k_quant;
+  p.ks = k_scale;
+  p.km = k_mn;
+  p.vq = v_quant;
+  p.vs = v_scale;
+  p.vm = v_mn;
+  p.rk = static_cast<const __nv_bfloat16*>(res_key);
+  p.rv = static_cast<const __nv_bfloat16*>(res_value);
+  p.res_rows = res_rows;
+  p.res_cap = res_capacity;
+  p.res_state = res_state;
+  p.bt = block_table;
+  p.bt_stride = bt_stride;
+  p.seq_lens = seq_lens;
+  p.batch = batch;
+  p.num_heads = num_heads;
+  p.kvh = num_kv_heads;
+  p.head_size = head_size;
+  p.gqa = num_heads / num_kv_heads;
+  p.group = group_size;
+  p.blk = block_size;
+  p.num_blocks = num_blocks;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_stride = out_stride;
+  p.err = device_error_ptr();
+  const SplitPlan plan = plan_for(p, true, max_seq_len);
+  p.num_hist_splits = plan.hist_splits;
+  p.split_tokens = plan.split_tokens;
+  p.splits_total = plan.total;
+  const size_t need = workspace_bytes(batch, num_heads, head_size, plan.total);
+  if (need > 0) {
+    if (workspace == nullptr || workspace_bytes_ < need)
+      return set_error(QKV_ERR_WORKSPACE,
+                       "qkv_kivi_paged_decode: workspace needs " +
+                           std::to_string(need) + " bytes");
+    p.ws_acc = static_cast<float*>(workspace);
+    p.ws_ml = p.ws_acc + static_cast<size_t>(batch) * num_heads * plan.total *
+                             head_size;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (decode_mma_supported(p, true)) return launch_decode_mma(p, true, s);
+  return launch_decode_generic(p, kKiviPages, s);
+}
+
+size_t qkv_dense_prefill_workspace(int total_q, int num_heads,
+                                   int num_kv_heads, int head_size,
+                                   int max_kv_len) {
+  using namespace qkv;
+  if (total_q <= 0 || num_kv_heads <= 0) return 0;
+  const SplitPlan plan = plan_splits(total_q, num_kv_heads, 128, max_kv_len,
+                                     false, sm_count(), 4, 512);
+  return workspace_bytes(total_q, num_heads, head_size, plan.total);
+}
+
+int qkv_dense_prefill(const void* query, const void* key, const void* value,
+                      const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
+                      int num_reqs, int total_q, int num_heads,
+                      int num_kv_heads, int head_size, int causal,
+                      int max_kv_len, float scale, void* workspace,
+                      size_t workspace_bytes_, void* out, qkv_stream_t stream) {
+  using namespace qkv;
+  QKV_CHECK_ARG(num_reqs >= 0 && total_q >= 0 && num_kv_heads > 0 &&
+                    num_heads > 0 && num_heads % num_kv_heads == 0,
+                "qkv_dense_prefill: bad sizes");
+  QKV_CHECK_ARG(head_size > 0 && head_size % 8 == 0 && head_size <= 256,
+                "qkv_dense_prefill: head_size must be a multiple of 8 and <= 256");
+  if (total_q == 0 || num_reqs == 0) return QKV_OK;
+  QKV_CHECK_ARG(query && key && value && cu_seqlens_q && cu_seqlens_k && out,
+                "qkv_dense_prefill: null pointer");
+  DecodeParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(query);
+  p.q_stride = static_cast<int64_t>(num_heads) * head_size;
+  p.dk = static_cast<const __nv_bfloat16*>(key);
+  p.dv = static_cast<const __nv_bfloat16*>(value);
+  p.cu_q = cu_seqlens_q;
+  p.cu_k = cu_seqlens_k;
+  p.num_reqs = num_reqs;
+  p.causal = causal;
+  p.batch = total_q;
+  p.num_heads = num_heads;
+  p.kvh = num_kv_heads;
+  p.head_size = head_size;
+  p.gqa = num_heads / num_kv_heads;
+  p.group = head_size;
+  p.blk = 128;
+  p.num_blocks = 1;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_stride = static_cast<int64_t>(num_heads) * head_size;
+  p.err = device_error_ptr();
+  const SplitPlan plan = plan_splits(total_q, num_kv_heads, 128, max_kv_len,
+                                     false, sm_count(), 4, 512);
+  p.num_hist_splits = plan.hist_splits;
+  p.split_tokens = plan.split_tokens;
+  p.splits_total = plan.total;
+  const size_t need = workspace_bytes(total_q, num_heads, head_size, plan.total);
+  if (need > 0) {
+    if (workspace == nullptr || workspace_bytes_ < need)
+      return set_error(QKV_ERR_WORKSPACE, "qkv_dense_prefill: workspace needs " +
+                                              std::to_string(need) + " bytes");
+    p.ws_acc = static_cast<float*>(workspace);
+    p.ws_ml = p.ws_acc + static_cast<size_t>(total_q) * num_heads * plan.total *
+                             head_size;
+  }
+  return launch_decode_generic(p, kDense, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

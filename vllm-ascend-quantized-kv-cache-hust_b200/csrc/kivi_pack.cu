@@ -1,0 +1,408 @@
+// KIVI INT4 pack kernels: full-precision K/V -> the paged int4 views.
+//
+// Bit-exact restatement of the reference pack arithmetic
+// (ops/triton/kivi_pack.py:61-131 value kernel, :134-226 key kernel; the CPU
+// contract is KiviInt4Semantics.group_scale / quantize_group / pack_int4,
+// methods/kivi_int4/semantics.py:76-111):
+//   scale = max((mx - mn) / 15, 1e-6)                 fp32, IEEE division
+//   code  = clamp(floor((x - mn) / scale + 0.5), 0, 15)
+//   word  = OR_L (code_L & 0xF) << 4L                 lane L at bits 4L
+// Every operation is written with explicit round-to-nearest intrinsics so the
+// compiler cannot contract or reassociate it.
+#include "qkv_common.cuh"
+
+namespace qkv {
+namespace {
+
+__device__ __forceinline__ float group_scale(float mn, float mx) {
+  return fmaxf(__fdiv_rn(__fsub_rn(mx, mn), 15.0f), 1.0e-6f);
+}
+
+__device__ __forceinline__ uint32_t quantize_code(float x, float mn,
+                                                  float scale) {
+  float q = floorf(__fadd_rn(__fdiv_rn(__fsub_rn(x, mn), scale), 0.5f));
+  q = fminf(fmaxf(q, 0.0f), 15.0f);
+  return static_cast<uint32_t>(static_cast<int>(q)) & 0xFu;
+}
+
+// Loads 8 consecutive elements starting at p (8-element aligned) as fp32.
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&v)[8]);
+
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float (&v)[8]) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0];
+  const float4 b = reinterpret_cast<const float4*>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p,
+                                                     float (&v)[8]) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+template <>
+__device__ __forceinline__ void load8<__half>(const __half* p, float (&v)[8]) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(p);
+  const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+// ------------------------------------------------------------------ values
+
+// One thread per (token, head, 8-dim word). The D/8 threads of a
+// (token, head) row are a power-of-two aligned run inside one warp, and a
+// quant group is an aligned run of g/8 of them, so the group min/max is an
+// xor-shuffle reduction. Every lane takes part in the shuffles; only lanes
+// with a valid slot store.
+template <typename T>
+__global__ void __launch_bounds__(256)
+pack_value_kernel(const T* __restrict__ value, const void* __restrict__ slots,
+                  int slot_dtype, int64_t num_tokens, int kvh, int head_size,
+                  int group_size, int64_t num_slots, int32_t* __restrict__ v_quant,
+                  float* __restrict__ v_scale, float* __restrict__ v_mn, int* err) {
+  const int words = head_size >> 3;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t total = num_tokens * kvh * words;
+  const bool in_range = tid < total;
+  const int64_t t_idx = in_range ? tid : 0;
+  const int w = static_cast<int>(t_idx % words);
+  const int64_t row = t_idx / words;  // token * kvh + head
+  const int64_t token = row / kvh;
+  const int head = static_cast<int>(row % kvh);
+
+  int64_t slot = -1;
+  if (in_range) slot = load_index(slots, slot_dtype, token);
+  bool valid = in_range && slot >= 0;
+  if (valid && slot >= num_slots) {
+    record_error(err, kErrSlot);
+    valid = false;
+  }
+
+  float v[8];
+  if (in_range) {
+    load8<T>(value + row * head_size + w * 8, v);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+  }
+  float mn = v[0], mx = v[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) {
+    mn = fminf(mn, v[i]);
+    mx = fmaxf(mx, v[i]);
+  }
+  const int gw = group_size >> 3;  // words per group (power of two)
+  for (int off = 1; off < gw; off <<= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  }
+  if (!valid) return;
+  const float scale = group_scale(mn, mx);
+  uint32_t word = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) word |= quantize_code(v[i], mn, scale) << (4 * i);
+  const int64_t dst_row = slot * kvh + head;  // [NB*B, KVH] flattened
+  v_quant[dst_row * words + w] = static_cast<int32_t>(word);
+  if ((w & (gw - 1)) == 0) {
+    const int groups = head_size / group_size;
+    const int64_t s = dst_row * groups + w / gw;
+    v_scale[s] = scale;
+    v_mn[s] = mn;
+  }
+}
+
+// Generic value packer for head sizes whose word count is not a power of two
+// up to 32: one thread per (token, head, group).
+template <typename T>
+__global__ void pack_value_generic_kernel(
+    const T* __restrict__ value, const void* __restrict__ slots, int slot_dtype,
+    int64_t num_tokens, int kvh, int head_size, int group_size, int64_t num_slots,
+    int32_t* __restrict__ v_quant, float* __restrict__ v_scale,
+    float* __restrict__ v_mn, int* err) {
+  const int groups = head_size / group_size;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (tid >= num_tokens * kvh * groups) return;
+  const int grp = static_cast<int>(tid % groups);
+  const int64_t row = tid / groups;
+  const int64_t token = row / kvh;
+  const int head = static_cast<int>(row % kvh);
+  const int64_t slot = load_index(slots, slot_dtype, token);
+  if (slot < 0) return;
+  if (slot >= num_slots) {
+    record_error(err, kErrSlot);
+    return;
+  }
+  const T* src = value + row * head_size + grp * group_size;
+  float mn = to_f32(src[0]), mx = mn;
+  for (int i = 1; i < group_size; ++i) {
+    const float x = to_f32(src[i]);
+    mn = fminf(mn, x);
+    mx = fmaxf(mx, x);
+  }
+  const float scale = group_scale(mn, mx);
+  const int64_t dst_row = slot * kvh + head;
+  for (int wbase = 0; wbase < group_size; wbase += 8) {
+    uint32_t word = 0;
+    for (int i = 0; i < 8; ++i)
+      word |= quantize_code(to_f32(src[wbase + i]), mn, scale) << (4 * i);
+    v_quant[dst_row * (head_size >> 3) + (grp * group_size + wbase) / 8] =
+        static_cast<int32_t>(word);
+  }
+  v_scale[dst_row * groups + grp] = scale;
+  v_mn[dst_row * groups + grp] = mn;
+}
+
+// -------------------------------------------------------------------- keys
+
+// One thread per (token group, head, channel). The group's g tokens of this
+// channel are reduced to mn/mx, then re-read (L1/L2 hit) and packed 8 tokens
+// per int32 word; the g/8 words of a channel are contiguous in k_quant
+// ([NB, KVH, D, B/8]) and are stored as 16-byte vectors when aligned.
+template <typename T, int GW>
+__global__ void __launch_bounds__(128)
+pack_key_kernel(const T* __restrict__ key, const void* __restrict__ slots,
+                int slot_dtype, int64_t num_groups, int kvh, int head_size,
+                int block_size, int64_t num_blocks, int32_t* __restrict__ k_quant,
+                float* __restrict__ k_scale, float* __restrict__ k_mn, int* err,
+                bool vector_store) {
+  constexpr int kGroup = GW * 8;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (tid >= num_groups * kvh * head_size) return;
+  const int d = static_cast<int>(tid % head_size);
+  const int64_t gh = tid / head_size;
+  const int head = static_cast<int>(gh % kvh);
+  const int64_t gi = gh / kvh;
+
+  const int64_t first_slot = load_index(slots, slot_dtype, gi * kGroup);
+  if (first_slot < 0) return;  // the reference kernel skips such groups
+  const int64_t blk = first_slot / block_size;
+  const int off = static_cast<int>(first_slot - blk * block_size);
+  if (blk >= num_blocks || (off % kGroup) != 0 || off + kGroup > block_size) {
+    record_error(err, kErrSlot);
+    return;
+  }
+
+  const int64_t row_stride = static_cast<int64_t>(kvh) * head_size;
+  const T* src = key + gi * kGroup * row_stride + head * head_size + d;
+  float mn = to_f32(src[0]), mx = mn;
+#pragma unroll 8
+  for (int t = 1; t < kGroup; ++t) {
+    const float x = to_f32(src[t * row_stride]);
+    mn = fminf(mn, x);
+    mx = fmaxf(mx, x);
+  }
+  const float scale = group_scale(mn, mx);
+
+  uint32_t words[GW];
+#pragma unroll
+  for (int j = 0; j < GW; ++j) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int l = 0; l < 8; ++l)
+      word |= quantize_code(to_f32(src[(j * 8 + l) * row_stride]), mn, scale)
+              << (4 * l);
+    words[j] = word;
+  }
+  const int64_t chan = (blk * kvh + head) * static_cast<int64_t>(head_size) + d;
+  int32_t* dst = k_quant + chan * (block_size >> 3) + (off >> 3);
+  if (GW % 4 == 0 && vector_store) {
+#pragma unroll
+    for (int j = 0; j + 3 < GW; j += 4)
+      reinterpret_cast<uint4*>(dst)[j / 4] =
+          make_uint4(words[j], words[j + 1], words[j + 2], words[j + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < GW; ++j) dst[j] = static_cast<int32_t>(words[j]);
+  }
+  const int64_t s = chan * (block_size / kGroup) + off / kGroup;
+  k_scale[s] = scale;
+  k_mn[s] = mn;
+}
+
+template <typename T>
+int launch_pack_key(const void* key, const void* slots, int slot_dtype,
+                    int64_t num_tokens, int kvh, int head_size, int group_size,
+                    int block_size, int64_t num_blocks, int32_t* kq, float* ks,
+                    float* km, cudaStream_t stream) {
+  const int64_t groups = num_tokens / group_size;
+  const int64_t threads = groups * kvh * head_size;
+  const int block = 128;
+  const int64_t grid = (threads + block - 1) / block;
+  const T* k = static_cast<const T*>(key);
+  int* err = device_error_ptr();
+  // 16-byte stores need a 16-byte aligned k_quant base and rows of whole
+  // 16-byte units; group offsets are multiples of g/8 words (a multiple of 4
+  // whenever the vector path is taken)
+  const bool vec = (reinterpret_cast<uintptr_t>(kq) & 15u) == 0 &&
+                   ((block_size / 8) % 4) == 0;
+#define QKV_PACK_KEY_CASE(GW)                                                  \
+  case GW:                                                                     \
+    pack_key_kernel<T, GW><<<grid, block, 0, stream>>>(                        \
+        k, slots, slot_dtype, groups, kvh, head_size, block_size, num_blocks, \
+        kq, ks, km, err, vec);                                                 \
+    break;
+  switch (group_size / 8) {
+    QKV_PACK_KEY_CASE(1)
+    QKV_PACK_KEY_CASE(2)
+    QKV_PACK_KEY_CASE(3)
+    QKV_PACK_KEY_CASE(4)
+    QKV_PACK_KEY_CASE(6)
+    QKV_PACK_KEY_CASE(8)
+    QKV_PACK_KEY_CASE(12)
+    QKV_PACK_KEY_CASE(16)
+    QKV_PACK_KEY_CASE(24)
+    QKV_PACK_KEY_CASE(32)
+    default:
+      return set_error(QKV_ERR_UNSUPPORTED,
+                       "qkv_kivi_pack_key: group_size " +
+                           std::to_string(group_size) +
+                           " is not one of 8,16,24,32,48,64,96,128,192,256");
+  }
+#undef QKV_PACK_KEY_CASE
+  QKV_CHECK_LAUNCH("pack_key_kernel");
+  return QKV_OK;
+}
+
+template <typename T>
+int launch_pack_value(const void* value, const void* slots, int slot_dtype,
+                      int64_t num_tokens, int kvh, int head_size, int group_size,
+                      int block_size, int64_t num_blocks, int32_t* vq, float* vs,
+                      float* vm, cudaStream_t stream) {
+  const int words = head_size / 8;
+  const int64_t num_slots = num_blocks * block_size;
+  const T* v = static_cast<const T*>(value);
+  int* err = device_error_ptr();
+  const bool pow2 = (words & (words - 1)) == 0 && words <= 32;
+  // the vector path loads 8 elements (16 or 32 bytes) per thread
+  const bool aligned = (reinterpret_cast<uintptr_t>(value) & 15u) == 0;
+  if (pow2 && aligned) {
+    const int64_t threads = num_tokens * kvh * words;
+    const int block = 256;
+    const int64_t grid = (threads + block - 1) / block;
+    pack_value_kernel<T><<<grid, block, 0, stream>>>(
+        v, slots, slot_dtype, num_tokens, kvh, head_size, group_size, num_slots,
+        vq, vs, vm, err);
+    QKV_CHECK_LAUNCH("pack_value_kernel");
+  } else {
+    const int64_t threads = num_tokens * kvh * (head_size / group_size);
+    const int block = 128;
+    const int64_t grid = (threads + block - 1) / block;
+    pack_value_generic_kernel<T><<<grid, block, 0, stream>>>(
+        v, slots, slot_dtype, num_tokens, kvh, head_size, group_size, num_slots,
+        vq, vs, vm, err);
+    QKV_CHECK_LAUNCH("pack_value_generic_kernel");
+  }
+  return QKV_OK;
+}
+
+int check_common(const char* fn, int dtype, int slot_dtype, int64_t num_tokens,
+                 int kvh, int head_size, int group_size, int block_size,
+                 int64_t num_blocks) {
+  const std::string f(fn);
+  QKV_CHECK_ARG(dtype == QKV_F32 || dtype == QKV_BF16 || dtype == QKV_F16,
+                f + ": unsupported input dtype");
+  QKV_CHECK_ARG(slot_dtype == QKV_I32 || slot_dtype == QKV_I64,
+                f + ": slot_mapping must be int32/int64");
+  QKV_CHECK_ARG(num_tokens >= 0 && kvh > 0 && num_blocks > 0,
+                f + ": bad sizes");
+  QKV_CHECK_ARG(group_size > 0 && group_size % 8 == 0,
+                f + ": group_size must be a positive multiple of 8");
+  QKV_CHECK_ARG(head_size > 0 && head_size % 8 == 0 && head_size <= 1024,
+                f + ": head_size must be a multiple of 8 (<= 1024)");
+  QKV_CHECK_ARG(block_size > 0 && block_size % 8 == 0,
+                f + ": block_size must be a multiple of 8");
+  return QKV_OK;
+}
+
+}  // namespace
+}  // namespace qkv
+
+extern "C" {
+
+int qkv_kivi_pack_key(const void* key, int key_dtype, const void* slot_mapping,
+                      int slot_dtype, int64_t num_tokens, int num_kv_heads,
+                      int head_size, int group_size, int block_size,
+                      int64_t num_blocks, int32_t* k_quant, float* k_scale,
+                      float* k_mn, qkv_stream_t stream) {
+  using namespace qkv;
+  int rc = check_common("qkv_kivi_pack_key", key_dtype, slot_dtype, num_tokens,
+                        num_kv_heads, head_size, group_size, block_size,
+                        num_blocks);
+  if (rc != QKV_OK) return rc;
+  QKV_CHECK_ARG(num_tokens % group_size == 0,
+                "qkv_kivi_pack_key: num_tokens must be a whole number of groups");
+  QKV_CHECK_ARG(block_size % group_size == 0,
+                "qkv_kivi_pack_key: block_size must be divisible by group_size");
+  if (num_tokens == 0) return QKV_OK;
+  QKV_CHECK_ARG(key && slot_mapping && k_quant && k_scale && k_mn,
+                "qkv_kivi_pack_key: null pointer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (key_dtype) {
+    case QKV_F32:
+      return launch_pack_key<float>(key, slot_mapping, slot_dtype, num_tokens,
+                                    num_kv_heads, head_size, group_size,
+                                    block_size, num_blocks, k_quant, k_scale,
+                                    k_mn, s);
+    case QKV_BF16:
+      return launch_pack_key<__nv_bfloat16>(
+          key, slot_mapping, slot_dtype, num_tokens, num_kv_heads, head_size,
+          group_size, block_size, num_blocks, k_quant, k_scale, k_mn, s);
+    default:
+      return launch_pack_key<__half>(key, slot_mapping, slot_dtype, num_tokens,
+                                     num_kv_heads, head_size, group_size,
+                                     block_size, num_blocks, k_quant, k_scale,
+                                     k_mn, s);
+  }
+}
+
+int qkv_kivi_pack_value(const void* value, int value_dtype,
+                        const void* slot_mapping, int slot_dtype,
+                        int64_t num_tokens, int num_kv_heads, int head_size,
+                        int group_size, int block_size, int64_t num_blocks,
+                        int32_t* v_quant, float* v_scale, float* v_mn,
+                        qkv_stream_t stream) {
+  using namespace qkv;
+  int rc = check_common("qkv_kivi_pack_value", value_dtype, slot_dtype,
+                        num_tokens, num_kv_heads, head_size, group_size,
+                        block_size, num_blocks);
+  if (rc != QKV_OK) return rc;
+  QKV_CHECK_ARG(head_size % group_size == 0,
+                "qkv_kivi_pack_value: head_size must be divisible by group_size");
+  if (num_tokens == 0) return QKV_OK;
+  QKV_CHECK_ARG(value && slot_mapping && v_quant && v_scale && v_mn,
+                "qkv_kivi_pack_value: null pointer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (value_dtype) {
+    case QKV_F32:
+      return launch_pack_value<float>(value, slot_mapping, slot_dtype,
+                                      num_tokens, num_kv_heads, head_size,
+                                      group_size, block_size, num_blocks,
+                                      v_quant, v_scale, v_mn, s);
+    case QKV_BF16:
+      return launch_pack_value<__nv_bfloat16>(
+          value, slot_mapping, slot_dtype, num_tokens, num_kv_heads, head_size,
+          group_size, block_size, num_blocks, v_quant, v_scale, v_mn, s);
+    default:
+      return launch_pack_value<__half>(value, slot_mapping, slot_dtype,
+                                       num_tokens, num_kv_heads, head_size,
+                                       group_size, block_size, num_blocks,
+                                       v_quant, v_scale, v_mn, s);
+  }
+}
+
+}  // extern "C"

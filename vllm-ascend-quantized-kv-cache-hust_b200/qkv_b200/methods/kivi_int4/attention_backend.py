@@ -1,0 +1,773 @@
+"""KIVI INT4 attention implementation for B200 (the plugin-owned mixin).
+
+Same role, method names, state and error behaviour as the reference's
+``AscendKiviInt4AttentionBackendMixin`` (methods/kivi_int4/attention_backend.py
+of vllm_ascend_quantized_kv_cache): the adapter mixes it over the live host
+``AscendAttentionBackendImpl``; it binds the two host byte buffers as the six
+KIVI views, keeps one residual-window row per live request, writes K/V through
+the window into the int4 history and computes attention.
+
+What runs where:
+* residual windows: bf16 ring buffers on the cache device; slot bookkeeping on
+  the host (``window.WindowPlanner``), applied once per forward;
+* int4 history writes: ``qkv_kivi_pack_key`` / ``qkv_kivi_pack_value``;
+* decode attention: ``qkv_kivi_paged_decode`` reads int4 pages and the bf16
+  window directly (no dense K/V copy);
+* prompt attention over raw K/V: ``qkv_dense_prefill``;
+* attention over history for multi-token rows (cache hits, chunked prefill
+  with history): ``qkv_kivi_paged_decode`` with one row per query token and
+  its causal length.
+The reference refuses chunked prefill with history (RuntimeError at
+attention_backend.py:1062-1069); this implementation serves it with the
+semantics of the reference's generic branch (:1157-1191).
+"""
+
+from __future__ import annotations
+
+from typing import Any
+
+import numpy as np
+import torch
+
+from .byte_cache import kivi_byte_cache_layout, kivi_caches_from_byte_tensors
+from .geometry import validate_kivi_geometry
+from .window import SidePlan, WindowPlanner, is_aligned_key_window, ordered_slots
+
+
+def _attn_state_name(attn_metadata: Any) -> str:
+    state = getattr(attn_metadata, "attn_state", None)
+    if state is None:
+        return "UNKNOWN"
+    return getattr(state, "name", None) or str(state)
+
+
+def _host_list(x) -> list[int]:
+    if isinstance(x, torch.Tensor):
+        return [int(v) for v in x.tolist()]
+    return [int(v) for v in x]
+
+
+class AscendKiviInt4AttentionBackendMixin:
+    """KIVI INT4 (int4 history + bf16 residual window) attention path."""
+
+    #: dtype of the residual ring buffers (the model's K/V dtype); the decode
+    #: kernel reads bf16 windows.
+    kivi_residual_dtype = torch.bfloat16
+
+    # ------------------------------------------------------------------
+    # state, geometry, cache binding
+    # ------------------------------------------------------------------
+
+    def _init_kivi_state(self, kv_cache_dtype: str | None, vllm_config: Any = None) -> None:
+        """All KIVI state; knobs from ``cache_config.kivi_group_size`` /
+        ``kivi_residual_length`` (default 128/128), residual rows from
+        ``scheduler_config.max_num_seqs`` (attention_backend.py:50-92)."""
+        self.enable_kivi = kv_cache_dtype in ("kivi_int4", "kivi")
+        cache_config = getattr(vllm_config, "cache_config", None)
+        group_size = getattr(cache_config, "kivi_group_size", 128)
+        residual_length = getattr(cache_config, "kivi_residual_length", 128)
+        self.kivi_group_size = group_size if isinstance(group_size, int) else 128
+        self.kivi_residual_length = residual_length if isinstance(residual_length, int) else 128
+        if self.enable_kivi:
+            self._validate_kivi_geometry()
+        self.kivi_bits = 4
+        self.k_quant_cache = self.k_scale_cache = self.k_mn_cache = None
+        self.v_quant_cache = self.v_scale_cache = self.v_mn_cache = None
+        self.kivi_residual_key_cache: torch.Tensor | None = None
+        self.kivi_residual_value_cache: torch.Tensor | None = None
+        scheduler_config = getattr(vllm_config, "scheduler_config", None)
+        max_num_seqs = getattr(scheduler_config, "max_num_seqs", 128)
+        self.kivi_max_num_seqs = max_num_seqs if isinstance(max_num_seqs, int) and max_num_seqs > 0 else 128
+        self.kivi_residual_req_to_row: dict[str, int] = {}
+        self.kivi_residual_row_to_req: list[str | None] = []
+        self.kivi_residual_free_rows: list[int] = []
+        self._kivi_planner: WindowPlanner | None = None
+        self._kivi_plan: tuple[SidePlan, SidePlan] | None = None
+
+    def _validate_kivi_geometry(self) -> None:
+        validate_kivi_geometry(
+            head_size=self.head_size, group_size=self.kivi_group_size, residual_length=self.kivi_residual_length
+        )
+
+    def _check_kivi_cache_bound(self) -> None:
+        if any(
+            t is None
+            for t in (
+                self.k_quant_cache, self.k_scale_cache, self.k_mn_cache,
+                self.v_quant_cache, self.v_scale_cache, self.v_mn_cache,
+            )
+        ):
+            raise RuntimeError("KIVI cache tensors are not bound.")
+
+    def _get_kivi_block_size(self) -> int:
+        self._check_kivi_cache_bound()
+        return self.k_quant_cache.shape[-1] * 8
+
+    def _kivi_views(self) -> tuple[torch.Tensor, ...]:
+        return (
+            self.k_quant_cache, self.k_scale_cache, self.k_mn_cache,
+            self.v_quant_cache, self.v_scale_cache, self.v_mn_cache,
+        )
+
+    def _bind_kivi_cache(self, kv_cache: Any) -> None:
+        """Binds the paged cache: the host's 2 byte buffers become the six
+        views (no copy); a 6-tuple is taken as is (attention_backend.py:135-175)."""
+        if kv_cache is None:
+            return
+        if not isinstance(kv_cache, list | tuple):
+            raise RuntimeError(
+                "KIVI INT4 kv_cache must be a 2-tuple of byte buffers or a "
+                f"6-tuple, got {type(kv_cache)}."
+            )
+        if len(kv_cache) == 0:
+            return
+        if len(kv_cache) == 2:
+            kv_cache = kivi_caches_from_byte_tensors(
+                *kv_cache,
+                layout=kivi_byte_cache_layout(
+                    kv_cache[0], kv_cache[1],
+                    num_kv_heads=self.num_kv_heads, head_size=self.head_size, group_size=self.kivi_group_size,
+                ),
+            )
+        if len(kv_cache) != 6:
+            raise RuntimeError(
+                "KIVI INT4 kv_cache must be a 2-tuple of byte buffers or a "
+                "6-tuple: (k_quant, k_scale, k_mn, v_quant, v_scale, v_mn)."
+            )
+        (
+            self.k_quant_cache, self.k_scale_cache, self.k_mn_cache,
+            self.v_quant_cache, self.v_scale_cache, self.v_mn_cache,
+        ) = kv_cache
+        self._ensure_kivi_residual_buffers()
+
+    # ------------------------------------------------------------------
+    # residual rows: one per live request (max_num_seqs rows)
+    # ------------------------------------------------------------------
+
+    def _ensure_kivi_residual_buffers(self) -> None:
+        if self.kivi_residual_key_cache is not None:
+            return
+        self._check_kivi_cache_bound()
+        rows, cap = self.kivi_max_num_seqs, self.kivi_residual_length
+        device = self.k_quant_cache.device
+        shape = (rows, cap, self.num_kv_heads, self.head_size)
+        self.kivi_residual_key_cache = torch.zeros(shape, dtype=self.kivi_residual_dtype, device=device)
+        self.kivi_residual_value_cache = torch.zeros(shape, dtype=self.kivi_residual_dtype, device=device)
+        self._kivi_planner = WindowPlanner(rows, cap, self.kivi_group_size)
+        self.kivi_residual_req_to_row = {}
+        self.kivi_residual_row_to_req = [None] * rows
+        self.kivi_residual_free_rows = list(range(rows - 1, -1, -1))
+
+    # host views of the per-row FIFO state (same names as the reference)
+    @property
+    def kivi_residual_key_start(self) -> list[int]:
+        self._ensure_kivi_residual_buffers()
+        return self._kivi_planner.key.start
+
+    @property
+    def kivi_residual_key_len(self) -> list[int]:
+        self._ensure_kivi_residual_buffers()
+        return self._kivi_planner.key.length
+
+    @property
+    def kivi_residual_value_start(self) -> list[int]:
+        self._ensure_kivi_residual_buffers()
+        return self._kivi_planner.value.start
+
+    @property
+    def kivi_residual_value_len(self) -> list[int]:
+        self._ensure_kivi_residual_buffers()
+        return self._kivi_planner.value.length
+
+    @property
+    def kivi_residual_key_slot_ids(self) -> torch.Tensor:
+        self._ensure_kivi_residual_buffers()
+        return torch.from_numpy(self._kivi_planner.key.slots)
+
+    @property
+    def kivi_residual_value_slot_ids(self) -> torch.Tensor:
+        self._ensure_kivi_residual_buffers()
+        return torch.from_numpy(self._kivi_planner.value.slots)
+
+    def _get_kivi_req_keys(self, req_ids: list[str] | None, num_reqs: int) -> list[str]:
+        if req_ids is not None and len(req_ids) >= num_reqs:
+            return [str(r) for r in req_ids[:num_reqs]]
+        return [f"__kivi_batch_row_{i}" for i in range(num_reqs)]
+
+    def _get_kivi_residual_row(self, req_key: str, *, create: bool) -> int | None:
+        self._ensure_kivi_residual_buffers()
+        row = self.kivi_residual_req_to_row.get(req_key)
+        if row is not None or not create:
+            return row
+        if not self.kivi_residual_free_rows:
+            raise RuntimeError(
+                "KIVI residual rows are exhausted. "
+                f"max_num_seqs={self.kivi_max_num_seqs}, req_id={req_key}."
+            )
+        row = self.kivi_residual_free_rows.pop()
+        self.kivi_residual_req_to_row[req_key] = row
+        self.kivi_residual_row_to_req[row] = req_key
+        return row
+
+    def _release_kivi_residual_row(self, req_key: str) -> None:
+        row = self.kivi_residual_req_to_row.pop(req_key, None)
+        if row is None:
+            return
+        self.kivi_residual_row_to_req[row] = None
+        self._kivi_planner.key.reset(row)
+        self._kivi_planner.value.reset(row)
+        self.kivi_residual_free_rows.append(row)
+
+    def _release_finished_kivi_residual_rows(self, finished_req_keys: set[str]) -> None:
+        for req_key in finished_req_keys:
+            self._release_kivi_residual_row(req_key)
+
+    def _get_kivi_residual_lanes(self, row_idx: int, *, is_key: bool) -> list[int]:
+        self._ensure_kivi_residual_buffers()
+        return self._kivi_planner.side(is_key).lanes(row_idx)
+
+    def _collect_kivi_residual_window(
+        self, req_key: str, *, is_key: bool, target_dtype: Any | None = None, target_device: Any | None = None
+    ) -> tuple[list[int], torch.Tensor | None]:
+        """(slots in FIFO order, window tensors ``[n, KVH, D]``) of a request."""
+        row = self._get_kivi_residual_row(req_key, create=False)
+        if row is None:
+            return [], None
+        slots, lanes = self._kivi_planner.window(row, is_key=is_key)
+        if not lanes:
+            return [], None
+        cache = self.kivi_residual_key_cache if is_key else self.kivi_residual_value_cache
+        idx = torch.tensor(lanes, dtype=torch.long, device=cache.device)
+        tensors = cache[row].index_select(0, idx)
+        if target_dtype is not None or target_device is not None:
+            tensors = tensors.to(
+                device=target_device or tensors.device, dtype=target_dtype or tensors.dtype
+            )
+        return slots, tensors
+
+    def _has_kivi_residual_entry(self, slot: int, *, req_key: str, is_key: bool) -> bool:
+        row = self._get_kivi_residual_row(req_key, create=False)
+        if row is None:
+            return False
+        return bool((self._kivi_planner.side(is_key).slots[row] == int(slot)).any())
+
+    # ------------------------------------------------------------------
+    # planned window updates
+    # ------------------------------------------------------------------
+
+    def _kivi_begin_plan(self) -> None:
+        self._ensure_kivi_residual_buffers()
+        self._kivi_plan = self._kivi_planner.begin()
+        self._kivi_plan_src: list[torch.Tensor | None] = [None, None]  # new K, new V
+
+    def _kivi_key_flush_gate(self, slots: list[int]) -> None:
+        block_size = self._get_kivi_block_size()
+        if not is_aligned_key_window(slots, self.kivi_group_size, block_size):
+            raise RuntimeError("KIVI key flush requires contiguous aligned token groups.")
+
+    def _kivi_plan_store(self, values: torch.Tensor, slots: list[int], token_index: list[int],
+                         *, req_key: str, is_key: bool) -> None:
+        row = self._get_kivi_residual_row(req_key, create=True)
+        plan = self._kivi_plan[0 if is_key else 1]
+        self._kivi_planner.store(
+            plan, row, slots, token_index, is_key=is_key,
+            on_flush=self._kivi_key_flush_gate if is_key else None,
+        )
+
+    def _kivi_gather_sources(self, sources: list, ring: torch.Tensor, src: torch.Tensor | None) -> torch.Tensor:
+        flat = ring.view(-1, *ring.shape[2:])
+        ring_pos = [i for i, s in enumerate(sources) if s[0] == "ring"]
+        new_pos = [i for i, s in enumerate(sources) if s[0] == "new"]
+        dev = ring.device
+
+        def idx(vals):
+            return torch.tensor(vals, dtype=torch.long).to(dev, non_blocking=True)
+
+        if not new_pos:
+            return flat.index_select(0, idx([sources[i][1] for i in ring_pos]))
+        if not ring_pos:
+            return src.index_select(0, idx([sources[i][1] for i in new_pos]))
+        out = torch.empty((len(sources), *ring.shape[2:]), dtype=ring.dtype, device=dev)
+        out[idx(ring_pos)] = flat.index_select(0, idx([sources[i][1] for i in ring_pos]))
+        out[idx(new_pos)] = src.index_select(0, idx([sources[i][1] for i in new_pos]))
+        return out
+
+    def _kivi_execute_plan(self) -> None:
+        """Applies the open plan: pack every flushed token (one launch per
+        side), then land the new tokens and compactions in the ring."""
+        if self._kivi_plan is None:
+            return
+        plans, srcs = self._kivi_plan, self._kivi_plan_src
+        self._kivi_plan = None
+        for is_key, plan, src in ((True, plans[0], srcs[0]), (False, plans[1], srcs[1])):
+            ring = self.kivi_residual_key_cache if is_key else self.kivi_residual_value_cache
+            if plan.flush_src:
+                sources, slots = self._kivi_dedupe_flush(plan.flush_src, plan.flush_slots, is_key)
+                data = self._kivi_gather_sources(sources, ring, src)
+                slot_t = torch.tensor(slots, dtype=torch.long).to(ring.device, non_blocking=True)
+                if is_key:
+                    self._write_kivi_key_quant_cache(data, slot_t, _host_slots=slots)
+                else:
+                    self._write_kivi_value_quant_cache(data, slot_t)
+            if plan.ring_writes:
+                lanes = sorted(plan.ring_writes)
+                data = self._kivi_gather_sources([plan.ring_writes[l] for l in lanes], ring, src)
+                lanes_t = torch.tensor(lanes, dtype=torch.long).to(ring.device, non_blocking=True)
+                ring.view(-1, *ring.shape[2:]).index_copy_(0, lanes_t, data)
+
+    def _kivi_dedupe_flush(self, sources: list, slots: list[int], is_key: bool):
+        """Keeps the last flush of a slot (keys: of a whole group): a batched
+        launch has no write order, the reference's sequential flushes do."""
+        if is_key:
+            g = self.kivi_group_size
+            seen: set[int] = set()
+            keep: list[int] = []
+            for gi in range(len(slots) // g - 1, -1, -1):
+                first = slots[gi * g]
+                if first not in seen:
+                    seen.add(first)
+                    keep.append(gi)
+            keep.reverse()
+            idx = [gi * g + j for gi in keep for j in range(g)]
+        else:
+            last: dict[int, int] = {}
+            for i, s in enumerate(slots):
+                last[s] = i
+            idx = sorted(last.values())
+        if len(idx) == len(slots):
+            return sources, slots
+        return [sources[i] for i in idx], [slots[i] for i in idx]
+
+    def _kivi_set_plan_source(self, key: torch.Tensor, value: torch.Tensor) -> None:
+        dt = self.kivi_residual_dtype
+        dev = self.kivi_residual_key_cache.device
+        self._kivi_plan_src = [
+            key.detach().to(device=dev, dtype=dt).contiguous(),
+            value.detach().to(device=dev, dtype=dt).contiguous(),
+        ]
+
+    def _store_kivi_residual_entries(self, values: torch.Tensor, slots: torch.Tensor, *, req_key: str,
+                                     is_key: bool) -> None:
+        """Appends tokens to a request's window, flushing per the asymmetric
+        policy (attention_backend.py:411-462); executes immediately."""
+        if values.numel() == 0 or slots.numel() == 0:
+            return
+        self._kivi_begin_plan()
+        src = values.detach().to(device=self.kivi_residual_key_cache.device, dtype=self.kivi_residual_dtype)
+        self._kivi_plan_src[0 if is_key else 1] = src.contiguous()
+        sl = _host_list(slots)
+        self._kivi_plan_store(src, sl, list(range(len(sl))), req_key=req_key, is_key=is_key)
+        self._kivi_execute_plan()
+
+    def _write_kivi_cache(self, key: Any, value: Any, slot_mapping: Any, req_ids: list[str] | None,
+                          actual_seq_qlen: Any) -> None:
+        """Incremental write of every request's new tokens through its window
+        (attention_backend.py:562-606), planned once for the whole batch."""
+        if key is None or value is None or slot_mapping is None:
+            return
+        qlen = _host_list(actual_seq_qlen)
+        if not qlen:
+            return
+        slots_all = _host_list(slot_mapping)
+        keys = self._get_kivi_req_keys(req_ids, len(qlen))
+        self._kivi_begin_plan()
+        self._kivi_set_plan_source(key, value)
+        n = len(slots_all)
+        prev = 0
+        for r, q_end in enumerate(qlen):
+            q_end = min(int(q_end), n)
+            if prev >= n:
+                break
+            if q_end <= prev:
+                prev = q_end
+                continue
+            idx = [i for i in range(prev, q_end) if slots_all[i] >= 0]
+            if idx:
+                sl = [slots_all[i] for i in idx]
+                self._kivi_plan_store(None, sl, idx, req_key=keys[r], is_key=True)
+                self._kivi_plan_store(None, sl, idx, req_key=keys[r], is_key=False)
+            prev = q_end
+        self._kivi_execute_plan()
+
+    def _write_kivi_prefill_cache(self, key: Any, value: Any, slot_mapping: Any, req_ids: list[str] | None,
+                                  actual_seq_qlen: Any) -> None:
+        """Bulk prompt write (attention_backend.py:608-674): the first
+        floor(n / r) * r tokens go straight to the int4 history, the rest to
+        the window."""
+        if key is None or value is None or slot_mapping is None:
+            return
+        qlen = _host_list(actual_seq_qlen)
+        if not qlen:
+            return
+        slots_all = _host_list(slot_mapping)
+        keys = self._get_kivi_req_keys(req_ids, len(qlen))
+        r_len = self.kivi_residual_length
+        self._kivi_begin_plan()
+        self._kivi_set_plan_source(key, value)
+        kplan, vplan = self._kivi_plan
+        n = len(slots_all)
+        prev = 0
+        for r, q_end in enumerate(qlen):
+            q_end = min(int(q_end), n)
+            if prev >= n:
+                break
+            if q_end <= prev:
+                prev = q_end
+                continue
+            idx = [i for i in range(prev, q_end) if slots_all[i] >= 0]
+            if not idx:
+                prev = q_end
+                continue
+            sl = [slots_all[i] for i in idx]
+            flush = (len(idx) // r_len) * r_len
+            if flush:
+                self._kivi_key_flush_gate(sl[:flush])
+                self._kivi_planner.flush_direct(kplan, sl[:flush], idx[:flush])
+                self._kivi_planner.flush_direct(vplan, sl[:flush], idx[:flush])
+            if flush < len(idx):
+                self._kivi_plan_store(None, sl[flush:], idx[flush:], req_key=keys[r], is_key=True)
+                self._kivi_plan_store(None, sl[flush:], idx[flush:], req_key=keys[r], is_key=False)
+            prev = q_end
+        self._kivi_execute_plan()
+
+    def _write_kivi_key_quant_cache(self, key: Any, slot_mapping: Any, _host_slots: list[int] | None = None) -> None:
+        """Whole-group key flush into the int4 history with every layout check
+        before the launch (attention_backend.py:676-726)."""
+        self._check_kivi_cache_bound()
+        if key is None or slot_mapping is None:
+            return
+        host_slots = _host_slots if _host_slots is not None else _host_list(slot_mapping)
+        keep = [i for i, s in enumerate(host_slots) if s >= 0]
+        if not keep:
+            return
+        if len(keep) != len(host_slots):
+            sel = torch.tensor(keep, dtype=torch.long, device=key.device)
+            key = key.index_select(0, sel)
+            slot_mapping = slot_mapping.index_select(0, sel.to(slot_mapping.device))
+            host_slots = [host_slots[i] for i in keep]
+        key = key.contiguous()
+        slots = slot_mapping.to(torch.long).contiguous()
+        if key.shape[-1] != self.head_size:
+            raise RuntimeError(
+                f"KIVI INT4 key head_size must match attention head_size ({self.head_size}), got {key.shape[-1]}."
+            )
+        if key.shape[0] % self.kivi_group_size != 0:
+            raise RuntimeError(
+                "KIVI key flush must contain whole token groups, got "
+                f"{key.shape[0]} tokens for group_size={self.kivi_group_size}."
+            )
+        if self.head_size % 8 != 0:
+            raise RuntimeError(
+                f"KIVI INT4 int32 packing requires head_size ({self.head_size}) to be divisible by 8."
+            )
+        if self.kivi_group_size % 8 != 0:
+            raise RuntimeError(
+                f"KIVI INT4 key packing requires kivi_group_size ({self.kivi_group_size}) to be divisible by 8."
+            )
+        block_size = self._get_kivi_block_size()
+        if block_size % self.kivi_group_size != 0:
+            raise RuntimeError(
+                f"KIVI INT4 key cache requires block_size ({block_size}) to be "
+                f"divisible by kivi_group_size ({self.kivi_group_size})."
+            )
+        if not is_aligned_key_window(host_slots, self.kivi_group_size, block_size):
+            raise RuntimeError("KIVI key flush requires contiguous aligned token groups.")
+        self._launch_kivi_key_pack(key, slots)
+
+    def _launch_kivi_key_pack(self, key: Any, slots: Any) -> None:
+        """Kernel launch seam (tests may replace it)."""
+        from ...ops.kivi_pack import kivi_pack_key_cache
+
+        kivi_pack_key_cache(
+            key, slots, self.k_quant_cache, self.k_scale_cache, self.k_mn_cache, self.kivi_group_size,
+            validate_slots=False,
+        )
+
+    def _write_kivi_value_quant_cache(self, value: Any, slot_mapping: Any) -> None:
+        """Value pack with the reference's checks (attention_backend.py:741-777)."""
+        self._check_kivi_cache_bound()
+        if value is None or slot_mapping is None:
+            return
+        head_size = value.shape[-1]
+        if head_size != self.head_size:
+            raise RuntimeError(
+                f"KIVI INT4 value head_size must match attention head_size ({self.head_size}), got {head_size}."
+            )
+        if head_size % self.kivi_group_size != 0:
+            raise RuntimeError(
+                f"KIVI INT4 value head_size ({head_size}) must be divisible by "
+                f"kivi_group_size ({self.kivi_group_size})."
+            )
+        if head_size % 8 != 0:
+            raise RuntimeError(f"KIVI INT4 int32 packing requires head_size ({head_size}) to be divisible by 8.")
+        if self.kivi_group_size % 8 != 0:
+            raise RuntimeError(
+                f"KIVI INT4 value packing requires kivi_group_size ({self.kivi_group_size}) to be divisible by 8."
+            )
+        # negative slots are skipped by the kernel itself
+        self._launch_kivi_value_pack(value.contiguous(), slot_mapping.to(torch.long).contiguous())
+
+    def _launch_kivi_value_pack(self, value: Any, slots: Any) -> None:
+        """Kernel launch seam (tests may replace it)."""
+        from ...ops.kivi_pack import kivi_pack_value_cache
+
+        kivi_pack_value_cache(
+            value, slots, self.v_quant_cache, self.v_scale_cache, self.v_mn_cache, self.kivi_group_size
+        )
+
+    # ------------------------------------------------------------------
+    # window sync
+    # ------------------------------------------------------------------
+
+    def _sync_kivi_residual_windows(self, block_table: Any, seq_lens: list[int], req_ids: list[str] | None,
+                                    finished_req_ids: set[str] | None = None) -> None:
+        """Releases finished rows and drops window slots a request no longer
+        owns (attention_backend.py:813-836). The common case — both windows
+        hold exactly the last positions — is checked in O(window); only a
+        mismatch expands the request's full slot list."""
+        if finished_req_ids:
+            self._release_finished_kivi_residual_rows({str(r) for r in finished_req_ids})
+        keys = self._get_kivi_req_keys(req_ids, len(seq_lens))
+        rows = [(i, self.kivi_residual_req_to_row.get(k)) for i, k in enumerate(keys)]
+        rows = [(i, r) for i, r in rows if r is not None]
+        if not rows:
+            return
+        bt = block_table
+        if isinstance(bt, torch.Tensor):
+            bt = (bt.cpu() if bt.is_cuda else bt).numpy()
+        bt = np.asarray(bt)
+        block_size = self._get_kivi_block_size()
+        planner = self._kivi_planner
+        stale = [(i, r) for i, r in rows if not planner.expected_live(r, int(seq_lens[i]), bt[i], block_size)]
+        if not stale:
+            return
+        own_plan = self._kivi_plan is None
+        if own_plan:
+            self._kivi_begin_plan()
+        for i, r in stale:
+            live = set(ordered_slots(bt[i:i + 1], [int(seq_lens[i])], block_size)[0])
+            planner.prune(self._kivi_plan[0], r, live, is_key=True)
+            planner.prune(self._kivi_plan[1], r, live, is_key=False)
+        if own_plan:
+            self._kivi_execute_plan()
+
+    # ------------------------------------------------------------------
+    # attention
+    # ------------------------------------------------------------------
+
+    def _is_kivi_chunked_prefill_all_new(self, attn_metadata: Any) -> bool:
+        qlen = attn_metadata.actual_seq_lengths_q
+        nd = attn_metadata.num_decodes
+        for i in range(nd, len(attn_metadata.seq_lens_list)):
+            q_start = qlen[i - 1] if i > 0 else 0
+            if attn_metadata.seq_lens_list[i] > qlen[i] - q_start:
+                return False
+        return True
+
+    def forward(self, layer: Any, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, kv_cache: Any,
+                attn_metadata: Any, output: torch.Tensor | None = None, output_scale: torch.Tensor | None = None,
+                output_block_scale: torch.Tensor | None = None) -> torch.Tensor:
+        """INT4 forward entry (attention_backend.py:972-1004); bypasses the
+        host's reshape_and_cache."""
+        assert output is not None, "Output tensor must be provided."
+        if not getattr(self, "enable_kivi", False):
+            raise RuntimeError(
+                "the KIVI INT4 attention impl was instantiated without the "
+                "kivi_int4 cache dtype; check the host get_impl_cls dispatch"
+            )
+        if output_scale is not None or output_block_scale is not None:
+            raise NotImplementedError(
+                "fused output quantization is not yet supported for AscendKiviInt4AttentionBackendImpl"
+            )
+        if attn_metadata is None:
+            return output.fill_(0)
+        return self._forward_kivi_attention(query, key, value, attn_metadata, output, kv_cache)
+
+    def _forward_kivi_attention(self, query, key, value, attn_metadata, output, kv_cache=None):
+        """Dispatch by attention state (attention_backend.py:1006-1191)."""
+        self._bind_kivi_cache(kv_cache)
+        finished = getattr(attn_metadata, "finished_req_ids", None)
+        if finished:
+            self._release_finished_kivi_residual_rows({str(r) for r in finished})
+        state = _attn_state_name(attn_metadata)
+        seq_lens = _host_list(attn_metadata.seq_lens_list)
+        req_ids = getattr(attn_metadata, "req_ids", None)
+        if state == "DecodeOnly":
+            qlen = list(range(1, len(seq_lens) + 1))
+        else:
+            qlen = _host_list(attn_metadata.actual_seq_lengths_q)
+        num_tokens = int(qlen[-1])
+        query = query[:num_tokens]
+
+        if state == "PrefillNoCache":
+            if key is None or value is None:
+                raise RuntimeError("KIVI PrefillNoCache requires dense key/value.")
+            n = min(getattr(attn_metadata, "num_actual_tokens", key.shape[0]), key.shape[0])
+            self._write_kivi_prefill_cache(key[:n], value[:n], attn_metadata.slot_mapping[:n], req_ids, qlen)
+            return self._forward_kivi_prefill_fia(query, key, value, attn_metadata, output)
+
+        history = state == "ChunkedPrefill" and not self._is_kivi_chunked_prefill_all_new(attn_metadata)
+
+        if state == "DecodeOnly":
+            if key is not None and value is not None:
+                n = min(getattr(attn_metadata, "num_actual_tokens", key.shape[0]), key.shape[0])
+                if n > 0:
+                    self._write_kivi_cache(key[:n], value[:n], attn_metadata.slot_mapping[:n], req_ids,
+                                           list(range(1, len(seq_lens) + 1)))
+            self._sync_kivi_residual_windows(attn_metadata.block_tables, seq_lens, req_ids, finished)
+            return self._forward_kivi_paged_decode_attention(query, attn_metadata.block_tables, seq_lens,
+                                                             req_ids, output)
+
+        if state == "ChunkedPrefill" and not history:
+            if key is not None and value is not None:
+                n = min(getattr(attn_metadata, "num_actual_tokens", key.shape[0]), key.shape[0])
+                if n > 0:
+                    nd_tok = min(attn_metadata.num_decode_tokens, n)
+                    nd = attn_metadata.num_decodes
+                    slot_mapping = attn_metadata.slot_mapping[:n]
+                    if nd_tok > 0:
+                        self._write_kivi_cache(key[:nd_tok], value[:nd_tok], slot_mapping[:nd_tok],
+                                               None if req_ids is None else req_ids[:nd],
+                                               list(range(1, nd + 1)))
+                    if nd_tok < n:
+                        pre_q = [int(qlen[i]) - nd_tok for i in range(nd, len(qlen))]
+                        self._write_kivi_prefill_cache(key[nd_tok:n], value[nd_tok:n], slot_mapping[nd_tok:n],
+                                                       None if req_ids is None else req_ids[nd:], pre_q)
+            self._sync_kivi_residual_windows(attn_metadata.block_tables, seq_lens, req_ids, finished)
+            return self._forward_kivi_chunked_prefill(query, key, value, attn_metadata, output)
+
+        # every other state (and chunked prefill with history): incremental
+        # write of all rows, sync, attention over history + window
+        if key is not None and value is not None:
+            n = min(getattr(attn_metadata, "num_actual_tokens", key.shape[0]), key.shape[0])
+            if n > 0:
+                self._write_kivi_cache(key[:n], value[:n], attn_metadata.slot_mapping[:n], req_ids, qlen)
+        self._sync_kivi_residual_windows(attn_metadata.block_tables, seq_lens, req_ids, finished)
+        causal = bool(getattr(attn_metadata, "causal", True))
+        return self._forward_kivi_history_attention(query, attn_metadata.block_tables, seq_lens, qlen, req_ids,
+                                                    causal, output)
+
+    # -- kernel calls ---------------------------------------------------
+
+    def _kivi_res_state(self, req_keys: list[str], ends: list[int]) -> np.ndarray:
+        st = np.zeros((len(req_keys), 6), dtype=np.int32)
+        st[:, 0] = -1
+        planner = self._kivi_planner
+        for i, k in enumerate(req_keys):
+            row = self.kivi_residual_req_to_row.get(k)
+            st[i, 5] = ends[i]
+            if row is None:
+                continue
+            st[i, 0] = row
+            st[i, 1] = planner.key.start[row]
+            st[i, 2] = planner.key.length[row]
+            st[i, 3] = planner.value.start[row]
+            st[i, 4] = planner.value.length[row]
+        return st
+
+    def _kivi_device_i32(self, arr) -> torch.Tensor:
+        t = torch.from_numpy(np.ascontiguousarray(arr, dtype=np.int32))
+        return t.to(self.k_quant_cache.device, non_blocking=True)
+
+    def _kivi_table(self, block_table: Any, rows: int) -> torch.Tensor:
+        dev = self.k_quant_cache.device
+        if isinstance(block_table, torch.Tensor):
+            bt = block_table[:rows]
+            if bt.device != dev:
+                bt = bt.to(dev, non_blocking=True)
+            return bt.to(torch.int32).contiguous()
+        return self._kivi_device_i32(np.asarray(block_table)[:rows])
+
+    def _forward_kivi_paged_decode_attention(self, query, block_table, seq_lens, req_ids, output):
+        """One query token per request over int4 pages + window
+        (replaces attention_backend.py:1193-1230)."""
+        from ...ops.kivi_decode import kivi_paged_decode
+
+        B = len(seq_lens)
+        if B == 0:
+            return output
+        self._ensure_kivi_residual_buffers()
+        keys = self._get_kivi_req_keys(req_ids, B)
+        res_state = self._kivi_device_i32(self._kivi_res_state(keys, list(seq_lens)))
+        sl = self._kivi_device_i32(seq_lens)
+        bt = self._kivi_table(block_table, B)
+        kivi_paged_decode(
+            query[:B], self._kivi_views(), self.kivi_residual_key_cache, self.kivi_residual_value_cache,
+            bt, sl, res_state, self.kivi_group_size, self.scale, output[:B], max(seq_lens),
+        )
+        return output
+
+    def _forward_kivi_history_attention(self, query, block_table, seq_lens, qlen, req_ids, causal, output):
+        """Multi-token rows over history + window: each query token becomes a
+        decode row with its causal length (the reference's generic branch,
+        attention_backend.py:1176-1191)."""
+        from ...ops.kivi_decode import kivi_paged_decode
+
+        B = len(seq_lens)
+        keys = self._get_kivi_req_keys(req_ids, B)
+        rows_req, rows_len = [], []
+        prev = 0
+        for b in range(B):
+            q_end = int(qlen[b])
+            ql = q_end - prev
+            L = int(seq_lens[b])
+            for i in range(ql):
+                rows_req.append(b)
+                rows_len.append(max(0, min(L, L - ql + i + 1)) if causal else L)
+            prev = q_end
+        R = len(rows_req)
+        if R == 0:
+            return output
+        st = self._kivi_res_state(keys, [int(s) for s in seq_lens])[rows_req]
+        bt_full = self._kivi_table(block_table, B)
+        sel = torch.tensor(rows_req, dtype=torch.long).to(bt_full.device, non_blocking=True)
+        bt = bt_full.index_select(0, sel).contiguous()
+        kivi_paged_decode(
+            query[:R], self._kivi_views(), self.kivi_residual_key_cache, self.kivi_residual_value_cache,
+            bt, self._kivi_device_i32(rows_len), self._kivi_device_i32(st), self.kivi_group_size, self.scale,
+            output[:R], max(max(rows_len), 1),
+        )
+        return output
+
+    def _forward_kivi_prefill_fia(self, query, key, value, attn_metadata, output):
+        """Causal prompt attention over the raw prompt K/V
+        (replaces attention_backend.py:1232-1266)."""
+        from ...ops.prefill import dense_prefill
+
+        qlen = _host_list(attn_metadata.actual_seq_lengths_q)
+        n = int(qlen[-1])
+        lens = [qlen[0]] + [qlen[i] - qlen[i - 1] for i in range(1, len(qlen))]
+        dense_prefill(query[:n].contiguous(), key[:n].contiguous(), value[:n].contiguous(), lens, lens,
+                      self.scale, output[:n], causal=bool(attn_metadata.causal))
+        return output
+
+    def _forward_kivi_chunked_prefill(self, query, key, value, attn_metadata, output):
+        """Decode rows over the paged history, all-new prompt rows over their
+        own raw K/V (replaces attention_backend.py:1268-1339)."""
+        from ...ops.prefill import dense_prefill
+
+        nd_tok = attn_metadata.num_decode_tokens
+        nd = attn_metadata.num_decodes
+        qlen = _host_list(attn_metadata.actual_seq_lengths_q)
+        seq_lens = _host_list(attn_metadata.seq_lens_list)
+        num_tokens = int(qlen[-1])
+        req_ids = getattr(attn_metadata, "req_ids", None)
+        if nd_tok > 0:
+            self._forward_kivi_paged_decode_attention(
+                query[:nd_tok], attn_metadata.block_tables[:nd], seq_lens[:nd],
+                None if req_ids is None else req_ids[:nd], output,
+            )
+        if attn_metadata.num_prefills <= 0:
+            return output
+        if key is None or value is None:
+            raise RuntimeError("KIVI ChunkedPrefill requires dense key/value for all-new prefill prompts.")
+        pre_q = [qlen[i] - nd_tok for i in range(nd, len(qlen))]
+        lens = [pre_q[0]] + [pre_q[i] - pre_q[i - 1] for i in range(1, len(pre_q))]
+        out = output[nd_tok:num_tokens]
+        dense_prefill(query[nd_tok:num_tokens].contiguous(), key[nd_tok:num_tokens].contiguous(),
+                      value[nd_tok:num_tokens].contiguous(), lens, lens, self.scale, out,
+                      causal=bool(attn_metadata.causal))
+        return output
+
+
+__all__ = ["AscendKiviInt4AttentionBackendMixin"]
