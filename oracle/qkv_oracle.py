@@ -103,10 +103,11 @@ def int8_quant_store(key, value, slots, k_inv, v_inv, key_cache, value_cache):
         value_cache[slot // blk, slot % blk] = vq[t]
 
 
-def int8_dequant_gather(key_cache, value_cache, k_aq, v_aq, block_table, seq_lens):
+def int8_dequant_gather(key_cache, value_cache, k_aq, v_aq, block_table, seq_lens, target_bf16: bool = True):
     """``_dequant_int8_paged_kv_to_dense`` (attention_backend.py:370-404):
-    gather live tokens by block table and dequantise ``bf16(code * aq)``.
-    Returns dense K, V ``[sum(seq_lens), H, D]`` float32 (bf16 values)."""
+    gather live tokens by block table and dequantise ``code * aq``, rounded to
+    bf16 as the reference's bf16 tensors are (``target_bf16=False`` keeps the
+    exact fp32 products). Returns dense K, V ``[sum(seq_lens), H, D]``."""
     blk = key_cache.shape[1]
     ks, vs = [], []
     for b, L in enumerate(seq_lens):
@@ -116,7 +117,8 @@ def int8_dequant_gather(key_cache, value_cache, k_aq, v_aq, block_table, seq_len
         vs.append(value_cache[pages, pos % blk].astype(F32))
     k = np.concatenate(ks) if ks else np.zeros((0,) + key_cache.shape[2:], F32)
     v = np.concatenate(vs) if vs else np.zeros((0,) + value_cache.shape[2:], F32)
-    return bf16_round(k * k_aq), bf16_round(v * v_aq)
+    k, v = k * k_aq, v * v_aq
+    return (bf16_round(k), bf16_round(v)) if target_bf16 else (k, v)
 
 
 # ---------------------------------------------------------------------------

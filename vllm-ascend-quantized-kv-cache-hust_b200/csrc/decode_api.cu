@@ -77,8 +77,13 @@ size_t qkv_kivi_paged_decode_workspace(int batch, int num_heads,
   p.gqa = num_heads / num_kv_heads;
   p.blk = block_size;
   p.group = group_size;
-  const SplitPlan plan = plan_for(p, true, max_seq_len);
-  return workspace_bytes(batch, num_heads, head_size, plan.total);
+  // the larger of the two kernels' plans: the call may take either path
+  const SplitPlan fast = plan_for(p, true, max_seq_len);
+  p.group = 8;  // a group the tensor-core kernel does not take
+  const SplitPlan gen = plan_for(p, true, max_seq_len);
+  const size_t a = workspace_bytes(batch, num_heads, head_size, fast.total);
+  const size_t b = workspace_bytes(batch, num_heads, head_size, gen.total);
+  return a > b ? a : b;
 }
 
 int qkv_int8_paged_decode(const void* query, int64_t q_stride,

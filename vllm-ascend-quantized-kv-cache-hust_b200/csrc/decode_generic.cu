@@ -2,16 +2,17 @@
 // split-KV combine kernel.
 //
 // These kernels serve every geometry the reference accepts (head_size <= 256,
-// gqa <= 16, any block/group size). They dequantise each element exactly the
-// way the reference's dequantise-then-attend path does before its attention
-// call, so their output is the reference result up to fp32 summation order:
-//   INT8: k = bf16(code * aq)  (methods/int8_dynamic/attention_backend.py:398-403)
-//   KIVI: k = bf16(code * scale + mn), mul and add rounded separately
-//         (ops/kivi_gather.py:110-136, cast to the query dtype at :150-156);
+// gqa <= 16, any block/group size). They dequantise each element with the
+// reference's fp32 arithmetic of its dequantise-then-attend path:
+//   INT8: k = code * aq  (methods/int8_dynamic/attention_backend.py:398-403)
+//   KIVI: k = code * scale + mn, mul and add rounded separately
+//         (ops/kivi_gather.py:110-136);
 //         residual positions read the bf16 window
 //         (methods/kivi_int4/attention_backend.py:889-935).
 // The production geometries run the tensor-core kernels in decode_mma.cu.
 #include <math_constants.h>
+
+#include <atomic>
 
 #include "decode_common.cuh"
 
@@ -23,15 +24,93 @@ constexpr int kGenChunk = 128;  // positions per softmax step (one per thread)
 constexpr int kGenMaxG = 16;
 #define kNegInf (-CUDART_INF_F)
 
+// Dequantised values in fp32 (the reference's arithmetic before its final
+// cast to the query dtype, which the tensor-core kernels do not apply either).
 __device__ __forceinline__ float int8_dequant(int8_t code, float aq) {
-  return bf16_round(__fmul_rn(static_cast<float>(code), aq));
+  return __fmul_rn(static_cast<float>(code), aq);
 }
 
 __device__ __forceinline__ float kivi_dequant(uint32_t code, float scale,
                                               float mn) {
-  return bf16_round(__fadd_rn(__fmul_rn(static_cast<float>(code), scale), mn));
+  return __fadd_rn(__fmul_rn(static_cast<float>(code), scale), mn);
 }
 
+// Stages rows [c, c + n) of K (IS_K) or V into tile[r][d] (fp32): one warp per
+// row, the row's source (residual window, dense K/V or a page) resolved once;
+// bf16 rows are read with 16-byte loads.
+template <int MODE, bool IS_K>
+__device__ __forceinline__ void stage_rows(float* tile, int ld, const DecodeParams& p, const TailState& ts,
+                                           int b, int h, int64_t kv_base, bool tail, int c, int n,
+                                           int warp, int lane) {
+  const int D = p.head_size;
+  const int64_t kvh = p.kvh;
+  for (int r = warp; r < n; r += kGenThreads / 32) {
+    const int pos = c + r;
+    float* dst = tile + r * ld;
+    const __nv_bfloat16* row16 = nullptr;
+    if constexpr (MODE == kDense) {
+      row16 = (IS_K ? p.dk : p.dv) + ((kv_base + pos) * kvh + h) * D;
+    } else if (MODE == kKiviPages && tail && pos >= (IS_K ? ts.k_begin : ts.v_begin)) {
+      const int start = IS_K ? ts.k_start : ts.v_start;
+      const int begin = IS_K ? ts.k_begin : ts.v_begin;
+      const int laneR = (start + (pos - begin)) % p.res_cap;
+      row16 = (IS_K ? p.rk : p.rv) + ((static_cast<int64_t>(ts.row) * p.res_cap + laneR) * kvh + h) * D;
+    }
+    if (row16 != nullptr) {
+      if ((D & 7) == 0 && (reinterpret_cast<uintptr_t>(row16) & 15u) == 0) {
+        for (int i = lane; i < D / 8; i += 32) {
+          const uint4 raw = reinterpret_cast<const uint4*>(row16)[i];
+          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = __bfloat1622float2(h2[k]);
+            dst[8 * i + 2 * k] = f.x;
+            dst[8 * i + 2 * k + 1] = f.y;
+          }
+        }
+      } else {
+        for (int d = lane; d < D; d += 32) dst[d] = __bfloat162float(row16[d]);
+      }
+      continue;
+    }
+    if constexpr (MODE != kDense) {
+      int64_t page = -1;
+      if (lane == 0) page = page_of(p, b, pos);
+      page = __shfl_sync(0xffffffffu, page, 0);
+      if (page < 0) {
+        for (int d = lane; d < D; d += 32) dst[d] = 0.0f;
+        continue;
+      }
+      const int off = pos % p.blk;
+      if constexpr (MODE == kKiviPages) {
+        if (IS_K) {
+          const int64_t chan0 = (page * kvh + h) * D;
+          for (int d = lane; d < D; d += 32) {
+            const int64_t chan = chan0 + d;
+            const uint32_t w = static_cast<uint32_t>(p.kq[chan * (p.blk >> 3) + (off >> 3)]);
+            const int64_t si = chan * (p.blk / p.group) + off / p.group;
+            dst[d] = kivi_dequant((w >> (4 * (off & 7))) & 0xFu, p.ks[si], p.km[si]);
+          }
+        } else {
+          const int64_t vrow = (page * p.blk + off) * kvh + h;
+          for (int d = lane; d < D; d += 32) {
+            const uint32_t w = static_cast<uint32_t>(p.vq[vrow * (D >> 3) + (d >> 3)]);
+            const int64_t si = vrow * (D / p.group) + d / p.group;
+            dst[d] = kivi_dequant((w >> (4 * (d & 7))) & 0xFu, p.vs[si], p.vm[si]);
+          }
+        }
+      } else {
+        const int8_t* row8 = (IS_K ? p.kc : p.vc) + ((page * p.blk + off) * kvh + h) * D;
+        const __nv_bfloat16* aq = (IS_K ? p.k_aq : p.v_aq) + static_cast<int64_t>(h) * D;
+        for (int d = lane; d < D; d += 32) dst[d] = int8_dequant(row8[d], __bfloat162float(aq[d]));
+      }
+    }
+  }
+}
+
+// One CTA per (split, kv head, query row). Each step stages 128 positions of
+// dequantised K (then V) in shared memory with coalesced loads, a padded row
+// stride keeping the per-position dot products conflict-free.
 template <int MODE>
 __global__ void __launch_bounds__(kGenThreads)
 decode_generic_kernel(const DecodeParams p) {
@@ -39,13 +118,15 @@ decode_generic_kernel(const DecodeParams p) {
   constexpr bool DENSE = MODE == kDense;
   extern __shared__ float smem[];
   const int G = p.gqa, D = p.head_size;
-  float* qs = smem;                    // [G][D]   q * scale * log2(e)
+  const int ld = D + 1;                // padded row stride of the K/V tile
+  float* tile = smem;                  // [kGenChunk][D + 1]
+  float* qs = tile + kGenChunk * ld;   // [G][D]   q * scale * log2(e)
   float* sc = qs + G * D;              // [G][kGenChunk] scores, then probs
   float* st_m = sc + G * kGenChunk;    // [G] running max (log2 units)
   float* st_l = st_m + G;              // [G] running sum
   float* st_a = st_l + G;              // [G] rescale factor of this step
 
-  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int split = blockIdx.x + p.split_base, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   int L;
   int64_t kv_base = 0;  // first dense K/V row of this query's request
@@ -65,9 +146,7 @@ decode_generic_kernel(const DecodeParams p) {
     L = max(p.seq_lens[b], 0);
   }
   const TailState ts = KIVI ? load_tail_state(p, b, L) : TailState{-1, 0, L, 0, L, L};
-  const int lk = ts.k_begin;  // first position whose key is in the window
-  const int lv = ts.v_begin;  // first position whose value is in the window
-  const int body_end = min(lk, lv);
+  const int body_end = min(ts.k_begin, ts.v_begin);
   int t0, t1;
   bool tail = false;
   if (split < p.num_hist_splits) {
@@ -92,64 +171,23 @@ decode_generic_kernel(const DecodeParams p) {
   for (int j = 0; j < kGenMaxG; ++j) acc[j][0] = acc[j][1] = 0.0f;
   __syncthreads();
 
-  const int64_t kvh = p.kvh;
   for (int c = t0; c < t1; c += kGenChunk) {
+    const int n = min(kGenChunk, t1 - c);
+    // ---- stage K rows of positions c .. c+n-1 (thread -> channel)
+    stage_rows<MODE, true>(tile, ld, p, ts, b, h, kv_base, tail, c, n, warp, lane);
+    __syncthreads();
     // ---- scores: one position per thread
-    const int t = c + tid;
     float dots[kGenMaxG];
 #pragma unroll
     for (int j = 0; j < kGenMaxG; ++j) dots[j] = 0.0f;
-    bool valid = t < t1;
+    const bool valid = tid < n;
     if (valid) {
-      if constexpr (DENSE) {
-        const __nv_bfloat16* kr = p.dk + ((kv_base + t) * kvh + h) * D;
-        for (int d = 0; d < D; ++d) {
-          const float kd = __bfloat162float(kr[d]);
+      const float* kr = tile + tid * ld;
+      for (int d = 0; d < D; ++d) {
+        const float kd = kr[d];
 #pragma unroll
-          for (int j = 0; j < kGenMaxG; ++j)
-            if (j < G) dots[j] += qs[j * D + d] * kd;
-        }
-      } else if (KIVI && tail && t >= lk) {
-        const int laneR = (ts.k_start + (t - lk)) % p.res_cap;
-        const __nv_bfloat16* kr =
-            p.rk + ((static_cast<int64_t>(ts.row) * p.res_cap + laneR) * kvh + h) * D;
-        for (int d = 0; d < D; ++d) {
-          const float kd = __bfloat162float(kr[d]);
-#pragma unroll
-          for (int j = 0; j < kGenMaxG; ++j)
-            if (j < G) dots[j] += qs[j * D + d] * kd;
-        }
-      } else {
-        const int64_t page = page_of(p, b, t);
-        if (page < 0) {
-          valid = false;
-        } else {
-          const int off = t % p.blk;
-          if constexpr (KIVI) {
-            const int wpb = p.blk >> 3;      // words per channel per page
-            const int gpb = p.blk / p.group;  // key groups per page
-            const int64_t chan0 = (page * kvh + h) * D;
-            for (int d = 0; d < D; ++d) {
-              const int64_t chan = chan0 + d;
-              const uint32_t w = static_cast<uint32_t>(p.kq[chan * wpb + (off >> 3)]);
-              const uint32_t code = (w >> (4 * (off & 7))) & 0xFu;
-              const int64_t si = chan * gpb + off / p.group;
-              const float kd = kivi_dequant(code, p.ks[si], p.km[si]);
-#pragma unroll
-              for (int j = 0; j < kGenMaxG; ++j)
-                if (j < G) dots[j] += qs[j * D + d] * kd;
-            }
-          } else {
-            const int8_t* kr = p.kc + ((page * p.blk + off) * kvh + h) * D;
-            const __nv_bfloat16* aq = p.k_aq + static_cast<int64_t>(h) * D;
-            for (int d = 0; d < D; ++d) {
-              const float kd = int8_dequant(kr[d], __bfloat162float(aq[d]));
-#pragma unroll
-              for (int j = 0; j < kGenMaxG; ++j)
-                if (j < G) dots[j] += qs[j * D + d] * kd;
-            }
-          }
-        }
+        for (int j = 0; j < kGenMaxG; ++j)
+          if (j < G) dots[j] = fmaf(qs[j * D + d], kd, dots[j]);
       }
     }
 #pragma unroll
@@ -157,7 +195,7 @@ decode_generic_kernel(const DecodeParams p) {
       if (j < G) sc[j * kGenChunk + tid] = valid ? dots[j] : kNegInf;
     __syncthreads();
 
-    // ---- online softmax update, one warp per head
+    // ---- online softmax update, one warp per head; V staged meanwhile
     for (int j = warp; j < G; j += kGenThreads / 32) {
       float v[kGenChunk / 32];
       float mx = kNegInf;
@@ -187,10 +225,10 @@ decode_generic_kernel(const DecodeParams p) {
         st_a[j] = alpha;
       }
     }
+    stage_rows<MODE, false>(tile, ld, p, ts, b, h, kv_base, tail, c, n, warp, lane);
     __syncthreads();
 
     // ---- P @ V: thread owns channels tid and tid + 128
-    const int n = min(kGenChunk, t1 - c);
 #pragma unroll
     for (int dd = 0; dd < 2; ++dd) {
       const int d = tid + dd * kGenThreads;
@@ -199,33 +237,10 @@ decode_generic_kernel(const DecodeParams p) {
       for (int j = 0; j < kGenMaxG; ++j)
         if (j < G) acc[j][dd] *= st_a[j];
       for (int tt = 0; tt < n; ++tt) {
-        const int pos = c + tt;
-        float vd = 0.0f;
-        if constexpr (DENSE) {
-          vd = __bfloat162float(p.dv[((kv_base + pos) * kvh + h) * D + d]);
-        } else if (KIVI && tail && pos >= lv) {
-          const int laneR = (ts.v_start + (pos - lv)) % p.res_cap;
-          vd = __bfloat162float(
-              p.rv[((static_cast<int64_t>(ts.row) * p.res_cap + laneR) * kvh + h) * D + d]);
-        } else {
-          const int64_t page = page_of(p, b, pos);
-          if (page >= 0) {
-            const int off = pos % p.blk;
-            const int64_t row = (page * p.blk + off) * kvh + h;
-            if constexpr (KIVI) {
-              const uint32_t w = static_cast<uint32_t>(p.vq[row * (D >> 3) + (d >> 3)]);
-              const uint32_t code = (w >> (4 * (d & 7))) & 0xFu;
-              const int64_t si = row * (D / p.group) + d / p.group;
-              vd = kivi_dequant(code, p.vs[si], p.vm[si]);
-            } else {
-              vd = int8_dequant(p.vc[row * D + d],
-                                __bfloat162float(p.v_aq[static_cast<int64_t>(h) * D + d]));
-            }
-          }
-        }
+        const float vd = tile[tt * ld + d];
 #pragma unroll
         for (int j = 0; j < kGenMaxG; ++j)
-          if (j < G) acc[j][dd] += sc[j * kGenChunk + tt] * vd;
+          if (j < G) acc[j][dd] = fmaf(sc[j * kGenChunk + tt], vd, acc[j][dd]);
       }
     }
     __syncthreads();
@@ -274,17 +289,47 @@ void launch_combine(const DecodeParams& p, cudaStream_t stream) {
 }
 
 size_t generic_smem_bytes(int gqa, int head_size) {
-  return static_cast<size_t>(gqa * head_size + gqa * kGenChunk + 3 * gqa) *
+  return static_cast<size_t>(kGenChunk * (head_size + 1) + gqa * head_size +
+                             gqa * kGenChunk + 3 * gqa) *
          sizeof(float);
 }
 
-int launch_decode_generic(const DecodeParams& p, int mode,
-                          cudaStream_t stream) {
+// Opts every instantiation into more than 48 KB of dynamic shared memory,
+// once per device.
+int ensure_generic_smem(int mode, size_t bytes) {
+  static std::atomic<uint64_t> done{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << ((3 * dev + mode) & 63);
+  if (done.load() & bit) return QKV_OK;
+  cudaError_t e;
+  const int limit = 160 * 1024;
+  if (mode == kKiviPages)
+    e = cudaFuncSetAttribute(decode_generic_kernel<kKiviPages>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, limit);
+  else if (mode == kInt8Pages)
+    e = cudaFuncSetAttribute(decode_generic_kernel<kInt8Pages>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, limit);
+  else
+    e = cudaFuncSetAttribute(decode_generic_kernel<kDense>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, limit);
+  if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(decode_generic_kernel)");
+  (void)bytes;
+  done.fetch_or(bit);
+  return QKV_OK;
+}
+
+// Runs splits [p.split_base, p.split_base + num_splits) of the plan; the
+// combine kernel runs when `combine` is set and the plan has several splits.
+int launch_decode_generic_splits(const DecodeParams& p, int mode, int num_splits,
+                                 bool combine, cudaStream_t stream) {
   if (p.gqa > kGenMaxG || p.head_size > 2 * kGenThreads)
     return set_error(QKV_ERR_UNSUPPORTED,
                      "paged decode: gqa must be <= 16 and head_size <= 256");
-  dim3 grid(p.splits_total, p.kvh, p.batch);
+  dim3 grid(num_splits, p.kvh, p.batch);
   const size_t smem = generic_smem_bytes(p.gqa, p.head_size);
+  const int rc = ensure_generic_smem(mode, smem);
+  if (rc != QKV_OK) return rc;
   if (mode == kKiviPages)
     decode_generic_kernel<kKiviPages><<<grid, kGenThreads, smem, stream>>>(p);
   else if (mode == kInt8Pages)
@@ -292,11 +337,17 @@ int launch_decode_generic(const DecodeParams& p, int mode,
   else
     decode_generic_kernel<kDense><<<grid, kGenThreads, smem, stream>>>(p);
   QKV_CHECK_LAUNCH("decode_generic_kernel");
-  if (p.splits_total > 1) {
+  if (combine && p.splits_total > 1) {
     launch_combine(p, stream);
     QKV_CHECK_LAUNCH("combine_kernel");
   }
   return QKV_OK;
+}
+
+int launch_decode_generic(const DecodeParams& p, int mode, cudaStream_t stream) {
+  DecodeParams q = p;
+  q.split_base = 0;
+  return launch_decode_generic_splits(q, mode, p.splits_total, true, stream);
 }
 
 }  // namespace qkv

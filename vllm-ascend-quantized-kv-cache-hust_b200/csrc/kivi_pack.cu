@@ -234,6 +234,68 @@ pack_key_kernel(const T* __restrict__ key, const void* __restrict__ slots,
   k_mn[s] = mn;
 }
 
+// Tiled key packer for group_size in {32, 64, 128}: one CTA per
+// (token group, head) stages the group's [g x D] slice in shared memory with
+// 16-byte coalesced loads, then thread d quantises channel d from there.
+template <typename T, int GW>
+__global__ void __launch_bounds__(128)
+pack_key_tiled_kernel(const T* __restrict__ key, const void* __restrict__ slots,
+                      int slot_dtype, int kvh, int head_size, int block_size,
+                      int64_t num_blocks, int32_t* __restrict__ k_quant,
+                      float* __restrict__ k_scale, float* __restrict__ k_mn,
+                      int* err) {
+  constexpr int kGroup = GW * 8;
+  extern __shared__ __align__(16) unsigned char tile_raw[];
+  T* tile = reinterpret_cast<T*>(tile_raw);  // [kGroup][head_size]
+  const int head = blockIdx.y;
+  const int64_t gi = blockIdx.x;
+  const int64_t first_slot = load_index(slots, slot_dtype, gi * kGroup);
+  if (first_slot < 0) return;
+  const int64_t blk = first_slot / block_size;
+  const int off = static_cast<int>(first_slot - blk * block_size);
+  if (blk >= num_blocks || (off % kGroup) != 0 || off + kGroup > block_size) {
+    if (threadIdx.x == 0) record_error(err, kErrSlot);
+    return;
+  }
+  const int64_t row_stride = static_cast<int64_t>(kvh) * head_size;
+  const T* src = key + gi * kGroup * row_stride + static_cast<int64_t>(head) * head_size;
+  constexpr int kVec = 16 / sizeof(T);  // elements per 16-byte load
+  const int vec_per_row = head_size / kVec;
+  for (int i = threadIdx.x; i < kGroup * vec_per_row; i += blockDim.x) {
+    const int r = i / vec_per_row, c = i % vec_per_row;
+    reinterpret_cast<uint4*>(tile + r * head_size)[c] =
+        reinterpret_cast<const uint4*>(src + r * row_stride)[c];
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < head_size; d += blockDim.x) {
+    float mn = to_f32(tile[d]), mx = mn;
+#pragma unroll 8
+    for (int r = 1; r < kGroup; ++r) {
+      const float x = to_f32(tile[r * head_size + d]);
+      mn = fminf(mn, x);
+      mx = fmaxf(mx, x);
+    }
+    const float scale = group_scale(mn, mx);
+    uint32_t words[GW];
+#pragma unroll
+    for (int j = 0; j < GW; ++j) {
+      uint32_t word = 0;
+#pragma unroll
+      for (int l = 0; l < 8; ++l)
+        word |= quantize_code(to_f32(tile[(j * 8 + l) * head_size + d]), mn, scale) << (4 * l);
+      words[j] = word;
+    }
+    const int64_t chan = (blk * kvh + head) * static_cast<int64_t>(head_size) + d;
+    int32_t* dst = k_quant + chan * (block_size >> 3) + (off >> 3);
+#pragma unroll
+    for (int j = 0; j < GW; j += 4)
+      reinterpret_cast<uint4*>(dst)[j / 4] = make_uint4(words[j], words[j + 1], words[j + 2], words[j + 3]);
+    const int64_t s = chan * (block_size / kGroup) + off / kGroup;
+    k_scale[s] = scale;
+    k_mn[s] = mn;
+  }
+}
+
 template <typename T>
 int launch_pack_key(const void* key, const void* slots, int slot_dtype,
                     int64_t num_tokens, int kvh, int head_size, int group_size,
@@ -250,6 +312,26 @@ int launch_pack_key(const void* key, const void* slots, int slot_dtype,
   // whenever the vector path is taken)
   const bool vec = (reinterpret_cast<uintptr_t>(kq) & 15u) == 0 &&
                    ((block_size / 8) % 4) == 0;
+  // the tiled kernel: 16-byte aligned rows and a tile that fits in 48 KB
+  const size_t tile_bytes = static_cast<size_t>(group_size) * head_size * sizeof(T);
+  const bool tiled = vec && (reinterpret_cast<uintptr_t>(key) & 15u) == 0 &&
+                     (head_size * sizeof(T)) % 16 == 0 && tile_bytes <= 48 * 1024 &&
+                     (group_size == 32 || group_size == 64 || group_size == 128);
+  if (tiled) {
+    dim3 tgrid(static_cast<unsigned>(groups), kvh);
+    const int threads = head_size < 128 ? 64 : 128;
+    if (group_size == 128)
+      pack_key_tiled_kernel<T, 16><<<tgrid, threads, tile_bytes, stream>>>(
+          k, slots, slot_dtype, kvh, head_size, block_size, num_blocks, kq, ks, km, err);
+    else if (group_size == 64)
+      pack_key_tiled_kernel<T, 8><<<tgrid, threads, tile_bytes, stream>>>(
+          k, slots, slot_dtype, kvh, head_size, block_size, num_blocks, kq, ks, km, err);
+    else
+      pack_key_tiled_kernel<T, 4><<<tgrid, threads, tile_bytes, stream>>>(
+          k, slots, slot_dtype, kvh, head_size, block_size, num_blocks, kq, ks, km, err);
+    QKV_CHECK_LAUNCH("pack_key_tiled_kernel");
+    return QKV_OK;
+  }
 #define QKV_PACK_KEY_CASE(GW)                                                  \
   case GW:                                                                     \
     pack_key_kernel<T, GW><<<grid, block, 0, stream>>>(                        \
