@@ -51,6 +51,7 @@ UNIT = "tokens/s/layer"
 CONFIG5 = dict(batch=32, context=32768, num_heads=64, num_kv_heads=8, head_size=128, group_size=128,
                residual=128, block_size=128)
 CONFIG2_PACK = dict(tokens=8192, num_kv_heads=8, head_size=128, group_size=128, block_size=128)
+CONFIG3 = dict(batch=64, context=8192, num_heads=32, num_kv_heads=8, head_size=128, block_size=128)
 
 
 def parse():
@@ -59,8 +60,13 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--e2e-steps", type=int, default=30)
+    ap.add_argument("--e2e-steps", type=int, default=30, help="0 skips the end-to-end leg")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-int8", action="store_true", help="skip the config-3 INT8 leg")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the request count (small cases for ncu captures)")
+    ap.add_argument("--only", choices=("kivi", "int8"), default=None,
+                    help="run just one decode kernel loop (for ncu captures)")
     return ap.parse_args()
 
 
@@ -229,6 +235,66 @@ def build_workload(cfg, rank, world, device, seed=1234):
         state=state, seq_lens=torch.full((B,), L, dtype=torch.int32, device=device), hist=hist, res=res,
         B=B, L=L, Hl=Hl, Hql=Hql, D=D, g=g, r=r, blk=blk, nb=nb, pages=pages,
     )
+
+
+def build_int8_workload(cfg, rank, world, device, seed=4321):
+    """Config 3 on this rank's KV heads: 64 requests x 8192 tokens in int8
+    pages (block tables a permutation of the physical blocks), K/V ~ N(0,1)
+    with x16 outliers on 1% of (head, channel) pairs, scales calibrated on the
+    first request's K/V (the first batch a layer sees), then quantised."""
+    import torch
+
+    from qkv_b200.ops import int8_calc_scales, int8_quant_store
+
+    B, L, Hq, H, D, blk = (cfg[k] for k in ("batch", "context", "num_heads", "num_kv_heads", "head_size",
+                                           "block_size"))
+    Hl, Hql = H // world, Hq // world
+    pages = L // blk
+    nb = B * pages
+    gen = torch.Generator(device=device).manual_seed(seed)
+    cpu_gen = torch.Generator().manual_seed(seed)
+    n_out = max(1, int(0.01 * H * D))
+    scale = torch.ones(H * D)
+    scale[torch.randperm(H * D, generator=cpu_gen)[:n_out]] = 16.0
+    scale = scale.view(H, D)[rank * Hl:(rank + 1) * Hl].to(device)
+    bt = torch.randperm(nb, generator=cpu_gen).view(B, pages).to(torch.int32)
+    kc = torch.empty(nb, blk, Hl, D, dtype=torch.int8, device=device)
+    vc = torch.empty_like(kc)
+    pos = torch.arange(L, device=device)
+    k_inv = v_inv = k_aq = v_aq = None
+    for b in range(B):
+        k = (torch.randn(L, Hl, D, generator=gen, device=device) * scale).to(torch.bfloat16)
+        v = (torch.randn(L, Hl, D, generator=gen, device=device) * scale).to(torch.bfloat16)
+        if k_inv is None:
+            k_inv, v_inv, k_aq, v_aq = int8_calc_scales(k, v)
+        slots = bt[b].to(device).long()[pos // blk] * blk + pos % blk
+        int8_quant_store(k, v, slots, k_inv, v_inv, kc, vc)
+    torch.cuda.synchronize(device)
+    q = torch.randn(B, Hql, D, generator=gen, device=device).to(torch.bfloat16)
+    return SimpleNamespace(kc=kc, vc=vc, k_aq=k_aq, v_aq=v_aq, bt_dev=bt.to(device), q=q,
+                           seq_lens=torch.full((B,), L, dtype=torch.int32, device=device),
+                           B=B, L=L, Hl=Hl, Hql=Hql, D=D, blk=blk)
+
+
+def int8_bytes(w) -> int:
+    """int8 K and V of every live token, the bf16 antiquant scales, q, out
+    and the block table."""
+    return w.B * (w.Hl * w.L * w.D * 2 + 2 * w.Hql * w.D * 2 + 4 * (w.L // w.blk)) + 2 * w.Hl * w.D * 2
+
+
+def time_loop(fn, steps, warmup, device):
+    import torch
+
+    for _ in range(max(warmup, 3)):
+        fn()
+    torch.cuda.synchronize(device)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        fn()
+    e.record()
+    torch.cuda.synchronize(device)
+    return s.elapsed_time(e) / steps
 
 
 def algorithmic_bytes(w) -> int:
@@ -446,7 +512,13 @@ def main():
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
-    cfg = CONFIG5
+    cfg = dict(CONFIG5)
+    cfg3 = dict(CONFIG3)
+    if args.batch:
+        cfg["batch"] = cfg3["batch"] = args.batch
+    if args.only == "int8":
+        run_only_int8(cfg3, rank, world, device, args)
+        return
     w = build_workload(cfg, rank, world, device)
     out = torch.empty(w.B, w.Hql, w.D, dtype=torch.bfloat16, device=device)
     gathered = torch.empty(world, w.B, w.Hql, w.D, dtype=torch.bfloat16, device=device) if world > 1 else None
@@ -461,6 +533,11 @@ def main():
             dist.all_gather_into_tensor(gathered, out)
             full.view(w.B, world, w.Hql, w.D).copy_(gathered.permute(1, 0, 2, 3))
 
+    if args.only == "kivi":
+        decode_ms = time_loop(decode, args.steps, args.warmup, device)
+        print(json.dumps({"only": "kivi", "batch": w.B, "decode_ms": decode_ms,
+                          "gbs": algorithmic_bytes(w) / (decode_ms * 1e-3) / 1e9}), flush=True)
+        return
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize(device)
@@ -495,14 +572,20 @@ def main():
     from qkv_b200.ops import _lib
 
     workspace_splits = _lib.load().qkv_kivi_paged_decode_workspace(w.B, w.Hql, w.Hl, w.D, w.g, w.blk, w.L)
-    launches_per_step = 2 if workspace_splits > 0 else 1
+    # residual-window tail kernel + history kernel (+ combine when split)
+    launches_per_step = 3 if workspace_splits > 0 else 2
 
     pack = bench_pack(device) if rank == 0 else None
-    e2e_dt, h2d, d2h = run_e2e(w, device, args.e2e_steps, 3)
-    t = torch.tensor([e2e_dt], dtype=torch.float64, device=device)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_dt = float(t.item())
+    int8 = None
+    if not args.no_int8:
+        int8 = run_int8_leg(cfg3, rank, world, device, args)
+    e2e_dt, h2d, d2h = (None, 0, 0)
+    if args.e2e_steps > 0:
+        e2e_dt, h2d, d2h = run_e2e(w, device, args.e2e_steps, 3)
+        t = torch.tensor([e2e_dt], dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_dt = float(t.item())
 
     if rank == 0:
         peaks = measured_peaks()
@@ -543,8 +626,10 @@ def main():
                          "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
                          "bytes_per_launch": by, "kernel_ms": decode_ms},
             "pack": pack,
-            "e2e": {"value": w.B / e2e_dt, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": e2e_dt * 1e3, "api": "AscendKiviInt4AttentionBackendMixin.forward (DecodeOnly)"},
+            "int8_config3": int8,
+            "e2e": None if e2e_dt is None else {
+                "value": w.B / e2e_dt, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_dt * 1e3, "api": "AscendKiviInt4AttentionBackendMixin.forward (DecodeOnly)"},
             "cpu_baseline": cpu,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": sampler.summary(),
@@ -553,6 +638,42 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_int8_leg(cfg3, rank, world, device, args):
+    """Config 3 (INT8, 64 x 8192): decode tokens/s/layer and HBM GB/s of the
+    int8 paged decode on this rank's heads (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    from qkv_b200.ops import int8_paged_decode
+
+    w8 = build_int8_workload(cfg3, rank, world, device)
+    out8 = torch.empty(w8.B, w8.Hql, w8.D, dtype=torch.bfloat16, device=device)
+
+    def decode8():
+        int8_paged_decode(w8.q, w8.kc, w8.vc, w8.k_aq, w8.v_aq, w8.bt_dev, w8.seq_lens, w8.D ** -0.5, out8, w8.L)
+
+    ms8 = time_loop(decode8, args.steps, args.warmup, device)
+    t = torch.tensor([ms8], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms8 = float(t.item())
+    peak = measured_peaks().get("hbm_gbs") or 6650.0
+    by = int8_bytes(w8)
+    gbs = by / (ms8 * 1e-3) / 1e9
+    del w8, out8
+    torch.cuda.empty_cache()
+    return {"workload": "BASELINE config 3: INT8 decode, 64 x 8192, Hq 32 / KVH 8, head 128",
+            "tokens_per_s_per_layer": cfg3["batch"] / (ms8 * 1e-3), "ms_per_step": ms8,
+            "bytes_per_launch": by, "hbm_gbs": gbs, "frac_of_measured_hbm": gbs / peak,
+            "frac_of_8tbs": gbs / 8000.0}
+
+
+def run_only_int8(cfg3, rank, world, device, args):
+    res = run_int8_leg(cfg3, rank, world, device, args)
+    if rank == 0:
+        print(json.dumps({"only": "int8", **res}), flush=True)
 
 
 if __name__ == "__main__":
