@@ -197,6 +197,31 @@ QKV_API int qkv_kivi_paged_decode(
     int max_seq_len, float scale, void* workspace, size_t workspace_bytes,
     void* out, int64_t out_stride, qkv_stream_t stream);
 
+/* qkv_kivi_paged_decode for callers that cannot allocate device memory. This
+ * entry point has no counterpart in the reference; it exists for callers of
+ * this library that cannot hand it a workspace: an engine that has given all
+ * free device memory to its own KV-cache pool, a host in another language with
+ * no device allocator of its own behind the C ABI, or a serving loop that must
+ * not call cudaMalloc because that call can synchronise the device.
+ * Same arguments and result as qkv_kivi_paged_decode minus the workspace: the
+ * split-KV partials live in a static device array of 8 MiB inside the library
+ * (held on every GPU that loads it until the process exits). A batch whose
+ * partials need more (see qkv_kivi_paged_decode_workspace) is rejected with
+ * QKV_ERR_WORKSPACE. The call allocates nothing. Its first call on a device,
+ * with that device current, looks the array's address up once, so make it
+ * before any stream capture. All calls on a device share the array: calls
+ * that overlap on the GPU race on it and must be serialised by the caller. */
+QKV_API int qkv_kivi_paged_decode_noalloc(
+    const void* query, int64_t q_stride, const int32_t* k_quant,
+    const float* k_scale, const float* k_mn, const int32_t* v_quant,
+    const float* v_scale, const float* v_mn, const void* res_key,
+    const void* res_value, int res_rows, int res_capacity,
+    const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
+    const int32_t* res_state, int batch, int num_heads, int num_kv_heads,
+    int head_size, int group_size, int block_size, int64_t num_blocks,
+    int max_seq_len, float scale, void* out, int64_t out_stride,
+    qkv_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Dense prefill attention (TND)
  * ---------------------------------------------------------------------- */

@@ -69,6 +69,15 @@ SIGNATURES: dict[str, tuple] = {
             c_vp, c_size, c_vp, c_i64, c_vp,
         ],
     ),
+    "qkv_kivi_paged_decode_noalloc": (
+        c_int,
+        [
+            c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int,
+            c_vp, c_i64, c_vp, c_vp,
+            c_int, c_int, c_int, c_int, c_int, c_int, c_i64, c_int, c_float,
+            c_vp, c_i64, c_vp,
+        ],
+    ),
     "qkv_dense_prefill_workspace": (c_size, [c_int, c_int, c_int, c_int, c_int]),
     "qkv_dense_prefill": (
         c_int,
