@@ -291,6 +291,8 @@ def _kivi_decode_case(rng, lens, k_res, v_res, Hq, H, D, g, blk, cap):
         ([40, 77], [8, 5], [16, 16], 4, 2, 32, 8, 16, 16),  # reference toy geometry
         ([300, 1000], [64, 100], [128, 128], 8, 1, 256, 128, 128, 128),  # head 256 / 1 kv head
         ([2000], [32], [32], 64, 8, 128, 128, 128, 128),  # GQA 8
+        ([16384], [77], [128], 64, 8, 128, 128, 128, 128),  # one long request, many splits
+        ([333, 9000, 128, 4000], [128, 5, 0, 128], [128, 128, 0, 100], 16, 2, 128, 64, 128, 128),
     ],
 )
 def test_kivi_paged_decode_vs_oracle(lens, k_res, v_res, Hq, H, D, g, blk, cap):
@@ -318,11 +320,32 @@ def test_kivi_paged_decode_vs_oracle(lens, k_res, v_res, Hq, H, D, g, blk, cap):
     assert_no_device_error()
 
 
-def test_kivi_decode_records_bad_block_ids_without_faulting():
+def test_kivi_decode_without_window_vs_oracle():
+    """No residual state: every position comes from the int4 pages."""
+    from qkv_b200.ops import kivi_paged_decode
+
+    rng = np.random.default_rng(11)
+    lens, Hq, H, D, g, blk = [2048, 700, 5000], 32, 8, 128, 128, 128
+    views, bt, _, _, _ = _kivi_decode_case(rng, lens, [0] * 3, [0] * 3, Hq, H, D, g, blk, 128)
+    B = len(lens)
+    q = O.bf16_round(rng.standard_normal((B, Hq, D)).astype(np.float32))
+    out = torch.zeros(B, Hq, D, dtype=torch.bfloat16, device=dev())
+    tv = tuple(torch.from_numpy(v).to(dev()) for v in views)
+    kivi_paged_decode(bf16_tensor(q), tv, None, None, torch.from_numpy(bt).to(dev()),
+                      torch.tensor(lens, dtype=torch.int32, device=dev()), None, g, D ** -0.5, out, max(lens))
+    # keys past the last whole group stay zero codes in both views and oracle
+    dk, dv = O.kivi_dequant_gather(*views, bt, lens, g, target_bf16=False)
+    want = O.dense_attention(q, dk, dv, [1] * B, lens, D ** -0.5, causal=True)
+    assert_attention_close(to_np(out), want, ATOL)
+    assert_no_device_error()
+
+
+@pytest.mark.parametrize("D,g,blk", [(64, 64, 64), (128, 128, 128)])
+def test_kivi_decode_records_bad_block_ids_without_faulting(D, g, blk):
     """A block id beyond the cache is skipped and reported, never read."""
     from qkv_b200.ops import kivi_paged_decode
 
-    H, D, g, blk = 2, 64, 64, 64
+    H = 2
     views = tuple(torch.from_numpy(v).to(dev()) for v in (
         np.zeros((2, H, D, blk // 8), np.int32), np.ones((2, H, D, 1), np.float32), np.zeros((2, H, D, 1), np.float32),
         np.zeros((2, blk, H, D // 8), np.int32), np.ones((2, blk, H, 1), np.float32), np.zeros((2, blk, H, 1), np.float32),
@@ -330,8 +353,9 @@ def test_kivi_decode_records_bad_block_ids_without_faulting():
     bt = torch.tensor([[0, 5]], dtype=torch.int32, device=dev())  # 5 >= num_blocks
     out = torch.zeros(1, 4, D, dtype=torch.bfloat16, device=dev())
     q = torch.randn(1, 4, D, device=dev()).to(torch.bfloat16)
-    kivi_paged_decode(q, views, None, None, bt, torch.tensor([100], dtype=torch.int32, device=dev()), None, g,
-                      0.1, out, 100)
+    L = blk + blk // 2  # the second page is the bad one
+    kivi_paged_decode(q, views, None, None, bt, torch.tensor([L], dtype=torch.int32, device=dev()), None, g,
+                      0.1, out, L)
     from qkv_b200.ops import _lib
 
     code = _lib.device_error(torch.cuda.current_stream().cuda_stream)

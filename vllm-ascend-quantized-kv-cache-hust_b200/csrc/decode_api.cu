@@ -13,6 +13,11 @@ int launch_decode_generic(const DecodeParams& p, int mode, cudaStream_t stream);
 int launch_decode_mma(const DecodeParams& p, bool kivi, cudaStream_t stream);
 bool decode_mma_supported(const DecodeParams& p, bool kivi);
 SplitPlan plan_for(const DecodeParams& p, bool kivi, int max_seq_len);
+SplitPlan plan_generic(const DecodeParams& p, bool kivi, int max_seq_len);
+bool kivi_tma_geometry(const DecodeParams& p);
+bool kivi_tma_supported(const DecodeParams& p);
+SplitPlan plan_kivi_tma(int batch, int kvh, int max_seq_len, int sms);
+int launch_kivi_tma(const DecodeParams& p, cudaStream_t stream);
 
 namespace {
 
@@ -34,12 +39,20 @@ int check_decode_args(const char* fn, int batch, int num_heads, int kvh,
 
 }  // namespace
 
+// Split plan of the generic CUDA-core kernels (one window split for KIVI).
+SplitPlan plan_generic(const DecodeParams& p, bool kivi, int max_seq_len) {
+  return plan_splits(p.batch, p.kvh, p.blk, max_seq_len, kivi, sm_count(), 4, 256);
+}
+
+// Split plan of the kernel a call with these arguments runs.
 SplitPlan plan_for(const DecodeParams& p, bool kivi, int max_seq_len) {
-  if (decode_mma_supported(p, kivi))
-    return plan_splits(p.batch, p.kvh, p.blk, max_seq_len, kivi, sm_count(), 2,
-                       1024);
-  return plan_splits(p.batch, p.kvh, p.blk, max_seq_len, kivi, sm_count(), 4,
-                     256);
+  if (kivi) {
+    if (kivi_tma_supported(p)) return plan_kivi_tma(p.batch, p.kvh, max_seq_len, sm_count());
+    return plan_generic(p, true, max_seq_len);
+  }
+  if (decode_mma_supported(p, false))
+    return plan_splits(p.batch, p.kvh, p.blk, max_seq_len, false, sm_count(), 2, 1024);
+  return plan_generic(p, false, max_seq_len);
 }
 
 }  // namespace qkv
@@ -78,11 +91,12 @@ size_t qkv_kivi_paged_decode_workspace(int batch, int num_heads,
   p.blk = block_size;
   p.group = group_size;
   // the larger of the two kernels' plans: the call may take either path
-  const SplitPlan fast = plan_for(p, true, max_seq_len);
-  p.group = 8;  // a group the tensor-core kernel does not take
-  const SplitPlan gen = plan_for(p, true, max_seq_len);
-  const size_t a = workspace_bytes(batch, num_heads, head_size, fast.total);
-  const size_t b = workspace_bytes(batch, num_heads, head_size, gen.total);
+  size_t a = 0;
+  if (kivi_tma_geometry(p))
+    a = workspace_bytes(batch, num_heads, head_size,
+                        plan_kivi_tma(batch, num_kv_heads, max_seq_len, sm_count()).total);
+  const size_t b = workspace_bytes(batch, num_heads, head_size,
+                                   plan_generic(p, true, max_seq_len).total);
   return a > b ? a : b;
 }
 
@@ -216,8 +230,8 @@ int qkv_kivi_paged_decode(
                              head_size;
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (decode_mma_supported(p, true)) return launch_decode_mma(p, true, s);
-  return launch_decode_generic(p, kKiviPages, s);
+  if (kivi_tma_supported(p)) return launch_kivi_tma(p, s);
+  return launch_decode_generic(p, kKiviPages, s);  // planned for it by plan_for
 }
 
 size_t qkv_dense_prefill_workspace(int total_q, int num_heads,

@@ -1,0 +1,944 @@
+// KIVI paged decode, page-pipelined version (production geometry: head_size
+// 128, page size 128, group 64/128, up to 8 query heads per KV head).
+//
+// One CTA of 4 warps owns (request, kv head, history split) and streams the
+// split's pages through an S-stage ring in shared memory. One thread issues
+// each page's copies with the Tensor Memory Accelerator:
+//     k_quant  4 boxes {4 words, 128 channels}   (one token quarter each)
+//     v_quant  2 boxes {8 words, 1 head, 128 tokens} (one dim half each)
+//     k_scale, k_mn  one bulk copy each (contiguous per page and head)
+// and every thread copies the v_scale / v_mn of one token with cp.async; all
+// of it completes on the stage's mbarrier. Warp w computes tokens
+// [32w, 32w + 32) of every page:
+//     S^T[token][head] = K[token][channel] . Q'^T[channel][head]
+//     O^T[dim][head]  += V^T[dim][token]   . P'^T[token][head]
+// with mma.sync m16n8k16 (fp16 x fp16 -> fp32), the 8 query heads of the KV
+// head as N. Q' = q * k_scale * softmax_scale * log2(e) (and the per-head
+// constant sum_d q k_mn) depend only on the page and group, so the CTA builds
+// them once per page into shared memory, already in B-fragment order.
+//
+// int4 -> fp16: PRMT gathers byte j of two 32-bit words into the low bytes of
+// a half pair; LOP3 ((x & 0x000F000F) | 0x64006400) yields 1024 + n and the
+// high-nibble mask 1024 + 16 n; one HSUB2 removes the 1024 exactly, so the MMA
+// accumulates the codes n (or 16 n, divided out in fp32). Scales fold into the
+// other operand:
+//     K: S = S' / f + sum_d q[h][d] k_mn[d][group]
+//     V: P'[t][h] = p[t][h] * v_scale[t][group],
+//        O = O' / f + sum_t p[t][h] v_mn[t][group]
+// so the dequantised values enter exactly (code * scale + min in real
+// arithmetic), without the bf16 rounding of a dense gather.
+//
+// Token placement inside a warp's 32 tokens (4 words x 4 bytes x 2 nibbles
+// per channel): score m-tile j, row g holds the low-nibble token of byte
+// B(g, j) = ((g >> 1) + 2j) & 3 of word W(g) = 2 (g >> 2) + (g & 1), row
+// g + 8 the high-nibble token. Each K word a thread loads feeds both m-tiles,
+// the K fragment loads are free of bank conflicts, and the V rows one PV
+// load touches spread over two bank groups.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <math_constants.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "decode_common.cuh"
+
+namespace qkv {
+
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kD = 128;
+constexpr int kBlk = 128;
+constexpr int kHeads = 8;
+constexpr int kTokW = kBlk / kWarps;  // tokens per warp per page
+constexpr int kMaxPages = 64;         // pages per split (ids staged in smem)
+constexpr int kStages = 2;
+constexpr float kInv16 = 0.0625f;
+constexpr long long kWaitCycles = 2000000000ll;  // about a second
+
+template <int NG>
+struct __align__(128) PageStage {
+  uint32_t k[kWarps][kD][4];  // [token quarter][channel][word]
+  uint32_t v[2][kBlk][8];     // [dim half][token][word]
+  float ks[kD * NG];          // [channel][group]
+  float km[kD * NG];
+  float vs[kBlk * NG];        // [token][group]
+  float vm[kBlk * NG];
+};
+
+template <int NG>
+struct __align__(128) PageShared {
+  PageStage<NG> st[kStages];
+  uint4 qf[2][NG][kWarps][32];     // Q' B fragments: [buffer][group][k-step pair][lane]
+  float cmn[2][NG][kWarps][kHeads];  // partial sum_d q k_mn: [buffer][group][k-step pair][head]
+  unsigned long long full[kStages];
+  int pid[kMaxPages];
+};
+
+template <int NG>
+constexpr uint32_t stage_tx_bytes() {
+  return static_cast<uint32_t>(sizeof(uint32_t) * (kWarps * kD * 4 + 2 * kBlk * 8) +
+                               2 * sizeof(float) * kD * NG);
+}
+
+// ------------------------------------------------------------ PTX helpers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(unsigned long long* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred P;\n"
+      " mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, P;\n}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+// Bounded wait: false when the phase did not complete within kWaitCycles.
+__device__ __forceinline__ bool mbar_wait(unsigned long long* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity))
+    if (clock64() - t0 > kWaitCycles) return false;
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            unsigned long long* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];\n" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y,
+                                            int z, unsigned long long* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];\n" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          unsigned long long* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+template <int BYTES>
+__device__ __forceinline__ void cp_async_small(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], %2;\n" ::"r"(smem_u32(dst)), "l"(src),
+               "n"(BYTES));
+}
+__device__ __forceinline__ void cp_async_arrive_noinc(unsigned long long* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(y) : "r"(x));
+  return y;
+}
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t hsub2_1024(uint32_t x) {
+  uint32_t y;
+  asm("sub.f16x2 %0, %1, %2;\n" : "=r"(y) : "r"(x), "r"(0x64006400u));
+  return y;
+}
+// (x & mask) | 0x64006400 as one LOP3 (immLut 0xEA = (a & b) | c)
+__device__ __forceinline__ uint32_t nib_lo(uint32_t x) {
+  uint32_t y;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n" : "=r"(y) : "r"(x), "n"(0x000F000F), "n"(0x64006400));
+  return y;
+}
+__device__ __forceinline__ uint32_t nib_hi(uint32_t x) {
+  uint32_t y;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n" : "=r"(y) : "r"(x), "n"(0x00F000F0), "n"(0x64006400));
+  return y;
+}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  return __byte_perm(a, b, sel);
+}
+// 2^x for x <= 0 (or -inf -> 0) with the SFU's approximate exp2.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// ------------------------------------------------------------ window tail
+
+constexpr int kTailCtas = 4;    // extra CTAs per (request, kv head) for the window
+constexpr int kTailBlock = 32;  // positions per tail step
+
+// Key row `pos` of request b, channels 4 lane .. 4 lane + 3, in fp32: the bf16
+// residual window for positions >= k_begin, else the int4 page.
+__device__ __forceinline__ float4 tail_key4(const DecodeParams& p, const TailState& ts, int b,
+                                           int h, int pos, int lane) {
+  const int64_t kvh = p.kvh;
+  if (pos >= ts.k_begin) {
+    const int slot = (ts.k_start + (pos - ts.k_begin)) % p.res_cap;
+    const __nv_bfloat16* row =
+        p.rk + ((static_cast<int64_t>(ts.row) * p.res_cap + slot) * kvh + h) * kD + 4 * lane;
+    const uint2 raw = *reinterpret_cast<const uint2*>(row);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+    const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+    return make_float4(a.x, a.y, c.x, c.y);
+  }
+  int64_t page = -1;
+  if (lane == 0) page = page_of(p, b, pos);
+  page = __shfl_sync(0xffffffffu, page, 0);
+  if (page < 0) return make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  const int off = pos % kBlk, ng = kBlk / p.group;
+  float r[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int64_t chan = (page * kvh + h) * kD + 4 * lane + k;
+    const uint32_t w = static_cast<uint32_t>(p.kq[chan * (kBlk / 8) + (off >> 3)]);
+    const int64_t si = chan * ng + off / p.group;
+    r[k] = __fadd_rn(__fmul_rn(static_cast<float>((w >> (4 * (off & 7))) & 0xFu), p.ks[si]), p.km[si]);
+  }
+  return make_float4(r[0], r[1], r[2], r[3]);
+}
+
+// Value row `pos` of request b, dims 4 lane .. 4 lane + 3, in fp32 (window
+// for positions >= v_begin, else the int4 page).
+__device__ __forceinline__ float4 tail_value4(const DecodeParams& p, const TailState& ts, int b,
+                                             int h, int pos, int lane) {
+  const int64_t kvh = p.kvh;
+  if (pos >= ts.v_begin) {
+    const int slot = (ts.v_start + (pos - ts.v_begin)) % p.res_cap;
+    const __nv_bfloat16* row =
+        p.rv + ((static_cast<int64_t>(ts.row) * p.res_cap + slot) * kvh + h) * kD + 4 * lane;
+    const uint2 raw = *reinterpret_cast<const uint2*>(row);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+    const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+    return make_float4(a.x, a.y, c.x, c.y);
+  }
+  int64_t page = -1;
+  if (lane == 0) page = page_of(p, b, pos);
+  page = __shfl_sync(0xffffffffu, page, 0);
+  if (page < 0) return make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  const int64_t vrow = (page * kBlk + pos % kBlk) * kvh + h;
+  const uint32_t w = static_cast<uint32_t>(p.vq[vrow * (kD / 8) + (lane >> 1)]);
+  const int64_t si = vrow * (kD / p.group) + (4 * lane) / p.group;  // 4 dims share a group
+  const float sc = p.vs[si], mn = p.vm[si];
+  float r[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t code = (w >> (4 * (4 * (lane & 1) + k))) & 0xFu;
+    r[k] = __fadd_rn(__fmul_rn(static_cast<float>(code), sc), mn);
+  }
+  return make_float4(r[0], r[1], r[2], r[3]);
+}
+
+constexpr int kTailLd = kD + 4;  // padded fp32 row of the staged keys
+
+// One tail CTA: positions [body_end, L) in blocks of kTailBlock, blocks
+// c, c + n_tail, ...; its partial softmax state is split num_hist_splits + c.
+// Each block's K and V rows are staged in shared memory (fp32) with
+// independent 8-byte loads, then scored and accumulated from there; fp32
+// CUDA-core math (the window is < 1% of the bytes).
+__device__ __forceinline__ void window_tail(const DecodeParams& p, int c, int n_tail, int h, int b,
+                                            unsigned char* smem) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = p.gqa;
+  float* kt = reinterpret_cast<float*>(smem);  // [kTailBlock][kTailLd]
+  float* vt = kt + kTailBlock * kTailLd;        // [kTailBlock][kD]
+  float* sc = vt + kTailBlock * kD;             // [kTailBlock][kHeads] scores, then probs
+  float* st_m = sc + kTailBlock * kHeads;       // [kHeads]
+  float* st_l = st_m + kHeads;
+  float* st_a = st_l + kHeads;
+  const int L = max(p.seq_lens[b], 0);
+  const TailState ts = load_tail_state(p, b, L);
+  const int body_end = min(ts.k_begin, ts.v_begin);
+
+  // q * scale * log2(e), channels 4 lane .. 4 lane + 3 of every head
+  float q[kHeads][4];
+  const __nv_bfloat16* qrow =
+      p.q + static_cast<int64_t>(b) * p.q_stride + static_cast<int64_t>(h) * G * kD + 4 * lane;
+#pragma unroll
+  for (int hd = 0; hd < kHeads; ++hd)
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      q[hd][k] = hd < G ? __bfloat162float(qrow[hd * kD + k]) * p.scale_log2 : 0.0f;
+  if (tid < kHeads) {
+    st_m[tid] = -CUDART_INF_F;
+    st_l[tid] = 0.0f;
+  }
+  float acc[kHeads];
+#pragma unroll
+  for (int hd = 0; hd < kHeads; ++hd) acc[hd] = 0.0f;
+  // after the butterfly, lane holds the sum of head bit4 * 4 + bit3 * 2 + bit2
+  const int my_head = (((lane >> 4) & 1) << 2) | (((lane >> 3) & 1) << 1) | ((lane >> 2) & 1);
+  const bool b4 = (lane >> 4) & 1, b3 = (lane >> 3) & 1, b2 = (lane >> 2) & 1;
+
+  for (int blk = c; body_end + kTailBlock * blk < L; blk += n_tail) {
+    const int p0 = body_end + kTailBlock * blk;
+    const int n = min(kTailBlock, L - p0);
+    // ---- stage rows 8 warp .. 8 warp + 7 of K and V
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = 8 * warp + i;
+      float4 k4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f), v4 = k4;
+      if (r < n) {
+        k4 = tail_key4(p, ts, b, h, p0 + r, lane);
+        v4 = tail_value4(p, ts, b, h, p0 + r, lane);
+      }
+      *reinterpret_cast<float4*>(&kt[r * kTailLd + 4 * lane]) = k4;
+      *reinterpret_cast<float4*>(&vt[r * kD + 4 * lane]) = v4;
+    }
+    __syncthreads();
+    // ---- scores: warp w, positions 8 w .. 8 w + 7 of the block
+#pragma unroll 2
+    for (int i = 0; i < 8; ++i) {
+      const int r = 8 * warp + i;
+      const float4 k4 = *reinterpret_cast<const float4*>(&kt[r * kTailLd + 4 * lane]);
+      float part[kHeads];
+#pragma unroll
+      for (int hd = 0; hd < kHeads; ++hd)
+        part[hd] = fmaf(q[hd][0], k4.x, fmaf(q[hd][1], k4.y, fmaf(q[hd][2], k4.z, q[hd][3] * k4.w)));
+      // transpose-reduce the 8 head sums over the 32 lanes (9 shuffles)
+      float h4[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float keep = b4 ? part[k + 4] : part[k];
+        const float send = b4 ? part[k] : part[k + 4];
+        h4[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+      }
+      float h2[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const float keep = b3 ? h4[k + 2] : h4[k];
+        const float send = b3 ? h4[k] : h4[k + 2];
+        h2[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+      }
+      float v;
+      {
+        const float keep = b2 ? h2[1] : h2[0];
+        const float send = b2 ? h2[0] : h2[1];
+        v = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+      }
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      if ((lane & 3) == 0) sc[r * kHeads + my_head] = r < n ? v : -CUDART_INF_F;
+    }
+    __syncthreads();
+    // ---- online softmax: warp w owns heads 2w, 2w + 1; lanes = positions
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int hd = 2 * warp + e;
+      const float v = sc[lane * kHeads + hd];
+      float mx = v;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float m_old = st_m[hd];
+      const float m_new = fmaxf(m_old, mx);
+      const float pr = v == -CUDART_INF_F ? 0.0f : exp2f(v - m_new);
+      float sum = pr;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      sc[lane * kHeads + hd] = pr;
+      __syncwarp();
+      if (lane == 0) {
+        const float alpha =
+            m_new == -CUDART_INF_F ? 1.0f : (m_old == -CUDART_INF_F ? 0.0f : exp2f(m_old - m_new));
+        st_m[hd] = m_new;
+        st_l[hd] = st_l[hd] * alpha + sum;
+        st_a[hd] = alpha;
+      }
+    }
+    __syncthreads();
+    // ---- P V: thread = dim
+#pragma unroll
+    for (int hd = 0; hd < kHeads; ++hd) acc[hd] *= st_a[hd];
+    for (int j = 0; j < n; ++j) {
+      const float v = vt[j * kD + tid];
+      const float4 pa = *reinterpret_cast<const float4*>(&sc[j * kHeads]);
+      const float4 pb = *reinterpret_cast<const float4*>(&sc[j * kHeads + 4]);
+      acc[0] = fmaf(pa.x, v, acc[0]);
+      acc[1] = fmaf(pa.y, v, acc[1]);
+      acc[2] = fmaf(pa.z, v, acc[2]);
+      acc[3] = fmaf(pa.w, v, acc[3]);
+      acc[4] = fmaf(pb.x, v, acc[4]);
+      acc[5] = fmaf(pb.y, v, acc[5]);
+      acc[6] = fmaf(pb.z, v, acc[6]);
+      acc[7] = fmaf(pb.w, v, acc[7]);
+    }
+    __syncthreads();
+  }
+  const int split = p.num_hist_splits + c;
+#pragma unroll
+  for (int hd = 0; hd < kHeads; ++hd)
+    if (hd < G) store_partial(p, b, h * G + hd, split, tid, acc[hd], st_m[hd], st_l[hd]);
+}
+
+static_assert(sizeof(float) * (kTailBlock * (kTailLd + kD + kHeads) + 3 * kHeads) <=
+                  sizeof(PageShared<1>),
+              "tail staging must fit in the kernel's shared memory");
+
+// ------------------------------------------------------------ the kernel
+
+template <int NG>
+__global__ void __launch_bounds__(kThreads, 4)
+kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tmap_k,
+                       const __grid_constant__ CUtensorMap tmap_v) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  PageShared<NG>& sh = *reinterpret_cast<PageShared<NG>*>(smem_raw);
+  const int n_tail = p.splits_total - p.num_hist_splits;  // window CTAs come first
+  const int h = blockIdx.y, b = blockIdx.z;
+  if (static_cast<int>(blockIdx.x) < n_tail) {
+    window_tail(p, blockIdx.x, n_tail, h, b, smem_raw);
+    return;
+  }
+  const int split = blockIdx.x - n_tail;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int G = p.gqa;
+  const int kvh = p.kvh;
+
+  // ---- the split's history range [t0, t1): positions before the window
+  const int L = max(p.seq_lens[b], 0);
+  const TailState ts = load_tail_state(p, b, L);
+  const int body_end = min(ts.k_begin, ts.v_begin);
+  const int t0 = split * p.split_tokens;
+  const int t1 = min(body_end, t0 + p.split_tokens);
+  const int n_pages = t1 > t0 ? min((t1 - t0 + kBlk - 1) / kBlk, kMaxPages) : 0;
+
+  for (int i = tid; i < n_pages; i += kThreads)
+    sh.pid[i] = static_cast<int>(page_of(p, b, t0 + i * kBlk));
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) mbar_init(&sh.full[s], kThreads + 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+  }
+
+  // q of the Q' entries this thread builds: head g, channels
+  // 16 (2 warp + e) + 4 r + t (k-steps 2 warp and 2 warp + 1)
+  float qv[8];
+  {
+    const __nv_bfloat16* qrow =
+        p.q + static_cast<int64_t>(b) * p.q_stride + (static_cast<int64_t>(h) * G + g) * kD;
+#pragma unroll
+    for (int e = 0; e < 2; ++e)
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+        qv[4 * e + r] =
+            g < G ? __bfloat162float(qrow[16 * (2 * warp + e) + 4 * r + t]) * p.scale_log2 : 0.0f;
+  }
+  __syncthreads();
+
+  // Issues the copies of page ii into stage ii % kStages (all threads).
+  auto issue = [&](int ii) {
+    const int s = ii % kStages;
+    PageStage<NG>& st = sh.st[s];
+    const int pg = sh.pid[ii];
+    if (pg >= 0) {
+      if (tid == 0) {
+        mbar_expect_tx(&sh.full[s], stage_tx_bytes<NG>());
+        const int krow = (pg * kvh + h) * kD;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) tma_load_2d(&st.k[w][0][0], &tmap_k, 4 * w, krow, &sh.full[s]);
+#pragma unroll
+        for (int hp = 0; hp < 2; ++hp)
+          tma_load_3d(&st.v[hp][0][0], &tmap_v, 8 * hp, h, pg * kBlk, &sh.full[s]);
+        const int64_t soff = (static_cast<int64_t>(pg) * kvh + h) * kD * NG;
+        bulk_load(st.ks, p.ks + soff, sizeof(float) * kD * NG, &sh.full[s]);
+        bulk_load(st.km, p.km + soff, sizeof(float) * kD * NG, &sh.full[s]);
+      }
+      const int64_t voff = ((static_cast<int64_t>(pg) * kBlk + tid) * kvh + h) * NG;
+      cp_async_small<4 * NG>(&st.vs[tid * NG], p.vs + voff);
+      cp_async_small<4 * NG>(&st.vm[tid * NG], p.vm + voff);
+      cp_async_arrive_noinc(&sh.full[s]);
+    } else {
+      if (tid == 0) mbar_arrive(&sh.full[s]);
+      mbar_arrive(&sh.full[s]);
+    }
+  };
+
+#pragma unroll
+  for (int i = 0; i < kStages - 1; ++i)
+    if (i < n_pages) issue(i);
+
+  // ---- per-warp running state: heads 2t, 2t+1 of this thread
+  float o[8][4];
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.0f;
+  float m_run[2] = {-CUDART_INF_F, -CUDART_INF_F};
+  float l_run[2] = {0.0f, 0.0f};
+  float mn_acc[2][NG];
+#pragma unroll
+  for (int e = 0; e < 2; ++e)
+#pragma unroll
+    for (int gg = 0; gg < NG; ++gg) mn_acc[e][gg] = 0.0f;
+
+  // token placement (see the file comment)
+  const int W = 2 * (g >> 2) + (g & 1);
+  uint32_t ksel[2];
+  int tok_j[2];  // local token of row g in m-tile j (row g + 8: + 1)
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int B = ((g >> 1) + 2 * j) & 3;
+    ksel[j] = static_cast<uint32_t>(B | ((4 + B) << 8));
+    tok_j[j] = 8 * W + 2 * B;
+  }
+  // PV k-step j: rows 2t, 2t+1 of score m-tile j -> tokens va[j], va[j] + 8
+  int va[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) va[j] = 16 * (t >> 1) + 2 * (t ^ (2 * j));
+  const int grp = NG == 2 ? (warp >> 1) : 0;  // key group of this warp's tokens
+
+  int consumed = 0;
+  bool aborted = false;
+  for (int i = 0; i < n_pages; ++i) {
+    const int s = i % kStages;
+    const uint32_t parity = static_cast<uint32_t>((i / kStages) & 1);
+    const bool ok = mbar_wait(&sh.full[s], parity);
+    const PageStage<NG>& st = sh.st[s];
+    const int pg = sh.pid[i];
+    const int qb = i & 1;
+    if (pg >= 0 && ok) {
+      // Q' entries of k-steps 2 warp, 2 warp + 1 (lane = fragment owner)
+#pragma unroll
+      for (int gq = 0; gq < NG; ++gq) {
+        float c = 0.0f;
+        uint32_t f[4];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          float qq[4];
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const int ch = 16 * (2 * warp + e) + 4 * r + t;
+            qq[r] = qv[4 * e + r] * st.ks[ch * NG + gq];
+            c = fmaf(qv[4 * e + r], st.km[ch * NG + gq], c);
+          }
+          f[2 * e] = pack_half2(qq[0], qq[1]);
+          f[2 * e + 1] = pack_half2(qq[2], qq[3]);
+        }
+        sh.qf[qb][gq][warp][lane] = make_uint4(f[0], f[1], f[2], f[3]);
+        c += __shfl_xor_sync(0xffffffffu, c, 1);
+        c += __shfl_xor_sync(0xffffffffu, c, 2);
+        if (t == 0) sh.cmn[qb][gq][warp][g] = c;
+      }
+    }
+    if (!__syncthreads_and(ok ? 1 : 0)) {  // uniform: every thread leaves here
+      if (tid == 0) record_error(p.err, kErrPipelineTimeout);
+      aborted = true;
+      consumed = i;
+      break;
+    }
+    consumed = i + 1;
+    if (i + kStages - 1 < n_pages) issue(i + kStages - 1);
+    if (pg < 0) continue;
+    const int pos0 = t0 + i * kBlk;
+    const int valid = min(kBlk, t1 - pos0) - kTokW * warp;  // live tokens of this warp
+    if (valid <= 0) continue;
+
+    // ---- B fragments of Q' and the per-head constants
+    uint32_t bq[8][2];
+#pragma unroll
+    for (int kp = 0; kp < 4; ++kp) {
+      const uint4 v = sh.qf[qb][grp][kp][lane];
+      bq[2 * kp][0] = v.x;
+      bq[2 * kp][1] = v.y;
+      bq[2 * kp + 1][0] = v.z;
+      bq[2 * kp + 1][1] = v.w;
+    }
+    float cmn[2];
+    {
+      float2 c = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int kp = 0; kp < 4; ++kp) {
+        const float2 v = *reinterpret_cast<const float2*>(&sh.cmn[qb][grp][kp][2 * t]);
+        c.x += v.x;
+        c.y += v.y;
+      }
+      cmn[0] = c.x;
+      cmn[1] = c.y;
+    }
+
+    // ---- S'^T = K . Q'^T for the warp's two m-tiles
+    float sc[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
+    const uint32_t* kb = &st.k[warp][t][W];
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const uint32_t w0 = kb[(16 * kk + 0) * 4];
+      const uint32_t w1 = kb[(16 * kk + 4) * 4];
+      const uint32_t w2 = kb[(16 * kk + 8) * 4];
+      const uint32_t w3 = kb[(16 * kk + 12) * 4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint32_t x01 = prmt(w0, w1, ksel[j]);
+        const uint32_t x23 = prmt(w2, w3, ksel[j]);
+        mma16816(sc[j], hsub2_1024(nib_lo(x01)), hsub2_1024(nib_hi(x01)), hsub2_1024(nib_lo(x23)),
+                 hsub2_1024(nib_hi(x23)), bq[kk][0], bq[kk][1]);
+      }
+    }
+    // scores in log2 units: [j][0..1] low-nibble token, heads 2t, 2t+1; [j][2..3] its +1
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        sc[j][e] += cmn[e];
+        sc[j][2 + e] = fmaf(sc[j][2 + e], kInv16, cmn[e]);
+      }
+    const bool partial = valid < kTokW;
+    if (partial) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const bool lo_ok = tok_j[j] < valid, hi_ok = tok_j[j] + 1 < valid;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          if (!lo_ok) sc[j][e] = -CUDART_INF_F;
+          if (!hi_ok) sc[j][2 + e] = -CUDART_INF_F;
+        }
+      }
+    }
+
+    // ---- online softmax over heads 2t, 2t+1 (max over the warp's tokens)
+    float mx[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      mx[e] = fmaxf(fmaxf(sc[0][e], sc[0][2 + e]), fmaxf(sc[1][e], sc[1][2 + e]));
+      mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 4));
+      mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 8));
+      mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 16));
+    }
+    const bool grow0 = mx[0] > m_run[0], grow1 = mx[1] > m_run[1];
+    if (__any_sync(0xffffffffu, grow0 || grow1)) {
+      float alpha[2];
+      alpha[0] = grow0 ? fast_exp2(m_run[0] - mx[0]) : 1.0f;
+      alpha[1] = grow1 ? fast_exp2(m_run[1] - mx[1]) : 1.0f;
+      if (grow0) m_run[0] = mx[0];
+      if (grow1) m_run[1] = mx[1];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        l_run[e] *= alpha[e];
+#pragma unroll
+        for (int gg = 0; gg < NG; ++gg) mn_acc[e][gg] *= alpha[e];
+      }
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        o[mt][0] *= alpha[0];
+        o[mt][1] *= alpha[1];
+        o[mt][2] *= alpha[0];
+        o[mt][3] *= alpha[1];
+      }
+    }
+
+    // ---- probabilities -> P'^T B fragments (per value group), v_mn terms
+    uint32_t pb[2][NG][2];
+    const float* vsw = &st.vs[kTokW * warp * NG];
+    const float* vmw = &st.vm[kTokW * warp * NG];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float pr[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) pr[c] = fast_exp2(sc[j][c] - m_run[c & 1]);
+      l_run[0] += pr[0] + pr[2];
+      l_run[1] += pr[1] + pr[3];
+      float sl[NG], sh_[NG], ml[NG], mh[NG];
+      if (NG == 1) {
+        const float2 s2 = *reinterpret_cast<const float2*>(vsw + tok_j[j]);
+        const float2 m2 = *reinterpret_cast<const float2*>(vmw + tok_j[j]);
+        sl[0] = s2.x;
+        sh_[0] = s2.y;
+        ml[0] = m2.x;
+        mh[0] = m2.y;
+      } else {
+        const float4 s4 = *reinterpret_cast<const float4*>(vsw + 2 * tok_j[j]);
+        const float4 m4 = *reinterpret_cast<const float4*>(vmw + 2 * tok_j[j]);
+        sl[0] = s4.x;
+        sl[NG - 1] = s4.y;
+        sh_[0] = s4.z;
+        sh_[NG - 1] = s4.w;
+        ml[0] = m4.x;
+        ml[NG - 1] = m4.y;
+        mh[0] = m4.z;
+        mh[NG - 1] = m4.w;
+      }
+      if (partial) {
+        // dead tokens contribute nothing, whatever their (stale) scales hold
+        const bool lo_ok = tok_j[j] < valid, hi_ok = tok_j[j] + 1 < valid;
+#pragma unroll
+        for (int gg = 0; gg < NG; ++gg) {
+          sl[gg] = lo_ok ? sl[gg] : 0.0f;
+          ml[gg] = lo_ok ? ml[gg] : 0.0f;
+          sh_[gg] = hi_ok ? sh_[gg] : 0.0f;
+          mh[gg] = hi_ok ? mh[gg] : 0.0f;
+        }
+      }
+#pragma unroll
+      for (int gg = 0; gg < NG; ++gg) {
+        mn_acc[0][gg] = fmaf(pr[0], ml[gg], fmaf(pr[2], mh[gg], mn_acc[0][gg]));
+        mn_acc[1][gg] = fmaf(pr[1], ml[gg], fmaf(pr[3], mh[gg], mn_acc[1][gg]));
+        pb[j][gg][0] = movmatrix_t(pack_half2(pr[0] * sl[gg], pr[1] * sl[gg]));
+        pb[j][gg][1] = movmatrix_t(pack_half2(pr[2] * sh_[gg], pr[3] * sh_[gg]));
+      }
+    }
+
+    // ---- O'^T += V^T . P'^T; k-step j: k (2t, 2t+1) = tokens (va, va + 8),
+    // k (2t+8, 2t+9) = their + 1; m-tile (jp, hp): byte jp of word 8 hp + g
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint32_t* vb = &st.v[0][kTokW * warp + va[j]][g];
+      uint32_t wa0[2], wb0[2], wa1[2], wb1[2];
+#pragma unroll
+      for (int hp = 0; hp < 2; ++hp) {
+        wa0[hp] = vb[hp * kBlk * 8 + 0];
+        wb0[hp] = vb[hp * kBlk * 8 + 8 * 8];
+        wa1[hp] = vb[hp * kBlk * 8 + 1 * 8];
+        wb1[hp] = vb[hp * kBlk * 8 + 9 * 8];
+      }
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        const int jp = mt & 3, hp = mt >> 2;
+        const uint32_t sel = static_cast<uint32_t>(jp | ((4 + jp) << 8));
+        const uint32_t x0 = prmt(wa0[hp], wb0[hp], sel);
+        const uint32_t x1 = prmt(wa1[hp], wb1[hp], sel);
+        const int gg = NG == 2 ? hp : 0;
+        mma16816(o[mt], hsub2_1024(nib_lo(x0)), hsub2_1024(nib_hi(x0)), hsub2_1024(nib_lo(x1)),
+                 hsub2_1024(nib_hi(x1)), pb[j][gg][0], pb[j][gg][1]);
+      }
+    }
+  }
+
+  if (aborted) {
+    // let the copies still in flight land before the shared memory is reused
+    if (tid == 0)
+      for (int i = consumed; i < min(n_pages, consumed + kStages - 1); ++i)
+        (void)mbar_wait(&sh.full[i % kStages], static_cast<uint32_t>((i / kStages) & 1));
+  }
+  __syncthreads();
+
+  // ---- merge the 4 warps: sum l and mn over the 8 row groups first
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      l_run[e] += __shfl_xor_sync(0xffffffffu, l_run[e], off);
+#pragma unroll
+      for (int gg = 0; gg < NG; ++gg) mn_acc[e][gg] += __shfl_xor_sync(0xffffffffu, mn_acc[e][gg], off);
+    }
+  }
+  float* mo = reinterpret_cast<float*>(smem_raw);  // [warp][head][dim]
+  float* mm = mo + kWarps * kHeads * kD;            // [warp][head]
+  float* ml = mm + kWarps * kHeads;
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    const int jp = mt & 3, hp = mt >> 2;
+    const int d_lo = 8 * (8 * hp + g) + 2 * jp;
+    const int gg = NG == 2 ? hp : 0;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int head = 2 * t + e;
+      mo[(warp * kHeads + head) * kD + d_lo] = o[mt][e] + mn_acc[e][gg];
+      mo[(warp * kHeads + head) * kD + d_lo + 1] = fmaf(o[mt][2 + e], kInv16, mn_acc[e][gg]);
+    }
+  }
+  if (g == 0) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      mm[warp * kHeads + 2 * t + e] = m_run[e];
+      ml[warp * kHeads + 2 * t + e] = l_run[e];
+    }
+  }
+  __syncthreads();
+  for (int idx = tid; idx < kHeads * kD; idx += kThreads) {
+    const int head = idx / kD, d = idx % kD;
+    if (head >= G) continue;
+    float M = -CUDART_INF_F;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, mm[w * kHeads + head]);
+    float acc = 0.0f, l = 0.0f;
+    if (M != -CUDART_INF_F) {
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        const float mw = mm[w * kHeads + head];
+        if (mw == -CUDART_INF_F) continue;
+        const float sc = exp2f(mw - M);
+        acc = fmaf(sc, mo[(w * kHeads + head) * kD + d], acc);
+        l = fmaf(sc, ml[w * kHeads + head], l);
+      }
+    }
+    store_partial(p, b, h * G + head, split, d, acc, M, l);
+  }
+}
+
+static_assert(sizeof(PageStage<1>) * kStages >= sizeof(float) * (kWarps * kHeads * kD + 2 * kWarps * kHeads),
+              "merge buffers must fit in the stage memory");
+
+// ------------------------------------------------------------ host side
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+int encode_maps(const DecodeParams& p, CUtensorMap* tk, CUtensorMap* tv) {
+  auto enc = encode_fn();
+  if (enc == nullptr) return set_error(QKV_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  {
+    // k_quant as [NB * KVH * D rows][B/8 words]
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kBlk / 8),
+                                static_cast<cuuint64_t>(p.num_blocks) * p.kvh * kD};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kBlk / 8) * 4};
+    const cuuint32_t box[2] = {4, kD};
+    const cuuint32_t es[2] = {1, 1};
+    const CUresult r = enc(tk, CU_TENSOR_MAP_DATA_TYPE_INT32, 2, const_cast<int32_t*>(p.kq), dims,
+                           strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+      return set_error(QKV_ERR_CUDA, "cuTensorMapEncodeTiled(k_quant) failed: " + std::to_string(r));
+  }
+  {
+    // v_quant as [NB * B tokens][KVH][D/8 words]
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD / 8), static_cast<cuuint64_t>(p.kvh),
+                                static_cast<cuuint64_t>(p.num_blocks) * kBlk};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kD / 8) * 4,
+                                   static_cast<cuuint64_t>(kD / 8) * 4 * p.kvh};
+    const cuuint32_t box[3] = {8, 1, kBlk};
+    const cuuint32_t es[3] = {1, 1, 1};
+    const CUresult r = enc(tv, CU_TENSOR_MAP_DATA_TYPE_INT32, 3, const_cast<int32_t*>(p.vq), dims,
+                           strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+      return set_error(QKV_ERR_CUDA, "cuTensorMapEncodeTiled(v_quant) failed: " + std::to_string(r));
+  }
+  return QKV_OK;
+}
+
+template <int NG>
+int set_smem_attr() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::atomic<uint64_t> done{0};
+  const uint64_t bit = 1ull << (dev & 63);
+  if ((done.load() & bit) == 0) {
+    const cudaError_t e = cudaFuncSetAttribute(kivi_decode_tma_kernel<NG>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(sizeof(PageShared<NG>)));
+    if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(kivi_decode_tma_kernel)");
+    done.fetch_or(bit);
+  }
+  return QKV_OK;
+}
+
+}  // namespace
+
+bool kivi_tma_geometry(const DecodeParams& p) {
+  return p.head_size == kD && p.blk == kBlk && (p.group == 64 || p.group == 128) && p.gqa >= 1 &&
+         p.gqa <= kHeads;
+}
+
+bool kivi_tma_supported(const DecodeParams& p) {
+  const auto al = [](const void* x, uintptr_t a) { return (reinterpret_cast<uintptr_t>(x) & (a - 1)) == 0; };
+  return kivi_tma_geometry(p) && p.num_blocks > 0 &&
+         static_cast<int64_t>(p.num_blocks) * p.kvh * kD < (int64_t{1} << 31) && al(p.kq, 16) && al(p.vq, 16) && al(p.ks, 16) &&
+         al(p.km, 16) && al(p.vs, 8) && al(p.vm, 8);
+}
+
+// CTAs of the page-pipelined kernel resident per SM (shared memory and
+// registers allow 4 for both group sizes).
+int kivi_tma_ctas_per_sm() { return 4; }
+
+// Splits chosen for whole waves: among split counts that keep each split
+// within kMaxPages pages, the one whose grid best fills its last wave, with a
+// small charge per split for the partial-state traffic of the combine.
+SplitPlan plan_kivi_tma(int batch, int kvh, int max_seq_len, int sms) {
+  SplitPlan plan;
+  const int pages = max_seq_len > 0 ? (max_seq_len + kBlk - 1) / kBlk : 1;
+  const int units = batch * kvh > 0 ? batch * kvh : 1;
+  const int resident = sms * kivi_tma_ctas_per_sm();
+  const int s_min = (pages + kMaxPages - 1) / kMaxPages;
+  int s_max = (8 * resident + units - 1) / units;
+  s_max = s_max < s_min ? s_min : s_max;
+  s_max = s_max > pages ? pages : s_max;
+  double best_score = -1.0;
+  int best_pps = pages;
+  for (int s = s_min; s <= s_max; ++s) {
+    const int pps = (pages + s - 1) / s;
+    if (pps > kMaxPages) continue;
+    const int se = (pages + pps - 1) / pps;
+    const long long grid = static_cast<long long>(units) * se;
+    const long long waves = (grid + resident - 1) / resident;
+    const double eff = static_cast<double>(grid) / static_cast<double>(waves * resident);
+    const double score = eff - 0.004 * se;
+    if (score > best_score + 1e-9) {
+      best_score = score;
+      best_pps = pps;
+    }
+  }
+  plan.split_tokens = best_pps * kBlk;
+  plan.hist_splits = (pages + best_pps - 1) / best_pps;
+  plan.total = plan.hist_splits + kTailCtas;
+  return plan;
+}
+
+int launch_kivi_tma(const DecodeParams& p0, cudaStream_t stream) {
+  DecodeParams p = p0;
+  // window CTAs only when there is a window; the partial count shrinks to match
+  if (p.res_state == nullptr) p.splits_total = p.num_hist_splits;
+  CUtensorMap tk, tv;
+  int rc = encode_maps(p, &tk, &tv);
+  if (rc != QKV_OK) return rc;
+  dim3 grid(p.splits_total, p.kvh, p.batch);
+  if (p.group == 128) {
+    if ((rc = set_smem_attr<1>()) != QKV_OK) return rc;
+    kivi_decode_tma_kernel<1><<<grid, kThreads, sizeof(PageShared<1>), stream>>>(p, tk, tv);
+  } else {
+    if ((rc = set_smem_attr<2>()) != QKV_OK) return rc;
+    kivi_decode_tma_kernel<2><<<grid, kThreads, sizeof(PageShared<2>), stream>>>(p, tk, tv);
+  }
+  QKV_CHECK_LAUNCH("kivi_decode_tma_kernel");
+  if (p.splits_total > 1) {
+    launch_combine(p, stream);
+    QKV_CHECK_LAUNCH("combine_kernel");
+  }
+  return QKV_OK;
+}
+
+}  // namespace qkv

@@ -44,6 +44,7 @@ enum DeviceError : int {
   kErrBlock = 2,
   kErrResidualRow = 3,
   kErrNegativeBlock = 4,
+  kErrPipelineTimeout = 5,  // a bounded wait on an in-kernel copy gave up
 };
 
 // Device address of this device's error word (a __device__ int defined in
