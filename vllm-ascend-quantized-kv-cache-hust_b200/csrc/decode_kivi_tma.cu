@@ -56,6 +56,7 @@ constexpr int kTokW = kBlk / kWarps;  // tokens per warp per page
 constexpr int kMaxPages = 64;         // pages per split (ids staged in smem)
 constexpr int kStages = 2;
 constexpr float kInv16 = 0.0625f;
+constexpr float kLazy = 4.0f;  // log2 headroom of the running max
 constexpr long long kWaitCycles = 2000000000ll;  // about a second
 
 template <int NG>
@@ -199,7 +200,7 @@ __device__ __forceinline__ float fast_exp2(float x) {
 
 // ------------------------------------------------------------ window tail
 
-constexpr int kTailCtas = 4;    // extra CTAs per (request, kv head) for the window
+constexpr int kTailCtas = 2;    // extra CTAs per (request, kv head) for the window
 constexpr int kTailBlock = 32;  // positions per tail step
 
 // Key row `pos` of request b, channels 4 lane .. 4 lane + 3, in fp32: the bf16
@@ -638,7 +639,11 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
       mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 8));
       mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 16));
     }
-    const bool grow0 = mx[0] > m_run[0], grow1 = mx[1] > m_run[1];
+    // lazy rescale: the running max only moves when a score passes it by more
+    // than kLazy (log2 units), so p <= 2^kLazy and P' stays far from fp16
+    // overflow; o, l and the v_mn sums share the stale max, so the result is
+    // unchanged. The first live page always sets it (m_run = -inf).
+    const bool grow0 = mx[0] > m_run[0] + kLazy, grow1 = mx[1] > m_run[1] + kLazy;
     if (__any_sync(0xffffffffu, grow0 || grow1)) {
       float alpha[2];
       alpha[0] = grow0 ? fast_exp2(m_run[0] - mx[0]) : 1.0f;
