@@ -307,46 +307,89 @@ def algorithmic_bytes(w) -> int:
     return B * (H * per_head + 2 * Hq * D * 2 + 4 * ((L + w.blk - 1) // w.blk))
 
 
-class ClockSampler:
-    """Samples SM clock and throttle reasons of one GPU during a region."""
+_CLOCK_POLLER = r"""
+import sys, time
+idx, uuid, period = int(sys.argv[1]), sys.argv[2], float(sys.argv[3])
+try:
+    import pynvml as nv
+    nv.nvmlInit()
+    try:
+        h = nv.nvmlDeviceGetHandleByUUID(uuid)
+    except Exception:
+        h = nv.nvmlDeviceGetHandleByIndex(idx)
+    flags = [nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+             nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap]
+    while True:
+        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        print(f"{sm},{mx},,{hex(r)}," + ",".join("Active" if r & f else "Not Active" for f in flags), flush=True)
+        time.sleep(period)
+except Exception:  # no NVML: nvidia-smi, slower
+    import subprocess
+    q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+    while True:
+        out = subprocess.run(["nvidia-smi", "--query-gpu=" + q, "--format=csv,noheader,nounits", "-i", str(idx)],
+                             capture_output=True, text=True, timeout=5).stdout.strip()
+        if out:
+            print(out, flush=True)
+        time.sleep(0.05)
+"""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons of one GPU during a region with
+    read-only NVML queries every few milliseconds (nvidia-smi when NVML is
+    missing). The poller is a child process, so the sampling rate does not
+    depend on the benchmark's own Python thread; the region starts only after
+    the first sample has arrived."""
+
+    PERIOD_S = 0.003
 
     def __init__(self, index: int) -> None:
         self.index = index
         self.rows: list[list[str]] = []
-        self._stop = threading.Event()
-        self._thread: threading.Thread | None = None
-
-    def _query(self):
+        self._proc = None
+        self._reader: threading.Thread | None = None
+        self._first = threading.Event()
+        self.uuid = ""
         try:
-            out = subprocess.run(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-i", str(self.index)],
-                capture_output=True, text=True, timeout=5,
-            ).stdout.strip()
-            if out:
-                self.rows.append([c.strip() for c in out.split(",")])
+            import torch
+
+            u = str(torch.cuda.get_device_properties(index).uuid)
+            self.uuid = u if u.startswith("GPU-") else "GPU-" + u
         except Exception:
             pass
 
-    def _loop(self):
-        while not self._stop.is_set():
-            self._query()
-            self._stop.wait(0.05)
+    def _read(self):
+        for line in self._proc.stdout:
+            self.rows.append([c.strip() for c in line.strip().split(",")])
+            self._first.set()
+        self._first.set()
 
     def __enter__(self):
-        self._thread = threading.Thread(target=self._loop, daemon=True)
-        self._thread.start()
+        try:
+            self._proc = subprocess.Popen(
+                [sys.executable, "-c", _CLOCK_POLLER, str(self.index), self.uuid, str(self.PERIOD_S)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._reader = threading.Thread(target=self._read, daemon=True)
+            self._reader.start()
+            self._first.wait(timeout=60)
+        except Exception:
+            self._proc = None
         return self
 
     def __exit__(self, *exc):
-        self._stop.set()
-        if self._thread:
-            self._thread.join(timeout=10)
-        if not self.rows:
-            self._query()
+        if self._proc is not None:
+            self._proc.terminate()  # the poller this object started, by its own handle
+            try:
+                self._proc.wait(timeout=10)
+            except Exception:
+                self._proc.kill()
+        if self._reader is not None:
+            self._reader.join(timeout=10)
 
     def summary(self) -> dict:
         sm, mx, reasons = [], None, set()
@@ -362,6 +405,20 @@ class ClockSampler:
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
                 "samples": len(sm)}
+
+
+def profiled_traffic(name: str, world: int) -> int | None:
+    """DRAM bytes (read + write) of one launch of the dominant kernel, from
+    the committed ncu summary ``profiles/<name>`` (its
+    ``traffic_bytes_per_launch:`` line, captured on one GPU); a rank of an
+    N-GPU run holds 1/N of the heads, so its launch moves 1/N of them."""
+    p = ROOT / "profiles" / name
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return int(line.split(":", 1)[1]) // max(world, 1)
+    return None
 
 
 def measured_peaks() -> dict:
@@ -572,8 +629,9 @@ def main():
     from qkv_b200.ops import _lib
 
     workspace_splits = _lib.load().qkv_kivi_paged_decode_workspace(w.B, w.Hql, w.Hl, w.D, w.g, w.blk, w.L)
-    # residual-window tail kernel + history kernel (+ combine when split)
-    launches_per_step = 3 if workspace_splits > 0 else 2
+    # the page-pipelined decode kernel (history splits + window CTAs in one
+    # grid), then the combine kernel when the plan has several splits
+    launches_per_step = 2 if workspace_splits > 0 else 1
 
     pack = bench_pack(device) if rank == 0 else None
     int8 = None
@@ -623,7 +681,10 @@ def main():
             "hbm_gbs": achieved,
             "hbm_frac_of_8tbs": achieved / 8000.0,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
+                         "frac": achieved / peak,
+                         "traffic": profiled_traffic("kivi_decode_tma_config5.md", world),
+                         "traffic_source": "profiles/kivi_decode_tma_config5.md (ncu, 1 GPU, scaled 1/N)",
+                         "peak_source": peak_src,
                          "bytes_per_launch": by, "kernel_ms": decode_ms},
             "pack": pack,
             "int8_config3": int8,

@@ -15,6 +15,7 @@ import torch
 
 import qkv_oracle as O
 from qkv_b200.methods.kivi_int4.attention_backend import AscendKiviInt4AttentionBackendMixin
+from qkv_b200.methods.kivi_int4.window import WindowPlanner
 
 
 class _Stub:
@@ -207,3 +208,65 @@ def test_forward_guards():
     impl.enable_kivi = False
     with pytest.raises(RuntimeError, match="kivi_int4 cache dtype"):
         impl.forward(None, out, out, out, None, object(), out)
+
+
+def _plans_equal(a, b):
+    return (a.flush_src == b.flush_src and a.flush_slots == b.flush_slots
+            and a.ring_writes == b.ring_writes and a.compactions == b.compactions)
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_batched_decode_store_matches_per_row_store(seed):
+    """store_one_each (one token per row, vectorised) leaves the same window
+    state and plan as store() called row by row: appends, in-place hits,
+    value evictions at capacity and whole-window key flushes."""
+    rng = np.random.default_rng(seed)
+    rows, cap, g, blk = 6, 8, 8, 16
+    a, b = WindowPlanner(rows, cap, g), WindowPlanner(rows, cap, g)
+    nxt = [int(r) * 4 * blk for r in range(rows)]  # each row owns 4 blocks, aligned start
+    for _ in range(40):
+        pa, pb = a.begin(), b.begin()
+        rs = rng.permutation(rows)[: rng.integers(1, rows + 1)]
+        slots = []
+        for r in rs:
+            if rng.random() < 0.2 and a.key.length[r] > 0:  # rewrite a held slot
+                held = a.key.slots[r][a.key.slots[r] >= 0]
+                slots.append(int(rng.choice(held)))
+            else:
+                slots.append(nxt[r])
+                nxt[r] += 1
+        tok = list(range(len(rs)))
+        for is_key, i in ((True, 0), (False, 1)):
+            for r, sl, t in zip(rs, slots, tok):
+                a.store(pa[i], int(r), [sl], [t], is_key=is_key)
+            b.store_one_each(pb[i], rs, slots, tok, is_key=is_key)
+            assert _plans_equal(pa[i], pb[i])
+        for side in ("key", "value"):
+            sa, sb = getattr(a, side), getattr(b, side)
+            assert np.array_equal(sa.slots, sb.slots)
+            assert np.array_equal(sa.start, sb.start) and np.array_equal(sa.length, sb.length)
+
+
+@pytest.mark.parametrize("seed", range(4))
+def test_batched_liveness_matches_per_row(seed):
+    rng = np.random.default_rng(100 + seed)
+    rows, cap, g, blk = 5, 8, 8, 4
+    pl = WindowPlanner(rows, cap, g)
+    table = rng.permutation(40).reshape(5, 8).astype(np.int64)
+    table[rng.random(table.shape) < 0.1] = -1
+    lens = rng.integers(0, 8 * blk + 1, rows)
+    for r in range(rows):
+        for side in (pl.key, pl.value):
+            n = int(rng.integers(0, cap + 1))
+            st = int(rng.integers(0, cap))
+            pos = np.arange(max(int(lens[r]) - n, 0), int(lens[r]))
+            ids = table[r, pos // blk] * blk + pos % blk
+            if rng.random() < 0.3 and ids.size:
+                ids[rng.integers(0, ids.size)] += 1  # a stale entry
+            side.slots[r].fill(-1)
+            for i, v in enumerate(ids):
+                side.slots[r, (st + i) % cap] = v
+            side.start[r], side.length[r] = st, ids.size
+    want = [pl.expected_live(r, int(lens[r]), table[r], blk) for r in range(rows)]
+    got = pl.expected_live_rows(np.arange(rows), lens, table, blk)
+    assert got.tolist() == want

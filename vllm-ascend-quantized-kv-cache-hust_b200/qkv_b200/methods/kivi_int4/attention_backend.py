@@ -373,6 +373,15 @@ class AscendKiviInt4AttentionBackendMixin:
         self._kivi_begin_plan()
         self._kivi_set_plan_source(key, value)
         n = len(slots_all)
+        if len(qlen) == n and qlen == list(range(1, n + 1)) and min(slots_all) >= 0:
+            # decode step: one token per request, planned for the whole batch
+            rows = [self._get_kivi_residual_row(k, create=True) for k in keys[:n]]
+            tok = list(range(n))
+            self._kivi_planner.store_one_each(self._kivi_plan[0], rows, slots_all, tok, is_key=True,
+                                              on_flush=self._kivi_key_flush_gate)
+            self._kivi_planner.store_one_each(self._kivi_plan[1], rows, slots_all, tok, is_key=False)
+            self._kivi_execute_plan()
+            return
         prev = 0
         for r, q_end in enumerate(qlen):
             q_end = min(int(q_end), n)
@@ -538,7 +547,10 @@ class AscendKiviInt4AttentionBackendMixin:
         bt = np.asarray(bt)
         block_size = self._get_kivi_block_size()
         planner = self._kivi_planner
-        stale = [(i, r) for i, r in rows if not planner.expected_live(r, int(seq_lens[i]), bt[i], block_size)]
+        idx = np.fromiter((i for i, _ in rows), dtype=np.int64, count=len(rows))
+        rws = np.fromiter((r for _, r in rows), dtype=np.int64, count=len(rows))
+        live = planner.expected_live_rows(rws, np.asarray(seq_lens, dtype=np.int64)[idx], bt[idx], block_size)
+        stale = [rows[j] for j in np.flatnonzero(~live)]
         if not stale:
             return
         own_plan = self._kivi_plan is None

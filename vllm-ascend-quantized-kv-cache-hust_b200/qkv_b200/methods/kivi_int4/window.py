@@ -67,14 +67,14 @@ class RingSide:
     def __init__(self, rows: int, capacity: int) -> None:
         self.capacity = capacity
         self.slots = np.full((rows, capacity), -1, dtype=np.int64)
-        self.start = [0] * rows
-        self.length = [0] * rows
+        self.start = np.zeros(rows, dtype=np.int64)
+        self.length = np.zeros(rows, dtype=np.int64)
 
     def lanes(self, row: int) -> list[int]:
-        n = self.length[row]
+        n = int(self.length[row])
         if n <= 0:
             return []
-        s, cap = self.start[row], self.capacity
+        s, cap = int(self.start[row]), self.capacity
         end = s + n
         if end <= cap:
             return list(range(s, end))
@@ -133,7 +133,14 @@ class WindowPlanner:
         side = self.side(is_key)
         cap = self.capacity
         rs = side.slots[row]
-        lane_of = {int(s): lane for lane, s in enumerate(rs.tolist()) if s >= 0}
+        if len(slots) <= 4:  # decode-sized: search the row instead of indexing it
+            lane_of = {}
+            for slot in slots:
+                hit = np.flatnonzero(rs == int(slot))
+                if hit.size:
+                    lane_of[int(slot)] = int(hit[0])
+        else:
+            lane_of = {int(s): lane for lane, s in enumerate(rs.tolist()) if s >= 0}
         base = row * cap
         for slot, t in zip(slots, token_index):
             slot = int(slot)
@@ -161,6 +168,53 @@ class WindowPlanner:
             lane_of[slot] = tail
             self._lane_src[(is_key, base + tail)] = ("new", int(t))
             plan.ring_writes[base + tail] = ("new", int(t))
+
+    def store_one_each(self, plan: SidePlan, rows, slots, token_index, *, is_key: bool,
+                       on_flush=None) -> None:
+        """``store`` of one token per row for a batch of distinct rows (a
+        decode step), vectorised: in-place hits, appends and one-lane value
+        evictions are array operations; a key window that must flush (a full
+        row) takes the per-row path with its alignment gate."""
+        rows = np.asarray(rows, dtype=np.int64)
+        slots = np.asarray(slots, dtype=np.int64)
+        tokens = np.asarray(token_index, dtype=np.int64)
+        if rows.size == 0:
+            return
+        side = self.side(is_key)
+        cap = self.capacity
+        rs = side.slots[rows]                            # [n, cap] (copy)
+        eq = rs == slots[:, None]
+        hit = eq.any(axis=1)
+        full = side.length[rows] >= cap
+        slow = ~hit & full if is_key else np.zeros_like(hit)
+        for i in np.flatnonzero(slow):                   # whole-window key flush
+            self.store(plan, int(rows[i]), [int(slots[i])], [int(tokens[i])], is_key=True, on_flush=on_flush)
+        fast = ~slow
+        # in-place overwrites
+        hit_lane = eq.argmax(axis=1)
+        # value windows at capacity drop their oldest lane first
+        ev = fast & ~hit & full
+        if ev.any():
+            er = rows[ev]
+            ev_lane = side.start[er] % cap
+            ev_slot = side.slots[er, ev_lane]
+            for r, l, sl in zip(er.tolist(), ev_lane.tolist(), ev_slot.tolist()):
+                plan.flush_src.append(self._src_of(is_key, r * cap + l))
+                plan.flush_slots.append(int(sl))
+            side.slots[er, ev_lane] = -1
+            side.length[er] -= 1
+            side.start[er] = np.where(side.length[er] == 0, 0, (side.start[er] + 1) % cap)
+        app = fast & ~hit
+        ar = rows[app]
+        tail = (side.start[ar] + side.length[ar]) % cap
+        side.slots[ar, tail] = slots[app]
+        side.length[ar] += 1
+        lane = np.where(hit, hit_lane, 0)
+        lane[app] = tail
+        for r, l, t in zip(rows[fast].tolist(), lane[fast].tolist(), tokens[fast].tolist()):
+            flat = r * cap + l
+            self._lane_src[(is_key, flat)] = ("new", t)
+            plan.ring_writes[flat] = ("new", t)
 
     def flush_direct(self, plan: SidePlan, slots, token_index) -> None:
         """Records tokens that go straight to the int4 history (bulk prefill)."""
@@ -200,6 +254,30 @@ class WindowPlanner:
         side = self.side(is_key)
         lanes = side.lanes(row)
         return [int(side.slots[row, l]) for l in lanes], lanes
+
+    def expected_live_rows(self, rows, seq_lens, table: np.ndarray, block_size: int) -> np.ndarray:
+        """``expected_live`` for many rows at once; ``table[i]`` is the block
+        table row of ``rows[i]``'s request."""
+        rows = np.asarray(rows, dtype=np.int64)
+        L = np.asarray(seq_lens, dtype=np.int64)
+        ok = np.ones(rows.size, dtype=bool)
+        if rows.size == 0:
+            return ok
+        cap = self.capacity
+        ar = np.arange(cap, dtype=np.int64)
+        table = np.asarray(table, dtype=np.int64)
+        for side in (self.key, self.value):
+            n = side.length[rows]
+            ok &= n <= L
+            valid = ar[None, :] < n[:, None]
+            pos = np.clip(L[:, None] - n[:, None] + ar[None, :], 0, None)
+            col = np.minimum(pos // block_size, table.shape[1] - 1)
+            blocks = np.take_along_axis(table, col, axis=1)
+            want = blocks * block_size + pos % block_size
+            got = side.slots[rows[:, None], (side.start[rows][:, None] + ar[None, :]) % cap]
+            good = (want == got) & (blocks >= 0) & (pos // block_size < table.shape[1])
+            ok &= np.all(good | ~valid, axis=1)
+        return ok
 
     def expected_live(self, row: int, seq_len: int, table_row: np.ndarray, block_size: int) -> bool:
         """Fast check that both windows hold exactly the request's last
