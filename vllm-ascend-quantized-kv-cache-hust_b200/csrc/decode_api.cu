@@ -16,7 +16,7 @@ SplitPlan plan_for(const DecodeParams& p, bool kivi, int max_seq_len);
 SplitPlan plan_generic(const DecodeParams& p, bool kivi, int max_seq_len);
 bool kivi_tma_geometry(const DecodeParams& p);
 bool kivi_tma_supported(const DecodeParams& p);
-SplitPlan plan_kivi_tma(int batch, int kvh, int max_seq_len, int sms);
+SplitPlan plan_kivi_tma(int batch, int kvh, int group, int max_seq_len, int sms);
 int launch_kivi_tma(const DecodeParams& p, cudaStream_t stream);
 
 namespace {
@@ -47,7 +47,7 @@ SplitPlan plan_generic(const DecodeParams& p, bool kivi, int max_seq_len) {
 // Split plan of the kernel a call with these arguments runs.
 SplitPlan plan_for(const DecodeParams& p, bool kivi, int max_seq_len) {
   if (kivi) {
-    if (kivi_tma_supported(p)) return plan_kivi_tma(p.batch, p.kvh, max_seq_len, sm_count());
+    if (kivi_tma_supported(p)) return plan_kivi_tma(p.batch, p.kvh, p.group, max_seq_len, sm_count());
     return plan_generic(p, true, max_seq_len);
   }
   if (decode_mma_supported(p, false))
@@ -94,7 +94,7 @@ size_t qkv_kivi_paged_decode_workspace(int batch, int num_heads,
   size_t a = 0;
   if (kivi_tma_geometry(p))
     a = workspace_bytes(batch, num_heads, head_size,
-                        plan_kivi_tma(batch, num_kv_heads, max_seq_len, sm_count()).total);
+                        plan_kivi_tma(batch, num_kv_heads, group_size, max_seq_len, sm_count()).total);
   const size_t b = workspace_bytes(batch, num_heads, head_size,
                                    plan_generic(p, true, max_seq_len).total);
   return a > b ? a : b;

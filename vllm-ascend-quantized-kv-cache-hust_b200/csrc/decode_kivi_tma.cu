@@ -412,7 +412,7 @@ static_assert(sizeof(float) * (kTailBlock * (kTailLd + kD + kHeads) + 3 * kHeads
 // ------------------------------------------------------------ the kernel
 
 template <int NG>
-__global__ void __launch_bounds__(kThreads, 4)
+__global__ void __launch_bounds__(kThreads, 5)
 kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tmap_k,
                        const __grid_constant__ CUtensorMap tmap_v) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -886,18 +886,24 @@ bool kivi_tma_supported(const DecodeParams& p) {
          al(p.km, 16) && al(p.vs, 8) && al(p.vm, 8);
 }
 
-// CTAs of the page-pipelined kernel resident per SM (shared memory and
-// registers allow 4 for both group sizes).
-int kivi_tma_ctas_per_sm() { return 4; }
+// CTAs of the page-pipelined kernel resident per SM: registers allow 5 (the
+// launch bound), shared memory 5 for group 128 and 4 for group 64.
+int kivi_tma_ctas_per_sm(int group) {
+  constexpr int kSmemPerSm = 228 * 1024, kReservedPerCta = 1024;
+  const int per = static_cast<int>(group == 128 ? sizeof(PageShared<1>) : sizeof(PageShared<2>)) +
+                  kReservedPerCta;
+  const int by_smem = kSmemPerSm / per;
+  return by_smem < 5 ? by_smem : 5;
+}
 
 // Splits chosen for whole waves: among split counts that keep each split
 // within kMaxPages pages, the one whose grid best fills its last wave, with a
 // small charge per split for the partial-state traffic of the combine.
-SplitPlan plan_kivi_tma(int batch, int kvh, int max_seq_len, int sms) {
+SplitPlan plan_kivi_tma(int batch, int kvh, int group, int max_seq_len, int sms) {
   SplitPlan plan;
   const int pages = max_seq_len > 0 ? (max_seq_len + kBlk - 1) / kBlk : 1;
   const int units = batch * kvh > 0 ? batch * kvh : 1;
-  const int resident = sms * kivi_tma_ctas_per_sm();
+  const int resident = sms * kivi_tma_ctas_per_sm(group);
   const int s_min = (pages + kMaxPages - 1) / kMaxPages;
   int s_max = (8 * resident + units - 1) / units;
   s_max = s_max < s_min ? s_min : s_max;
