@@ -16,13 +16,16 @@ for N > 1, by the all-gather. The caches (1.22 GB / N per GPU) exceed the
 
 Reported on one JSON line (rank 0):
   value     tokens/s/layer over all GPUs, inputs resident in HBM, device-timed
-            with CUDA events, max over ranks;
+            with CUDA events, max over ranks; the step is captured once as a
+            CUDA graph (decode + combine [+ all-gather]) and replayed, as a
+            serving loop does;
   roofline  algorithmic bytes per decode call / its CUDA-event time vs the
             measured HBM copy bandwidth (MEASURED_PEAKS.json);
   pack      KIVI pack GB/s (config 2 definition, 5248 B/token);
   e2e       the same metric through the plugin API — the KIVI mixin's
-            ``forward()`` in DecodeOnly state with pinned host q/k/v copied in
-            and the output copied out every step;
+            ``forward()`` in DecodeOnly state with pinned host q/k/v copied in,
+            the heads of all ranks gathered (N > 1) and the output copied out
+            every step;
   cpu_baseline  the reference's CPU path (numpy port in oracle/) on a bounded
             sample of the workload, rank 0, N = 1 only.
 
@@ -283,17 +286,29 @@ def int8_bytes(w) -> int:
 
 
 def time_loop(fn, steps, warmup, device):
+    """ms per call of ``fn`` replayed from a CUDA graph (captured after the
+    warm-up calls), timed with CUDA events."""
     import torch
 
-    for _ in range(max(warmup, 3)):
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for _ in range(max(warmup, 3)):
+            fn()
+    torch.cuda.current_stream(device).wait_stream(side)
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
         fn()
+    graph.replay()
     torch.cuda.synchronize(device)
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
     for _ in range(steps):
-        fn()
+        graph.replay()
     e.record()
     torch.cuda.synchronize(device)
+    del graph
     return s.elapsed_time(e) / steps
 
 
@@ -503,19 +518,29 @@ def e2e_impl(w, device):
     return impl
 
 
-def run_e2e(w, device, steps, warmup):
-    """tokens/s/layer through the plugin API with host buffers in the loop."""
+def run_e2e(w, device, steps, warmup, world=1, rank=0):
+    """tokens/s/layer through the plugin API with host buffers in the loop:
+    per step, pinned q/k/v of this rank's heads go in, the mixin's forward
+    runs (window planning, packs, decode), N > 1 gathers every rank's heads
+    with ``qkv_b200.distributed.gather_heads``, and the full output comes back
+    to the host."""
     import torch
+    import torch.distributed as dist
+
+    from qkv_b200.distributed import HeadShard, gather_heads
 
     impl = e2e_impl(w, device)
     B, Hq, H, D = w.B, w.Hql, w.Hl, w.D
+    shard = HeadShard(rank, world, num_kv_heads=H * world, num_heads=Hq * world)
+    g_buf = torch.empty(world * B, Hq, D, dtype=torch.bfloat16, device=device) if world > 1 else None
+    full = torch.empty(B, Hq * world, D, dtype=torch.bfloat16, device=device)
     bt_host = w.bt.numpy()
     total = steps + warmup
     gen = torch.Generator().manual_seed(7)
     q_h = torch.randn(total, B, Hq, D, generator=gen).to(torch.bfloat16).pin_memory()
     k_h = torch.randn(total, B, H, D, generator=gen).to(torch.bfloat16).pin_memory()
     v_h = torch.randn(total, B, H, D, generator=gen).to(torch.bfloat16).pin_memory()
-    out_h = torch.empty(B, Hq, D, dtype=torch.bfloat16).pin_memory()
+    out_h = torch.empty(B, Hq * world, D, dtype=torch.bfloat16).pin_memory()
     bt_pinned = w.bt.clone().pin_memory()
     lens = [w.L] * B
     names = [f"req{b}" for b in range(B)]
@@ -535,18 +560,22 @@ def run_e2e(w, device, steps, warmup):
         md.slot_mapping = md.slot_mapping.to(device, non_blocking=True)
         out = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=device)
         impl.forward(None, q, k, v, (w.kbuf, w.vbuf), md, out)
-        out_h.copy_(out, non_blocking=True)
+        res = gather_heads(out, shard, gathered=g_buf, out=full)
+        out_h.copy_(res, non_blocking=True)
 
     for i in range(warmup):
         step(i)
     torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+        torch.cuda.synchronize(device)
     t0 = time.perf_counter()
     for i in range(warmup, total):
         step(i)
     torch.cuda.synchronize(device)
     dt = (time.perf_counter() - t0) / max(steps, 1)
     h2d = B * (Hq + 2 * H) * D * 2 + B * 8 + B * 5 * 4 + B * 4 + w.bt.numel() * 4
-    d2h = B * Hq * D * 2
+    d2h = B * Hq * world * D * 2
     return dt, h2d, d2h
 
 
@@ -595,18 +624,38 @@ def main():
         print(json.dumps({"only": "kivi", "batch": w.B, "decode_ms": decode_ms,
                           "gbs": algorithmic_bytes(w) / (decode_ms * 1e-3) / 1e9}), flush=True)
         return
-    for _ in range(max(args.warmup, 3)):
-        step()
+    # warm-up on a side stream (allocator, NCCL communicators, kernel
+    # attributes), then one decode step (decode + combine [+ all-gather])
+    # captured as a CUDA graph: the serving loop replays it, so the timed
+    # region measures the device, not Python's launch rate
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for _ in range(max(args.warmup, 3)):
+            step()
+    torch.cuda.current_stream(device).wait_stream(side)
     torch.cuda.synchronize(device)
-    if world > 1:
-        dist.barrier()
+    step_graph, decode_graph = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(step_graph):
+        step()
+    with torch.cuda.graph(decode_graph):
+        decode()
+    for _ in range(3):
+        step_graph.replay()
+    torch.cuda.synchronize(device)
     sampler = ClockSampler(local)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with sampler:
+        # every rank's clock poller is live before the barrier, so the ranks
+        # enter the timed region together (a late rank would otherwise show
+        # up as all-gather wait time on the others)
         torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier()
+            torch.cuda.synchronize(device)
         start.record()
         for _ in range(args.steps):
-            step()
+            step_graph.replay()
         end.record()
         torch.cuda.synchronize(device)
     if world > 1:
@@ -617,10 +666,12 @@ def main():
     torch.cuda.synchronize(device)
     ks.record()
     for _ in range(args.steps):
-        decode()
+        decode_graph.replay()
     ke.record()
     torch.cuda.synchronize(device)
     decode_ms = ks.elapsed_time(ke) / args.steps
+    # graphs holding NCCL work are released before the process group goes
+    del step_graph, decode_graph
     t = torch.tensor([ms, decode_ms], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -639,7 +690,7 @@ def main():
         int8 = run_int8_leg(cfg3, rank, world, device, args)
     e2e_dt, h2d, d2h = (None, 0, 0)
     if args.e2e_steps > 0:
-        e2e_dt, h2d, d2h = run_e2e(w, device, args.e2e_steps, 3)
+        e2e_dt, h2d, d2h = run_e2e(w, device, args.e2e_steps, 3, world, rank)
         t = torch.tensor([e2e_dt], dtype=torch.float64, device=device)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
