@@ -8,16 +8,16 @@
 namespace qkv {
 
 int launch_decode_generic(const DecodeParams& p, int mode, cudaStream_t stream);
-// Returns QKV_ERR_UNSUPPORTED (without recording an error) when the geometry
-// has no tensor-core kernel; the caller then runs the generic kernel.
-int launch_decode_mma(const DecodeParams& p, bool kivi, cudaStream_t stream);
-bool decode_mma_supported(const DecodeParams& p, bool kivi);
 SplitPlan plan_for(const DecodeParams& p, bool kivi, int max_seq_len);
 SplitPlan plan_generic(const DecodeParams& p, bool kivi, int max_seq_len);
 bool kivi_tma_geometry(const DecodeParams& p);
 bool kivi_tma_supported(const DecodeParams& p);
 SplitPlan plan_kivi_tma(int batch, int kvh, int group, int max_seq_len, int sms);
 int launch_kivi_tma(const DecodeParams& p, cudaStream_t stream);
+bool int8_tma_geometry(const DecodeParams& p);
+bool int8_tma_supported(const DecodeParams& p);
+SplitPlan plan_int8_tma(int batch, int kvh, int max_seq_len, int sms);
+int launch_int8_tma(const DecodeParams& p, cudaStream_t stream);
 
 namespace {
 
@@ -50,8 +50,7 @@ SplitPlan plan_for(const DecodeParams& p, bool kivi, int max_seq_len) {
     if (kivi_tma_supported(p)) return plan_kivi_tma(p.batch, p.kvh, p.group, max_seq_len, sm_count());
     return plan_generic(p, true, max_seq_len);
   }
-  if (decode_mma_supported(p, false))
-    return plan_splits(p.batch, p.kvh, p.blk, max_seq_len, false, sm_count(), 2, 1024);
+  if (int8_tma_supported(p)) return plan_int8_tma(p.batch, p.kvh, max_seq_len, sm_count());
   return plan_generic(p, false, max_seq_len);
 }
 
@@ -72,8 +71,14 @@ size_t qkv_int8_paged_decode_workspace(int batch, int num_heads,
   p.gqa = num_heads / num_kv_heads;
   p.blk = block_size;
   p.group = head_size;
-  const SplitPlan plan = plan_for(p, false, max_seq_len);
-  return workspace_bytes(batch, num_heads, head_size, plan.total);
+  // the larger of the two kernels' plans: the call may take either path
+  size_t a = 0;
+  if (int8_tma_geometry(p))
+    a = workspace_bytes(batch, num_heads, head_size,
+                        plan_int8_tma(batch, num_kv_heads, max_seq_len, sm_count()).total);
+  const size_t b = workspace_bytes(batch, num_heads, head_size,
+                                   plan_generic(p, false, max_seq_len).total);
+  return a > b ? a : b;
 }
 
 size_t qkv_kivi_paged_decode_workspace(int batch, int num_heads,
@@ -155,8 +160,8 @@ int qkv_int8_paged_decode(const void* query, int64_t q_stride,
                              head_size;
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (decode_mma_supported(p, false)) return launch_decode_mma(p, false, s);
-  return launch_decode_generic(p, kInt8Pages, s);
+  if (int8_tma_supported(p)) return launch_int8_tma(p, s);
+  return launch_decode_generic(p, kInt8Pages, s);  // planned for it by plan_for
 }
 
 int qkv_kivi_paged_decode(
