@@ -55,6 +55,8 @@ CONFIG5 = dict(batch=32, context=32768, num_heads=64, num_kv_heads=8, head_size=
                residual=128, block_size=128)
 CONFIG2_PACK = dict(tokens=8192, num_kv_heads=8, head_size=128, group_size=128, block_size=128)
 CONFIG3 = dict(batch=64, context=8192, num_heads=32, num_kv_heads=8, head_size=128, block_size=128)
+CONFIG4 = dict(num_heads=32, num_kv_heads=8, head_size=128, group_size=64, residual=128, block_size=128,
+               chunk=2048, cached=6144, prefills=2, decodes=30, decode_min=2048, decode_max=16384)
 
 
 def parse():
@@ -68,7 +70,7 @@ def parse():
     ap.add_argument("--no-int8", action="store_true", help="skip the config-3 INT8 leg")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the request count (small cases for ncu captures)")
-    ap.add_argument("--only", choices=("kivi", "int8"), default=None,
+    ap.add_argument("--only", choices=("kivi", "int8", "config4"), default=None,
                     help="run just one decode kernel loop (for ncu captures)")
     return ap.parse_args()
 
@@ -238,6 +240,159 @@ def build_workload(cfg, rank, world, device, seed=1234):
         state=state, seq_lens=torch.full((B,), L, dtype=torch.int32, device=device), hist=hist, res=res,
         B=B, L=L, Hl=Hl, Hql=Hql, D=D, g=g, r=r, blk=blk, nb=nb, pages=pages,
     )
+
+
+def build_config4(cfg, device, seed=1004):
+    """Config 4 (chunked prefill mixed with decode, KIVI g 64): 2 requests
+    whose 2048-token chunk lands on 6144 cached tokens (history 8192 after the
+    chunk's write) and 30 decode requests at L ~ U{2048..16384}, every cache
+    in the state the reference's writes leave (int4 history + bf16 window),
+    K/V ~ N(0,1) bf16 with x10 key outliers on 2% of (head, channel) pairs."""
+    import torch
+
+    from qkv_b200.methods.kivi_int4.byte_cache import KiviByteCacheLayout, kivi_caches_from_byte_tensors
+    from qkv_b200.ops import kivi_pack_key_cache, kivi_pack_value_cache
+
+    Hq, H, D, g, r, blk = (cfg[k] for k in ("num_heads", "num_kv_heads", "head_size", "group_size", "residual",
+                                           "block_size"))
+    cpu_gen = torch.Generator().manual_seed(seed)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    lens = [cfg["cached"] + cfg["chunk"]] * cfg["prefills"] + torch.randint(
+        cfg["decode_min"], cfg["decode_max"] + 1, (cfg["decodes"],), generator=cpu_gen).tolist()
+    B = len(lens)
+    pages = [(L + blk - 1) // blk for L in lens]
+    maxp = max(pages)
+    nb = sum(pages) + 1
+    lay = KiviByteCacheLayout(num_blocks=nb, block_size=blk, num_kv_heads=H, head_size=D, group_size=g)
+    kbuf = torch.zeros(nb, blk, H, lay.bytes_per_token_head, dtype=torch.uint8, device=device)
+    vbuf = torch.zeros_like(kbuf)
+    views = kivi_caches_from_byte_tensors(kbuf, vbuf, lay)
+    perm = torch.randperm(nb, generator=cpu_gen)
+    bt = torch.zeros(B, maxp, dtype=torch.int32)
+    kscale = torch.ones(H * D)
+    kscale[torch.randperm(H * D, generator=cpu_gen)[:max(1, int(0.02 * H * D))]] = 10.0
+    kscale = kscale.view(H, D).to(device)
+    rk = torch.zeros(B + 1, r, H, D, dtype=torch.bfloat16, device=device)
+    rv = torch.zeros_like(rk)
+    state = []
+    cur = 0
+    for b, L in enumerate(lens):
+        bt[b, :pages[b]] = perm[cur:cur + pages[b]].to(torch.int32)
+        cur += pages[b]
+        hist = ((L - 1) // r) * r
+        res = L - hist
+        k = (torch.randn(L, H, D, generator=gen, device=device) * kscale).to(torch.bfloat16)
+        v = torch.randn(L, H, D, generator=gen, device=device).to(torch.bfloat16)
+        pos = torch.arange(L, device=device)
+        slots = bt[b].to(device).long()[pos // blk] * blk + pos % blk
+        kivi_pack_key_cache(k[:hist].contiguous(), slots[:hist].contiguous(), *views[:3], g, validate_slots=False)
+        kivi_pack_value_cache(v[:hist].contiguous(), slots[:hist].contiguous(), *views[3:], g)
+        rk[b, :res] = k[hist:]
+        rv[b, :res] = v[hist:]
+        state.append([b, 0, res, 0, res, L])
+    torch.cuda.synchronize(device)
+    P, C = cfg["prefills"], cfg["chunk"]
+    # query token i of a chunk attends to its causal length
+    rows_len = [lens[b] - C + i + 1 for b in range(P) for i in range(C)]
+    dec = list(range(P, B))
+    st = torch.tensor(state, dtype=torch.int32)
+    kv_pre = lens[:P]
+    cu = lambda ns: torch.tensor([0] + torch.tensor(ns).cumsum(0).tolist(), dtype=torch.int32, device=device)
+    return SimpleNamespace(
+        views=views, rk=rk, rv=rv, g=g, D=D, H=H, Hq=Hq, blk=blk, lens=lens,
+        # chunk requests: dense K/V gathered from int4 pages + windows, then
+        # prompt attention aligned to the end of each request's keys
+        q_pre=torch.randn(P * C, Hq, D, generator=gen, device=device).to(torch.bfloat16),
+        q_lens_pre=[C] * P, kv_pre=kv_pre, cu_q_pre=cu([C] * P), cu_k_pre=cu(kv_pre),
+        bt_pre=bt[:P].to(device), len_pre=torch.tensor(kv_pre, dtype=torch.int32, device=device),
+        st_pre=st[:P].to(device),
+        dk=torch.empty(sum(kv_pre), H, D, dtype=torch.bfloat16, device=device),
+        dv=torch.empty(sum(kv_pre), H, D, dtype=torch.bfloat16, device=device),
+        q_dec=torch.randn(len(dec), Hq, D, generator=gen, device=device).to(torch.bfloat16),
+        bt_dec=bt[dec].to(device), len_dec=torch.tensor([lens[b] for b in dec], dtype=torch.int32, device=device),
+        st_dec=st[dec].to(device), max_dec=max(lens[b] for b in dec),
+        # work: 2 FLOP per multiply-add, QK and PV, every prefill row over its causal length
+        prefill_flops=4 * Hq * D * sum(rows_len),
+        # gather: int4 codes + group scale/min read (history), bf16 window
+        # read, bf16 dense K and V written
+        gather_bytes=sum(gather_bytes(L, H, D, g, r) for L in kv_pre),
+        decode_bytes=sum(request_decode_bytes(lens[b], H, Hq, D, g, r, blk) for b in dec),
+    )
+
+
+def gather_bytes(L, H, D, g, r):
+    """Algorithmic bytes of one request's dense gather: the int4 history with
+    its per-group scale/min on both sides, the bf16 windows, and the bf16
+    dense K and V written."""
+    hist = ((L - 1) // r) * r
+    res = L - hist
+    return H * (2 * hist * (D // 2 + 8 * D // g) + 2 * res * D * 2 + 2 * L * D * 2)
+
+
+def request_decode_bytes(L, H, Hq, D, g, r, blk):
+    """Algorithmic bytes of one request's decode attention: int4 codes and
+    per-group scale/min of the history on both sides, the bf16 windows, q,
+    out and the block-table row."""
+    hist = ((L - 1) // r) * r
+    res = L - hist
+    return H * (2 * hist * (D // 2 + 8 * D // g) + 2 * res * D * 2) + 2 * Hq * D * 2 + 4 * ((L + blk - 1) // blk)
+
+
+def run_config4_leg(device, args):
+    """Config 4 through the path the mixin takes (ChunkedPrefill with
+    history): the chunk requests gather dense K/V from the int4 pages and the
+    windows and run the tcgen05 prompt attention; the decode rows run the
+    paged decode kernel. TFLOP/s of the prompt attention against the measured
+    bf16 tensor peak, GB/s of the gather and the decode rows against HBM."""
+    import torch
+
+    from qkv_b200.ops import dense_prefill, kivi_dequant_gather, kivi_paged_decode
+
+    c = build_config4(CONFIG4, device)
+    out_pre = torch.empty_like(c.q_pre)
+    out_dec = torch.empty_like(c.q_dec)
+    sc = c.D ** -0.5
+
+    def gather():
+        kivi_dequant_gather(c.views, c.rk, c.rv, c.bt_pre, c.kv_pre, c.st_pre, c.g, out_key=c.dk, out_value=c.dv,
+                            cu_seqlens=c.cu_k_pre, seq_lens_device=c.len_pre)
+
+    def attend():
+        dense_prefill(c.q_pre, c.dk, c.dv, c.q_lens_pre, c.kv_pre, sc, out_pre, causal=True,
+                      cu_seqlens_q=c.cu_q_pre, cu_seqlens_k=c.cu_k_pre)
+
+    def prefill():
+        gather()
+        attend()
+
+    def decode():
+        kivi_paged_decode(c.q_dec, c.views, c.rk, c.rv, c.bt_dec, c.len_dec, c.st_dec, c.g, sc, out_dec, c.max_dec)
+
+    def step():
+        prefill()
+        decode()
+
+    steps = max(3, min(args.steps, 50))
+    ms_gather = time_loop(gather, steps, 3, device)
+    ms_attn = time_loop(attend, steps, 3, device)
+    ms_pre = time_loop(prefill, steps, 3, device)
+    ms_dec = time_loop(decode, args.steps, args.warmup, device)
+    ms_step = time_loop(step, steps, 3, device)
+    peaks = measured_peaks()
+    tf_peak = peaks.get("bf16_tflops") or 1590.0
+    hbm = peaks.get("hbm_gbs") or 6650.0
+    tflops = c.prefill_flops / (ms_attn * 1e-3) / 1e12
+    gbs = c.decode_bytes / (ms_dec * 1e-3) / 1e9
+    gather_gbs = c.gather_bytes / (ms_gather * 1e-3) / 1e9
+    tokens = len(c.q_lens_pre) * c.q_lens_pre[0] + c.q_dec.shape[0]
+    return {"workload": "BASELINE config 4: 2 x 2048-token chunks on 6144 cached + 30 decodes, KIVI g 64, Hq 32 / KVH 8",
+            "step_ms": ms_step, "step_tokens": tokens, "step_tokens_per_s": tokens / (ms_step * 1e-3),
+            "prefill_ms": ms_pre, "prefill_path": "qkv_kivi_dequant_gather + tcgen05 qkv_dense_prefill",
+            "gather_ms": ms_gather, "gather_bytes": c.gather_bytes, "gather_gbs": gather_gbs,
+            "gather_frac_of_hbm": gather_gbs / hbm,
+            "attn_ms": ms_attn, "prefill_flops": c.prefill_flops, "prefill_tflops": tflops,
+            "prefill_frac_of_bf16_peak": tflops / tf_peak,
+            "decode_ms": ms_dec, "decode_bytes": c.decode_bytes, "decode_gbs": gbs, "decode_frac_of_hbm": gbs / hbm}
 
 
 def build_int8_workload(cfg, rank, world, device, seed=4321):
@@ -604,6 +759,9 @@ def main():
         cfg["batch"] = cfg3["batch"] = args.batch
     if args.only == "int8":
         run_only_int8(cfg3, rank, world, device, args)
+        return
+    if args.only == "config4":
+        print(json.dumps({"only": "config4", **run_config4_leg(device, args)}), flush=True)
         return
     w = build_workload(cfg, rank, world, device)
     out = torch.empty(w.B, w.Hql, w.D, dtype=torch.bfloat16, device=device)

@@ -243,13 +243,35 @@ QKV_API size_t qkv_dense_prefill_workspace(int total_q, int num_heads,
  * methods/kivi_int4/semantics.py:285-299).
  *   query, out     bf16 [total_q, num_heads, head_size]
  *   key, value     bf16 [cu_seqlens_k[num_reqs], num_kv_heads, head_size]
- *   cu_seqlens_*   int32 [num_reqs + 1], cu[0] = 0 */
+ *   cu_seqlens_*   int32 [num_reqs + 1], cu[0] = 0
+ *   total_k        cu_seqlens_k[num_reqs] (the rows of key / value)
+ * Head size 128 with num_heads / num_kv_heads in {1, 2, 4, 8} runs on the
+ * tcgen05 tensor cores (no workspace); other geometries on CUDA cores. */
 QKV_API int qkv_dense_prefill(const void* query, const void* key, const void* value,
                       const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
-                      int num_reqs, int total_q, int num_heads,
+                      int num_reqs, int total_q, int total_k, int num_heads,
                       int num_kv_heads, int head_size, int causal,
                       int max_kv_len, float scale, void* workspace,
                       size_t workspace_bytes, void* out, qkv_stream_t stream);
+
+/* Dense bf16 K/V of whole requests from the KIVI int4 pages and the bf16
+ * residual windows: kivi_dequant_gather_cache (ops/kivi_gather.py:36-156) +
+ * the residual overwrite of _gather_dequant_kivi_paged_cache
+ * (methods/kivi_int4/attention_backend.py:849-935). Position t of request b
+ * (t < seq_lens[b]) lands in row cu_seqlens_k[b] + t of out_key / out_value
+ * bf16 [total_k, num_kv_heads, head_size]; a history element is
+ * bf16(code * scale + mn) with the product and sum rounded in fp32, a window
+ * element is copied. Views, windows, block table and res_state as for
+ * qkv_kivi_paged_decode (res_state may be NULL: no windows). */
+QKV_API int qkv_kivi_dequant_gather(
+    const int32_t* k_quant, const float* k_scale, const float* k_mn,
+    const int32_t* v_quant, const float* v_scale, const float* v_mn,
+    const void* res_key, const void* res_value, int res_rows, int res_capacity,
+    const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
+    const int32_t* cu_seqlens_k, const int32_t* res_state, int batch,
+    int num_kv_heads, int head_size, int group_size, int block_size,
+    int64_t num_blocks, int total_k, void* out_key, void* out_value,
+    qkv_stream_t stream);
 
 #ifdef __cplusplus
 }

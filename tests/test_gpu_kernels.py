@@ -384,3 +384,119 @@ def test_dense_prefill_vs_oracle(q_lens, kv_lens, Hq, H, D, causal):
     dense_prefill(bf16_tensor(q), bf16_tensor(k), bf16_tensor(v), q_lens, kv_lens, scale, out, causal=causal)
     want = O.dense_attention(q, k, v, q_lens, kv_lens, scale, causal=causal)
     assert_attention_close(to_np(out), want)
+
+
+# ------------------------------------------------- tensor-core prompt attention
+
+
+@pytest.mark.parametrize("q_lens,kv_lens,Hq,H,causal", [
+    ([64, 1, 300], [1000, 513, 4096], 32, 8, True),  # chunks over history, 4 query heads per KV head
+    ([17, 129], [2017, 129], 64, 8, True),  # 8 per KV head: 16-token tiles
+    ([100], [257], 16, 8, False),  # 2 per KV head, no mask
+    ([128, 127, 129, 3], [128, 127, 129, 3], 8, 8, True),  # 1 per KV head: tile edges
+    ([2048], [2048], 40, 5, True),  # one long prompt
+    ([0, 5, 0], [7, 9, 0], 32, 8, True),  # empty requests between live ones
+])
+def test_dense_prefill_tensor_core_vs_oracle(q_lens, kv_lens, Hq, H, causal):
+    """Head 128 with 1, 2, 4 or 8 query heads per KV head runs the tcgen05
+    kernel (S and O in tensor memory, P in bf16 through shared memory)."""
+    from qkv_b200.ops import dense_prefill
+
+    rng = np.random.default_rng(sum(q_lens) + sum(kv_lens))
+    D = 128
+    q = O.bf16_round(rng.standard_normal((sum(q_lens), Hq, D)).astype(np.float32))
+    k = kv_data(rng, sum(kv_lens), H, D, 0.02, 5.0)
+    v = kv_data(rng, sum(kv_lens), H, D, 0.0, 1.0)
+    scale = D ** -0.5
+    out = torch.full((sum(q_lens), Hq, D), float("nan"), dtype=torch.bfloat16, device=dev())
+    dense_prefill(bf16_tensor(q), bf16_tensor(k), bf16_tensor(v), q_lens, kv_lens, scale, out, causal=causal)
+    want = O.dense_attention(q, k, v, q_lens, kv_lens, scale, causal=causal)
+    assert_attention_close(to_np(out), want)
+    assert_no_device_error()
+
+
+def test_dense_prefill_tensor_core_is_deterministic_at_config4_scale():
+    """The config-4 chunk shape (512-token chunks over 16k keys, GQA 4): two
+    runs give identical bits, rows of a request with the same prefix of keys
+    agree with a shorter causal run, and the last row matches the oracle."""
+    from qkv_b200.ops import dense_prefill
+
+    rng = np.random.default_rng(4)
+    Hq, H, D, ql, kl = 32, 8, 128, 512, 16384
+    q = bf16_tensor(O.bf16_round(rng.standard_normal((2 * ql, Hq, D)).astype(np.float32)))
+    kn = kv_data(rng, 2 * kl, H, D, 0.02, 5.0)
+    vn = kv_data(rng, 2 * kl, H, D, 0.0, 1.0)
+    k, v = bf16_tensor(kn), bf16_tensor(vn)
+    outs = []
+    for _ in range(2):
+        o = torch.empty(2 * ql, Hq, D, dtype=torch.bfloat16, device=dev())
+        dense_prefill(q, k, v, [ql, ql], [kl, kl], D ** -0.5, o, causal=True)
+        outs.append(o)
+    assert torch.equal(outs[0], outs[1])
+    # request 1 alone, cut to its first 100 queries over the first kl - ql + 100 keys
+    n = 100
+    short = torch.empty(n, Hq, D, dtype=torch.bfloat16, device=dev())
+    dense_prefill(q[ql:ql + n].contiguous(), k[kl:2 * kl - ql + n].contiguous(), v[kl:2 * kl - ql + n].contiguous(),
+                  [n], [kl - ql + n], D ** -0.5, short, causal=True)
+    assert_attention_close(to_np(short), to_np(outs[0][ql:ql + n]), 2e-3)
+    qn = to_np(q)
+    want = O.dense_attention(qn[2 * ql - 1:2 * ql], kn[kl:], vn[kl:], [1], [kl], D ** -0.5, causal=True)
+    assert_attention_close(to_np(outs[0][2 * ql - 1:2 * ql]), want)
+    assert_no_device_error()
+
+
+# ------------------------------------------------------------- KIVI dense gather
+
+
+@pytest.mark.parametrize("lens,k_res,v_res,H,D,g,blk,cap", [
+    ([1024, 3000, 5, 8192], [128, 1, 5, 0], [128, 128, 5, 0], 8, 128, 128, 128, 128),
+    ([6144, 2100, 1], [16, 128, 0], [128, 37, 1], 8, 128, 64, 128, 128),
+    ([40, 77], [8, 5], [16, 16], 2, 32, 8, 16, 16),  # reference toy geometry
+    ([300, 1000], [64, 100], [128, 128], 1, 256, 128, 128, 128),
+])
+def test_kivi_dequant_gather_bit_exact(lens, k_res, v_res, H, D, g, blk, cap):
+    """Dense K/V from int4 pages + bf16 windows equal the reference gather
+    (fp32 q * scale + mn, one bf16 rounding) with the window overwrite."""
+    from qkv_b200.ops import kivi_dequant_gather
+
+    rng = np.random.default_rng(sum(lens) + D)
+    views, bt, res_k, res_v, state = _kivi_decode_case(rng, lens, k_res, v_res, H, H, D, g, blk, cap)
+    B = len(lens)
+    tv = tuple(torch.from_numpy(x).to(dev()) for x in views)
+    dk, dv = kivi_dequant_gather(tv, bf16_tensor(res_k), bf16_tensor(res_v), torch.from_numpy(bt).to(dev()),
+                                 lens, torch.from_numpy(state).to(dev()), g)
+    kw = [[res_k[state[b, 0], (state[b, 1] + i) % cap] for i in range(k_res[b])] or None for b in range(B)]
+    vw = [[res_v[state[b, 0], (state[b, 3] + i) % cap] for i in range(v_res[b])] or None for b in range(B)]
+    wk, wv = O.kivi_dequant_gather(*views, bt, lens, g, target_bf16=True)
+    wk, wv = O.overwrite_residual_tail(wk, wv, lens, kw, vw)
+    assert np.array_equal(to_np(dk).view(np.uint32), wk.astype(np.float32).view(np.uint32))
+    assert np.array_equal(to_np(dv).view(np.uint32), wv.astype(np.float32).view(np.uint32))
+    # without window state every position comes from the pages
+    dk0, _ = kivi_dequant_gather(tv, None, None, torch.from_numpy(bt).to(dev()), lens, None, g)
+    nk, _ = O.kivi_dequant_gather(*views, bt, lens, g, target_bf16=True)
+    assert np.array_equal(to_np(dk0).view(np.uint32), nk.astype(np.float32).view(np.uint32))
+    assert_no_device_error()
+
+
+def test_kivi_history_chunk_via_gather_matches_oracle():
+    """A 64-token chunk over 3000 cached positions: gather + tensor-core
+    attention equals the oracle's dequantise-then-attend (cast to bf16 as the
+    reference's gather does)."""
+    from qkv_b200.ops import dense_prefill, kivi_dequant_gather
+
+    rng = np.random.default_rng(64)
+    lens, k_res, v_res, Hq, H, D, g, blk, cap = [3000, 700], [100, 64], [128, 128], 32, 8, 128, 128, 128, 128
+    views, bt, res_k, res_v, state = _kivi_decode_case(rng, lens, k_res, v_res, Hq, H, D, g, blk, cap)
+    ql = [64, 33]
+    q = O.bf16_round(rng.standard_normal((sum(ql), Hq, D)).astype(np.float32))
+    tv = tuple(torch.from_numpy(x).to(dev()) for x in views)
+    dk, dv = kivi_dequant_gather(tv, bf16_tensor(res_k), bf16_tensor(res_v), torch.from_numpy(bt).to(dev()),
+                                 lens, torch.from_numpy(state).to(dev()), g)
+    out = torch.empty(sum(ql), Hq, D, dtype=torch.bfloat16, device=dev())
+    dense_prefill(bf16_tensor(q), dk, dv, ql, lens, D ** -0.5, out, causal=True)
+    kw = [[res_k[state[b, 0], (state[b, 1] + i) % cap] for i in range(k_res[b])] for b in range(2)]
+    vw = [[res_v[state[b, 0], (state[b, 3] + i) % cap] for i in range(v_res[b])] for b in range(2)]
+    wk, wv = O.kivi_dequant_gather(*views, bt, lens, g, target_bf16=True)
+    wk, wv = O.overwrite_residual_tail(wk, wv, lens, kw, vw)
+    assert_attention_close(to_np(out), O.dense_attention(q, wk, wv, ql, lens, D ** -0.5, causal=True))
+    assert_no_device_error()

@@ -132,3 +132,48 @@ def test_mixin_on_host_byte_buffers_matches_six_views(golden):
     impl2.forward(None, q, k, v, (kbuf, vbuf), md, o2)
     assert torch.equal(o1, o2)
     assert kbuf.any() and vbuf.any()
+
+
+def test_mixin_chunk_over_history_matches_oracle():
+    """Prefill chunks on cached tokens next to a single-token row (head 128,
+    4 query heads per KV head): chunks run gather + tensor-core attention, the
+    single row the paged decode kernel; every output row matches the oracle's
+    dequantise-to-bf16-then-attend over the cache state after the write."""
+    import qkv_oracle as O
+
+    dev = torch.device("cuda", 0)
+    head, kvh, group, block, residual, nb, num_heads = 128, 8, 128, 128, 128, 64, 32
+    impl, six = make_impl({"geometry": np.array([head, kvh, group, block, residual, nb, num_heads])}, dev)
+    impl._bind_kivi_cache(six)
+    rng = np.random.default_rng(3)
+    reqs, prompt, ql = ["a", "b", "c"], [1000, 300, 777], [64, 1, 40]
+    bt = torch.arange(48, dtype=torch.int32).reshape(3, 16)
+    bf = lambda *s: torch.from_numpy(O.bf16_round(rng.standard_normal(s).astype(np.float32))).to(dev).bfloat16()
+
+    def slots(b, lo, hi):
+        return torch.tensor([int(bt[b, p // block]) * block + p % block for p in range(lo, hi)], device=dev)
+
+    for b, n in enumerate(prompt):
+        impl._write_kivi_prefill_cache(bf(n, kvh, head), bf(n, kvh, head), slots(b, 0, n), [reqs[b]], [n])
+    lens = [p + n for p, n in zip(prompt, ql)]
+    T = sum(ql)
+    q, k, v = bf(T, num_heads, head), bf(T, kvh, head), bf(T, kvh, head)
+    md = SimpleNamespace(
+        attn_state=SimpleNamespace(name="PrefillCacheHit"), actual_seq_lengths_q=np.cumsum(ql).tolist(),
+        seq_lens_list=lens, slot_mapping=torch.cat([slots(b, prompt[b], lens[b]) for b in range(3)]),
+        block_tables=bt.to(dev), req_ids=reqs, num_actual_tokens=T, causal=True, finished_req_ids=None,
+    )
+    out = torch.full((T, num_heads, head), float("nan"), dtype=torch.bfloat16, device=dev)
+    impl.forward(None, q, k, v, six, md, out)
+    views = [t.cpu().numpy() for t in six]
+    wins = {}
+    for tag, is_key in (("k", True), ("v", False)):
+        wins[tag] = []
+        for r in reqs:
+            _, data = impl._collect_kivi_residual_window(r, is_key=is_key)
+            wins[tag].append(None if data is None or len(data) == 0 else data.float().cpu().numpy())
+    dk, dv = O.kivi_dequant_gather(*views, bt.numpy(), lens, group, target_bf16=True)
+    dk, dv = O.overwrite_residual_tail(dk, dv, lens, wins["k"], wins["v"])
+    want = O.dense_attention(q.float().cpu().numpy(), dk, dv, ql, lens, head ** -0.5, causal=True)
+    err = np.abs(out.float().cpu().numpy() - want).max()
+    assert err <= ATOL, err

@@ -18,6 +18,14 @@ bool int8_tma_geometry(const DecodeParams& p);
 bool int8_tma_supported(const DecodeParams& p);
 SplitPlan plan_int8_tma(int batch, int kvh, int max_seq_len, int sms);
 int launch_int8_tma(const DecodeParams& p, cudaStream_t stream);
+bool prefill_tc_supported(int head_size, int gqa, const void* q, const void* k, const void* v,
+                          const void* out);
+int launch_prefill_tc(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v,
+                      const int32_t* cu_q, const int32_t* cu_k, int num_reqs, int total_q, int total_k,
+                      int num_heads, int kvh, int causal, float scale, __nv_bfloat16* out,
+                      cudaStream_t stream);
+int launch_kivi_gather(const DecodeParams& p, const int32_t* cu_k, int total_k, __nv_bfloat16* dense_k,
+                       __nv_bfloat16* dense_v, cudaStream_t stream);
 
 namespace {
 
@@ -251,12 +259,12 @@ size_t qkv_dense_prefill_workspace(int total_q, int num_heads,
 
 int qkv_dense_prefill(const void* query, const void* key, const void* value,
                       const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
-                      int num_reqs, int total_q, int num_heads,
+                      int num_reqs, int total_q, int total_k, int num_heads,
                       int num_kv_heads, int head_size, int causal,
                       int max_kv_len, float scale, void* workspace,
                       size_t workspace_bytes_, void* out, qkv_stream_t stream) {
   using namespace qkv;
-  QKV_CHECK_ARG(num_reqs >= 0 && total_q >= 0 && num_kv_heads > 0 &&
+  QKV_CHECK_ARG(num_reqs >= 0 && total_q >= 0 && total_k >= 0 && num_kv_heads > 0 &&
                     num_heads > 0 && num_heads % num_kv_heads == 0,
                 "qkv_dense_prefill: bad sizes");
   QKV_CHECK_ARG(head_size > 0 && head_size % 8 == 0 && head_size <= 256,
@@ -264,6 +272,11 @@ int qkv_dense_prefill(const void* query, const void* key, const void* value,
   if (total_q == 0 || num_reqs == 0) return QKV_OK;
   QKV_CHECK_ARG(query && key && value && cu_seqlens_q && cu_seqlens_k && out,
                 "qkv_dense_prefill: null pointer");
+  if (total_k > 0 && prefill_tc_supported(head_size, num_heads / num_kv_heads, query, key, value, out))
+    return launch_prefill_tc(static_cast<const __nv_bfloat16*>(query), static_cast<const __nv_bfloat16*>(key),
+                             static_cast<const __nv_bfloat16*>(value), cu_seqlens_q, cu_seqlens_k, num_reqs,
+                             total_q, total_k, num_heads, num_kv_heads, causal, scale,
+                             static_cast<__nv_bfloat16*>(out), reinterpret_cast<cudaStream_t>(stream));
   DecodeParams p{};
   p.q = static_cast<const __nv_bfloat16*>(query);
   p.q_stride = static_cast<int64_t>(num_heads) * head_size;
@@ -300,6 +313,57 @@ int qkv_dense_prefill(const void* query, const void* key, const void* value,
                              head_size;
   }
   return launch_decode_generic(p, kDense, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int qkv_kivi_dequant_gather(
+    const int32_t* k_quant, const float* k_scale, const float* k_mn,
+    const int32_t* v_quant, const float* v_scale, const float* v_mn,
+    const void* res_key, const void* res_value, int res_rows, int res_capacity,
+    const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
+    const int32_t* cu_seqlens_k, const int32_t* res_state, int batch,
+    int num_kv_heads, int head_size, int group_size, int block_size,
+    int64_t num_blocks, int total_k, void* out_key, void* out_value,
+    qkv_stream_t stream) {
+  using namespace qkv;
+  QKV_CHECK_ARG(batch >= 0 && total_k >= 0 && num_kv_heads > 0 && num_blocks > 0,
+                "qkv_kivi_dequant_gather: bad sizes");
+  QKV_CHECK_ARG(head_size > 0 && head_size % 8 == 0 && group_size > 0 && group_size % 8 == 0 &&
+                    head_size % group_size == 0 && block_size > 0 && block_size % group_size == 0,
+                "qkv_kivi_dequant_gather: bad geometry");
+  QKV_CHECK_ARG(res_state == nullptr || (res_key && res_value && res_rows > 0 && res_capacity > 0),
+                "qkv_kivi_dequant_gather: residual window needs buffers, rows and capacity");
+  if (batch == 0 || total_k == 0) return QKV_OK;
+  QKV_CHECK_ARG(k_quant && k_scale && k_mn && v_quant && v_scale && v_mn && block_table && seq_lens &&
+                    cu_seqlens_k && out_key && out_value,
+                "qkv_kivi_dequant_gather: null pointer");
+  const auto al16 = [](const void* x) { return x == nullptr || (reinterpret_cast<uintptr_t>(x) & 15u) == 0; };
+  QKV_CHECK_ARG(al16(out_key) && al16(out_value) && al16(res_key) && al16(res_value),
+                "qkv_kivi_dequant_gather: outputs and windows must be 16-byte aligned");
+  DecodeParams p{};
+  p.kq = k_quant;
+  p.ks = k_scale;
+  p.km = k_mn;
+  p.vq = v_quant;
+  p.vs = v_scale;
+  p.vm = v_mn;
+  p.rk = static_cast<const __nv_bfloat16*>(res_key);
+  p.rv = static_cast<const __nv_bfloat16*>(res_value);
+  p.res_rows = res_rows;
+  p.res_cap = res_capacity;
+  p.res_state = res_state;
+  p.bt = block_table;
+  p.bt_stride = bt_stride;
+  p.seq_lens = seq_lens;
+  p.num_reqs = batch;
+  p.batch = batch;
+  p.kvh = num_kv_heads;
+  p.head_size = head_size;
+  p.group = group_size;
+  p.blk = block_size;
+  p.num_blocks = num_blocks;
+  p.err = device_error_ptr();
+  return launch_kivi_gather(p, cu_seqlens_k, total_k, static_cast<__nv_bfloat16*>(out_key),
+                            static_cast<__nv_bfloat16*>(out_value), reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -1,0 +1,368 @@
+// Prompt / chunk attention on the fifth-generation tensor core (tcgen05).
+//
+// Varlen TND layout: q [total_q, Hq, 128] bf16, k / v [total_k, KVH, 128]
+// bf16, request r owns query rows [cu_q[r], cu_q[r+1]) and key rows
+// [cu_k[r], cu_k[r+1]); causal rows see keys up to (kv_len - q_len) + i, the
+// alignment of the reference's prompt attention (FIA TND, sparse_mode 3).
+//
+// One CTA (4 warps) owns a q-tile of one request and one KV head: the G query
+// heads of the KV head times 128 / G tokens form the 128 rows of the MMA, so
+// every K/V tile is read once for all of them. Per 64-key tile:
+//     S[128 x 64]  = Q . K^T   tcgen05.mma kind::f16, A = Q (K-major), B = K
+//                              (K-major), accumulator in tensor memory
+//     P = softmax row pieces   thread = row: tcgen05.ld S, mask, exp2,
+//                              bf16 P into shared memory (128-byte swizzle)
+//     O[128 x 128] += P . V    A = P (K-major), B = V (MN-major)
+// Q, K and V arrive by TMA with the 128-byte swizzle the descriptors name; K/V
+// tiles use a 2-stage ring. The running max moves lazily (8 log2 units), O is
+// rescaled in tensor memory only then. Thread 0 issues the TMA copies and the
+// MMAs; tcgen05.commit arrives on mbarriers (S ready, stage free, O final);
+// every wait is bounded.
+#include <math_constants.h>
+
+#include <atomic>
+
+#include "decode_common.cuh"
+#include "tma_common.cuh"
+
+namespace qkv {
+
+namespace {
+
+using namespace tma;
+
+constexpr int kD = 128;
+constexpr int kRows = 128;    // MMA M: q tokens x query heads of one KV head
+constexpr int kKTile = 64;    // keys per tile (MMA N of S, K of P.V)
+constexpr int kThreads = 128;
+constexpr float kLazyMax = 8.0f;
+constexpr uint32_t kTmemCols = 256;  // S at column 0 (64), O at column 128 (128)
+constexpr uint32_t kSCol = 0, kOCol = 128;
+
+struct __align__(1024) PrefillSmem {
+  __nv_bfloat16 q[2][kRows][64];           // 2 K-blocks of 64 dims, 128-B rows
+  __nv_bfloat16 k[2][2][kKTile][64];       // [stage][K-block][key][dims]
+  __nv_bfloat16 v[2][2][kKTile][64];       // [stage][N-block of dims][key][dims]
+  // P [128 rows][64 keys] (128-B rows) is written over the K tile of its own
+  // stage: S = Q.K^T has consumed it by then, and the stage is refilled only
+  // after P.V completes
+  unsigned long long q_full, s_full, o_done;
+  unsigned long long kv_full[2], kv_empty[2];
+  uint32_t tmem_base;
+};
+constexpr size_t kPrefillSmem = sizeof(PrefillSmem) + 1024;
+
+struct PrefillArgs {
+  const int32_t* cu_q;
+  const int32_t* cu_k;
+  int num_reqs;
+  int num_heads, kvh, gqa, tokens_per_tile;
+  int causal;
+  float scale_log2;
+  __nv_bfloat16* out;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+__global__ void __launch_bounds__(kThreads, 2)
+prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmap_q,
+                  const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  PrefillSmem& sm = *reinterpret_cast<PrefillSmem*>(smem_raw + (((raw + 1023u) & ~1023u) - raw));
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int h = blockIdx.y;
+  const int G = a.gqa, TPT = a.tokens_per_tile;
+
+  // ---- which request and q-tile (tiles never straddle requests)
+  int r = -1, tile = 0;
+  {
+    int acc = 0;
+    for (int i = 0; i < a.num_reqs; ++i) {
+      const int ql = a.cu_q[i + 1] - a.cu_q[i];
+      const int nt = ql > 0 ? (ql + TPT - 1) / TPT : 0;
+      if (static_cast<int>(blockIdx.x) < acc + nt) {
+        r = i;
+        tile = blockIdx.x - acc;
+        break;
+      }
+      acc += nt;
+    }
+  }
+  if (r < 0) return;  // uniform: past the last tile
+  const int q_begin = a.cu_q[r], q_len = a.cu_q[r + 1] - q_begin;
+  const int k_begin = a.cu_k[r], k_len = a.cu_k[r + 1] - k_begin;
+  const int q0 = q_begin + tile * TPT;                 // first query row of the tile
+  const int off = k_len - q_len;                        // causal alignment
+  const int last_qi = min(tile * TPT + TPT, q_len) - 1;  // last query index of the tile
+  const int kv_end = a.causal ? max(0, min(k_len, off + last_qi + 1)) : max(k_len, 0);
+  const int n_tiles = (kv_end + kKTile - 1) / kKTile;
+
+  // ---- tensor memory + barriers
+  if (warp == 0) {
+    tc::tmem_alloc(&sm.tmem_base, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&sm.q_full, 1);
+    mbar_init(&sm.s_full, 1);
+    mbar_init(&sm.o_done, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sm.kv_full[s], 1);
+      mbar_init(&sm.kv_empty[s], 1);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tbase = sm.tmem_base;
+
+  constexpr uint32_t kKvBytes = 2 * 2 * kKTile * 64 * 2;  // K + V tile
+  auto issue_kv = [&](int j) {  // thread 0
+    const int s = j & 1;
+    mbar_expect_tx(&sm.kv_full[s], kKvBytes);
+    const int z = k_begin + j * kKTile;
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      tma_load_3d(&sm.k[s][b][0][0], &tmap_k, 64 * b, h, z, &sm.kv_full[s]);
+      tma_load_3d(&sm.v[s][b][0][0], &tmap_v, 64 * b, h, z, &sm.kv_full[s]);
+    }
+  };
+  bool timed_out = false;
+  int issued = 0, consumed = 0;  // K/V tiles requested / waited for (thread 0)
+  if (tid == 0 && n_tiles > 0) {
+    mbar_expect_tx(&sm.q_full, static_cast<uint32_t>(sizeof(sm.q)));
+    tma_load_3d(&sm.q[0][0][0], &tmap_q, 0, h * G, q0, &sm.q_full);
+    tma_load_3d(&sm.q[1][0][0], &tmap_q, 64, h * G, q0, &sm.q_full);
+    issue_kv(0);
+    issued = 1;
+    if (n_tiles > 1) {
+      issue_kv(1);
+      issued = 2;
+    }
+  }
+
+  const uint32_t id_qk = tc::idesc_f16(kRows, kKTile, 1, 0, 0);
+  const uint32_t id_pv = tc::idesc_f16(kRows, kD, 1, 0, 1);
+  const uint32_t q_addr = smem_u32(&sm.q[0][0][0]);
+
+  // this thread's row: query token q0 + row / G, head h * G + row % G
+  const int row = tid;
+  const int qi = tile * TPT + row / G;  // query index inside the request
+  const int row_end = a.causal ? min(k_len, off + qi + 1) : k_len;  // keys [0, row_end)
+  float m_run = -CUDART_INF_F, l_run = 0.0f;
+  const uint32_t t_row = tbase + (static_cast<uint32_t>(32 * warp) << 16);
+
+  for (int j = 0; j < n_tiles; ++j) {
+    const int s = j & 1;
+    if (tid == 0) {
+      if (j == 0 && !mbar_wait(&sm.q_full, 0)) timed_out = true;
+      if (!mbar_wait(&sm.kv_full[s], static_cast<uint32_t>((j >> 1) & 1))) timed_out = true;
+      consumed = j + 1;
+      tc::fence_after_sync();
+      const uint32_t k_addr = smem_u32(&sm.k[s][0][0][0]);
+#pragma unroll
+      for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          tc::mma_ss(tbase + kSCol, tc::smem_desc_sw128(q_addr + kb * 16384 + ks * 32, 16, 1024),
+                     tc::smem_desc_sw128(k_addr + kb * 8192 + ks * 32, 16, 1024), id_qk,
+                     (kb | ks) != 0 ? 1u : 0u);
+      tc::mma_commit(&sm.s_full);
+      // the stage of tile j - 1 is refilled with tile j + 1 once P.V of j - 1 is done
+      if (j >= 1 && j + 1 < n_tiles) {
+        if (!mbar_wait(&sm.kv_empty[(j - 1) & 1], static_cast<uint32_t>(((j - 1) >> 1) & 1)))
+          timed_out = true;
+        if (!timed_out) {
+          issue_kv(j + 1);
+          issued = j + 2;
+        }
+      }
+    }
+    // ---- S row -> P (bf16, swizzled), lazy O rescale
+    if (!mbar_wait(&sm.s_full, static_cast<uint32_t>(j & 1))) timed_out = true;
+    tc::fence_after_sync();
+    uint32_t sv[2][32];
+    tc::tmem_ld32(t_row + kSCol, sv[0]);
+    tc::tmem_ld32(t_row + kSCol + 32, sv[1]);
+    float sc[64];
+    float mx = -CUDART_INF_F;
+#pragma unroll
+    for (int c = 0; c < 64; ++c) {
+      const int kpos = j * kKTile + c;
+      const float v = __uint_as_float(sv[c >> 5][c & 31]) * a.scale_log2;
+      sc[c] = kpos < row_end ? v : -CUDART_INF_F;
+      mx = fmaxf(mx, sc[c]);
+    }
+    const bool grow = mx > m_run + kLazyMax;
+    if (__any_sync(0xffffffffu, grow) && j > 0) {
+      const float alpha = grow ? exp2f(m_run - mx) : 1.0f;  // m_run finite once j > 0 and grow
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb) {
+        uint32_t ov[32];
+        tc::tmem_ld32(t_row + kOCol + 32 * cb, ov);
+    #pragma unroll
+        for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
+        tc::tmem_st32(t_row + kOCol + 32 * cb, ov);
+      }
+      tc::tmem_wait_st();
+      l_run *= alpha;
+    }
+    if (grow) m_run = mx;
+    const float m_use = m_run == -CUDART_INF_F ? 0.0f : m_run;
+    uint32_t pk[32];
+#pragma unroll
+    for (int c = 0; c < 64; c += 2) {
+      const float p0 = exp2f(sc[c] - m_use), p1 = exp2f(sc[c + 1] - m_use);
+      l_run += p0 + p1;
+      pk[c >> 1] = pack_bf16x2(p0, p1);
+    }
+    // 8 chunks of 16 B; chunk c of row r sits at chunk c ^ (r & 7)
+    unsigned char* prow = reinterpret_cast<unsigned char*>(&sm.k[s][0][0][0]) + row * 128;
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) =
+          make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // P visible to the tensor core
+    tc::fence_before_sync();
+    // a wait that gave up anywhere in the CTA ends the loop for every thread
+    if (__syncthreads_or(timed_out)) {
+      timed_out = true;
+      break;
+    }
+    if (tid == 0) {
+      tc::fence_after_sync();
+      const uint32_t v_addr = smem_u32(&sm.v[s][0][0][0]);
+      const uint32_t p_addr = smem_u32(&sm.k[s][0][0][0]);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        tc::mma_ss(tbase + kOCol, tc::smem_desc_sw128(p_addr + ks * 32, 16, 1024),
+                   tc::smem_desc_sw128(v_addr + ks * 16 * 128, 8192, 1024), id_pv,
+                   (j > 0 || ks > 0) ? 1u : 0u);
+      tc::mma_commit(&sm.kv_empty[s]);
+    }
+  }
+
+  // ---- epilogue: O / l -> bf16 (after an abort: drain the copies and MMAs
+  // in flight, each wait bounded, and skip the store)
+  if (tid == 0 && n_tiles > 0) {
+    tc::mma_commit(&sm.o_done);
+    for (int t = consumed; t < issued; ++t)
+      if (!mbar_wait(&sm.kv_full[t & 1], static_cast<uint32_t>((t >> 1) & 1))) timed_out = true;
+  }
+  const int qrow = q0 + row / G;
+  const bool live = qrow < q_begin + q_len && !timed_out;
+  if (n_tiles > 0) {
+    if (!mbar_wait(&sm.o_done, 0)) timed_out = true;
+    tc::fence_after_sync();
+  }
+  const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+  __nv_bfloat16* orow = a.out + (static_cast<int64_t>(qrow) * a.num_heads + h * G + row % G) * kD;
+#pragma unroll
+  for (int cb = 0; cb < 4; ++cb) {
+    uint32_t ov[32];
+    if (n_tiles > 0) {
+      tc::tmem_ld32(t_row + kOCol + 32 * cb, ov);
+      } else {
+#pragma unroll
+      for (int c = 0; c < 32; ++c) ov[c] = 0u;
+    }
+    if (live) {
+#pragma unroll
+      for (int c = 0; c < 32; c += 8) {
+        uint4 w;
+        w.x = pack_bf16x2(__uint_as_float(ov[c]) * inv, __uint_as_float(ov[c + 1]) * inv);
+        w.y = pack_bf16x2(__uint_as_float(ov[c + 2]) * inv, __uint_as_float(ov[c + 3]) * inv);
+        w.z = pack_bf16x2(__uint_as_float(ov[c + 4]) * inv, __uint_as_float(ov[c + 5]) * inv);
+        w.w = pack_bf16x2(__uint_as_float(ov[c + 6]) * inv, __uint_as_float(ov[c + 7]) * inv);
+        *reinterpret_cast<uint4*>(orow + 32 * cb + c) = w;
+      }
+    }
+  }
+  if (timed_out) record_error(a.err, kErrPipelineTimeout);
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tbase, kTmemCols);
+  }
+}
+
+static_assert(2 * (kPrefillSmem + 1024) <= 228 * 1024, "two CTAs per SM");
+
+int encode_rows_map(const void* base, int64_t rows, int heads, int box_heads, int box_rows,
+                    CUtensorMap* map, const char* what) {
+  auto enc = encode_fn();
+  if (enc == nullptr) return set_error(QKV_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(heads),
+                              static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kD) * 2, static_cast<cuuint64_t>(kD) * 2 * heads};
+  const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_heads), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t es[3] = {1, 1, 1};
+  const CUresult res = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+                           box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (res != CUDA_SUCCESS)
+    return set_error(QKV_ERR_CUDA, std::string("cuTensorMapEncodeTiled(") + what + ") failed: " +
+                                       std::to_string(res));
+  return QKV_OK;
+}
+
+}  // namespace
+
+bool prefill_tc_supported(int head_size, int gqa, const void* q, const void* k, const void* v,
+                          const void* out) {
+  const auto al = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15u) == 0; };
+  return head_size == kD && gqa >= 1 && gqa <= 8 && (kRows % gqa) == 0 && al(q) && al(k) && al(v) &&
+         al(out);
+}
+
+// Launches the tcgen05 prompt attention; q / out [total_q, Hq, 128],
+// k / v [total_k, KVH, 128] bf16; tiles_upper >= the q-tile count.
+int launch_prefill_tc(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v,
+                      const int32_t* cu_q, const int32_t* cu_k, int num_reqs, int total_q, int total_k,
+                      int num_heads, int kvh, int causal, float scale, __nv_bfloat16* out,
+                      cudaStream_t stream) {
+  const int G = num_heads / kvh;
+  const int tpt = kRows / G;
+  CUtensorMap tq, tk, tv;
+  int rc;
+  if ((rc = encode_rows_map(q, total_q, num_heads, G, tpt, &tq, "query")) != QKV_OK) return rc;
+  if ((rc = encode_rows_map(k, total_k, kvh, 1, kKTile, &tk, "key")) != QKV_OK) return rc;
+  if ((rc = encode_rows_map(v, total_k, kvh, 1, kKTile, &tv, "value")) != QKV_OK) return rc;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::atomic<uint64_t> attr{0};
+  const uint64_t bit = 1ull << (dev & 63);
+  if ((attr.load() & bit) == 0) {
+    const cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(kPrefillSmem));
+    if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(prefill_tc_kernel)");
+    attr.fetch_or(bit);
+  }
+  PrefillArgs a{};
+  a.cu_q = cu_q;
+  a.cu_k = cu_k;
+  a.num_reqs = num_reqs;
+  a.num_heads = num_heads;
+  a.kvh = kvh;
+  a.gqa = G;
+  a.tokens_per_tile = tpt;
+  a.causal = causal;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.out = out;
+  a.err = device_error_ptr();
+  const int tiles_upper = (total_q + tpt - 1) / tpt + num_reqs;
+  dim3 grid(tiles_upper, kvh);
+  prefill_tc_kernel<<<grid, kThreads, kPrefillSmem, stream>>>(a, tq, tk, tv);
+  QKV_CHECK_LAUNCH("prefill_tc_kernel");
+  return QKV_OK;
+}
+
+}  // namespace qkv

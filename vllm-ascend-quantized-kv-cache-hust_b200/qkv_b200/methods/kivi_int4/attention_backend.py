@@ -710,36 +710,93 @@ class AscendKiviInt4AttentionBackendMixin:
         return output
 
     def _forward_kivi_history_attention(self, query, block_table, seq_lens, qlen, req_ids, causal, output):
-        """Multi-token rows over history + window: each query token becomes a
-        decode row with its causal length (the reference's generic branch,
-        attention_backend.py:1176-1191)."""
+        """Rows over history + window (the reference's generic branch,
+        attention_backend.py:1176-1191). Requests with several query tokens
+        (prefill chunks on cached tokens) gather their K/V densely (int4 pages
+        dequantised + bf16 window) and run the tensor-core prompt attention,
+        aligned to the end of their keys; single-token rows run the paged
+        decode kernel, each with its causal length."""
         from ...ops.kivi_decode import kivi_paged_decode
 
         B = len(seq_lens)
         keys = self._get_kivi_req_keys(req_ids, B)
-        rows_req, rows_len = [], []
+        lens = [int(s) for s in seq_lens]
+        starts, ql = [], []
         prev = 0
         for b in range(B):
             q_end = int(qlen[b])
-            ql = q_end - prev
-            L = int(seq_lens[b])
-            for i in range(ql):
-                rows_req.append(b)
-                rows_len.append(max(0, min(L, L - ql + i + 1)) if causal else L)
+            starts.append(prev)
+            ql.append(q_end - prev)
             prev = q_end
+        if prev == 0:
+            return output
+        self._ensure_kivi_residual_buffers()
+        st_all = self._kivi_res_state(keys, lens)
+        bt_full = self._kivi_table(block_table, B)
+        dense = [b for b in range(B) if ql[b] > 1 and lens[b] > 0] if self._kivi_dense_prefill_ok() else []
+        if dense:
+            self._kivi_dense_history(query, bt_full, st_all, lens, starts, ql, dense, causal, output)
+        dense_set = set(dense)
+        rows_req, rows_len, rows_q = [], [], []
+        for b in range(B):
+            if b in dense_set:
+                continue
+            L = lens[b]
+            for i in range(ql[b]):
+                rows_req.append(b)
+                rows_len.append(max(0, min(L, L - ql[b] + i + 1)) if causal else L)
+                rows_q.append(starts[b] + i)
         R = len(rows_req)
         if R == 0:
             return output
-        st = self._kivi_res_state(keys, [int(s) for s in seq_lens])[rows_req]
-        bt_full = self._kivi_table(block_table, B)
-        sel = torch.tensor(rows_req, dtype=torch.long).to(bt_full.device, non_blocking=True)
+        dev = bt_full.device
+        sel = torch.tensor(rows_req, dtype=torch.long).to(dev, non_blocking=True)
         bt = bt_full.index_select(0, sel).contiguous()
+        contiguous = rows_q == list(range(rows_q[0], rows_q[0] + R))
+        if contiguous:
+            q_rows, o_rows = query[rows_q[0]:rows_q[0] + R], output[rows_q[0]:rows_q[0] + R]
+        else:
+            qsel = torch.tensor(rows_q, dtype=torch.long).to(dev, non_blocking=True)
+            q_rows, o_rows = query.index_select(0, qsel).contiguous(), torch.empty_like(output[:R])
         kivi_paged_decode(
-            query[:R], self._kivi_views(), self.kivi_residual_key_cache, self.kivi_residual_value_cache,
-            bt, self._kivi_device_i32(rows_len), self._kivi_device_i32(st), self.kivi_group_size, self.scale,
-            output[:R], max(max(rows_len), 1),
+            q_rows, self._kivi_views(), self.kivi_residual_key_cache, self.kivi_residual_value_cache,
+            bt, self._kivi_device_i32(rows_len), self._kivi_device_i32(st_all[rows_req]), self.kivi_group_size,
+            self.scale, o_rows, max(max(rows_len), 1),
         )
+        if not contiguous:
+            output.index_copy_(0, qsel, o_rows)
         return output
+
+    def _kivi_dense_prefill_ok(self) -> bool:
+        """The tensor-core prompt attention takes head 128 and 1-8 query heads
+        per KV head (a power of two)."""
+        g = self.num_heads // self.num_kv_heads
+        return self.head_size == 128 and g in (1, 2, 4, 8)
+
+    def _kivi_dense_history(self, query, bt_full, st_all, lens, starts, ql, reqs, causal, output):
+        from ...ops.kivi_gather import kivi_dequant_gather
+        from ...ops.prefill import dense_prefill
+
+        dev = bt_full.device
+        sel = torch.tensor(reqs, dtype=torch.long).to(dev, non_blocking=True)
+        bt = bt_full.index_select(0, sel).contiguous()
+        st = self._kivi_device_i32(st_all[reqs])
+        kv_lens = [lens[b] for b in reqs]
+        dk, dv = kivi_dequant_gather(self._kivi_views(), self.kivi_residual_key_cache,
+                                     self.kivi_residual_value_cache, bt, kv_lens, st, self.kivi_group_size)
+        q_lens = [ql[b] for b in reqs]
+        rows = [starts[b] + i for b in reqs for i in range(ql[b])]
+        contiguous = rows == list(range(rows[0], rows[0] + len(rows)))
+        if contiguous:
+            q_sub = query[rows[0]:rows[0] + len(rows)]
+            o_sub = output[rows[0]:rows[0] + len(rows)]
+        else:
+            qsel = torch.tensor(rows, dtype=torch.long).to(dev, non_blocking=True)
+            q_sub = query.index_select(0, qsel).contiguous()
+            o_sub = torch.empty_like(q_sub)
+        dense_prefill(q_sub.contiguous(), dk, dv, q_lens, kv_lens, self.scale, o_sub, causal=causal)
+        if not contiguous:
+            output.index_copy_(0, qsel, o_sub)
 
     def _forward_kivi_prefill_fia(self, query, key, value, attn_metadata, output):
         """Causal prompt attention over the raw prompt K/V

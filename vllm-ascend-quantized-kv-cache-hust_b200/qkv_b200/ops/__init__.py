@@ -7,6 +7,7 @@ fallback.
 
 from .int8 import int8_calc_scales, int8_paged_decode, int8_quant_store
 from .kivi_decode import kivi_paged_decode
+from .kivi_gather import kivi_dequant_gather
 from .kivi_pack import kivi_pack_key_cache, kivi_pack_value_cache
 from .prefill import dense_prefill
 
@@ -15,6 +16,7 @@ __all__ = [
     "int8_calc_scales",
     "int8_paged_decode",
     "int8_quant_store",
+    "kivi_dequant_gather",
     "kivi_pack_key_cache",
     "kivi_pack_value_cache",
     "kivi_paged_decode",

@@ -82,8 +82,16 @@ SIGNATURES: dict[str, tuple] = {
     "qkv_dense_prefill": (
         c_int,
         [
-            c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_float,
+            c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_float,
             c_vp, c_size, c_vp, c_vp,
+        ],
+    ),
+    "qkv_kivi_dequant_gather": (
+        c_int,
+        [
+            c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int,
+            c_vp, c_i64, c_vp, c_vp, c_vp, c_int,
+            c_int, c_int, c_int, c_int, c_i64, c_int, c_vp, c_vp, c_vp,
         ],
     ),
 }
