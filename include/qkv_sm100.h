@@ -273,6 +273,20 @@ QKV_API int qkv_kivi_dequant_gather(
     int64_t num_blocks, int total_k, void* out_key, void* out_value,
     qkv_stream_t stream);
 
+/* Dense bf16 K/V of whole requests from the int8 pages:
+ * _dequant_int8_paged_kv_to_dense (methods/int8_dynamic/attention_backend.py:
+ * 370-404). Position t of request b (t < seq_lens[b]) lands in row
+ * cu_seqlens_k[b] + t of out_key / out_value bf16 [total_k, num_kv_heads,
+ * head_size]; an element is bf16(code * aq) (the product is exact in fp32, so
+ * this is the reference's bf16 multiply). Caches, scales and block table as
+ * for qkv_int8_paged_decode; head_size a multiple of 16. */
+QKV_API int qkv_int8_dequant_gather(
+    const int8_t* key_cache, const int8_t* value_cache, const void* k_aq_scale,
+    const void* v_aq_scale, const int32_t* block_table, int64_t bt_stride,
+    const int32_t* seq_lens, const int32_t* cu_seqlens_k, int batch,
+    int num_kv_heads, int head_size, int block_size, int64_t num_blocks,
+    int total_k, void* out_key, void* out_value, qkv_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -177,3 +177,90 @@ def test_mixin_chunk_over_history_matches_oracle():
     want = O.dense_attention(q.float().cpu().numpy(), dk, dv, ql, lens, head ** -0.5, causal=True)
     err = np.abs(out.float().cpu().numpy() - want).max()
     assert err <= ATOL, err
+
+
+def test_int8_mixin_prompts_then_chunks_over_history_match_oracle():
+    """INT8 mixin, three batches: PrefillNoCache calibrates the scales and
+    fills the pages (attention over the raw K/V); ChunkedPrefill with two
+    decode rows and two chunks over cached tokens, and PrefillCacheHit, read
+    the int8 pages (chunks through the int8 gather + tensor-core attention,
+    single rows through the paged decode kernel). Every row matches the
+    oracle's dequantise-to-bf16-then-attend over the pages after the write."""
+    import qkv_oracle as O
+    from qkv_b200.methods.int8_dynamic.attention_backend import AscendInt8AttentionBackendMixin
+
+    dev = torch.device("cuda", 0)
+    H, Hq, D, blk, nb = 8, 32, 128, 128, 64
+
+    class Impl(AscendInt8AttentionBackendMixin):
+        pass
+
+    impl = Impl()
+    impl.num_heads, impl.num_kv_heads, impl.head_size, impl.num_queries_per_kv = Hq, H, D, Hq // H
+    impl.scale = D ** -0.5
+    layer = SimpleNamespace()
+    cache = torch.zeros(2, nb, blk, H, D, dtype=torch.int8, device=dev)
+    bt = torch.arange(48, dtype=torch.int32).reshape(4, 12)
+    rng = np.random.default_rng(8)
+    bf = lambda *s: torch.from_numpy(O.bf16_round(rng.standard_normal(s).astype(np.float32))).to(dev).bfloat16()
+
+    def slots(b, lo, hi):
+        return torch.tensor([int(bt[b, p // blk]) * blk + p % blk for p in range(lo, hi)], device=dev)
+
+    def run(state, reqs, ql, before, **extra):
+        lens = [before[b] + n for b, n in zip(reqs, ql)]
+        T = sum(ql)
+        q, k, v = bf(T, Hq, D), bf(T, H, D), bf(T, H, D)
+        md = SimpleNamespace(
+            attn_state=SimpleNamespace(name=state), actual_seq_lengths_q=np.cumsum(ql).tolist(),
+            seq_lens_list=lens, slot_mapping=torch.cat([slots(b, before[b], L) for b, L in zip(reqs, lens)]),
+            block_tables=bt[reqs].to(dev), num_actual_tokens=T, causal=True, **extra,
+        )
+        out = torch.full((T, Hq, D), float("nan"), dtype=torch.bfloat16, device=dev)
+        impl.forward(layer, q, k, v, cache, md, out)
+        for b, L in zip(reqs, lens):
+            before[b] = L
+        return q, k, v, out, lens
+
+    before = [0, 0, 0, 0]
+    prompts = [700, 300, 1000, 129]
+    q, k, v, out, _ = run("PrefillNoCache", [0, 1, 2, 3], prompts, before)
+    want = O.dense_attention(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(),
+                             prompts, prompts, D ** -0.5, causal=True)
+    assert np.abs(out.float().cpu().numpy() - want).max() <= ATOL
+
+    k_aq = layer._int8_k_aq_scale.reshape(H, D).float().cpu().numpy()
+    v_aq = layer._int8_v_aq_scale.reshape(H, D).float().cpu().numpy()
+    for state, reqs, ql, extra in (
+        ("ChunkedPrefill", [0, 1, 2, 3], [1, 1, 64, 33],
+         dict(num_decode_tokens=2, num_decodes=2, num_prefills=2)),
+        ("PrefillCacheHit", [2, 0], [50, 1], {}),
+    ):
+        q, _, _, out, lens = run(state, reqs, ql, before, **extra)
+        dk, dv = O.int8_dequant_gather(cache[0].cpu().numpy(), cache[1].cpu().numpy(), k_aq, v_aq,
+                                       bt[reqs].numpy(), lens, target_bf16=True)
+        want = O.dense_attention(q.float().cpu().numpy(), dk, dv, ql, lens, D ** -0.5, causal=True)
+        err = np.abs(out.float().cpu().numpy() - want).max()
+        assert err <= ATOL, (state, err)
+
+
+def test_int8_dequant_gather_bit_exact():
+    """Dense K/V from the int8 pages equal the oracle's gather (code * aq,
+    one bf16 rounding) bit for bit, block tables shuffled, ragged lengths."""
+    import qkv_oracle as O
+    from qkv_b200.ops import int8_dequant_gather
+
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(9)
+    H, D, blk, lens = 8, 128, 128, [1, 127, 128, 129, 3000]
+    maxp = max((L + blk - 1) // blk for L in lens)
+    nb = len(lens) * maxp + 3
+    kc = rng.integers(-128, 128, (nb, blk, H, D), dtype=np.int8)
+    vc = rng.integers(-128, 128, (nb, blk, H, D), dtype=np.int8)
+    aq = O.bf16_round(rng.uniform(0.001, 0.2, (2, H, D)).astype(np.float32))
+    bt = rng.permutation(nb)[:len(lens) * maxp].reshape(len(lens), maxp).astype(np.int32)
+    t = lambda x: torch.from_numpy(x).to(dev)
+    dk, dv = int8_dequant_gather(t(kc), t(vc), t(aq[0]).bfloat16(), t(aq[1]).bfloat16(), t(bt), lens)
+    wk, wv = O.int8_dequant_gather(kc, vc, aq[0], aq[1], bt, lens, target_bf16=True)
+    assert np.array_equal(dk.float().cpu().numpy().view(np.uint32), wk.astype(np.float32).view(np.uint32))
+    assert np.array_equal(dv.float().cpu().numpy().view(np.uint32), wv.astype(np.float32).view(np.uint32))

@@ -26,6 +26,8 @@ int launch_prefill_tc(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv
                       cudaStream_t stream);
 int launch_kivi_gather(const DecodeParams& p, const int32_t* cu_k, int total_k, __nv_bfloat16* dense_k,
                        __nv_bfloat16* dense_v, cudaStream_t stream);
+int launch_int8_gather(const DecodeParams& p, const int32_t* cu_k, int total_k, __nv_bfloat16* dense_k,
+                       __nv_bfloat16* dense_v, cudaStream_t stream);
 
 namespace {
 
@@ -363,6 +365,42 @@ int qkv_kivi_dequant_gather(
   p.num_blocks = num_blocks;
   p.err = device_error_ptr();
   return launch_kivi_gather(p, cu_seqlens_k, total_k, static_cast<__nv_bfloat16*>(out_key),
+                            static_cast<__nv_bfloat16*>(out_value), reinterpret_cast<cudaStream_t>(stream));
+}
+
+int qkv_int8_dequant_gather(
+    const int8_t* key_cache, const int8_t* value_cache, const void* k_aq_scale, const void* v_aq_scale,
+    const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens, const int32_t* cu_seqlens_k,
+    int batch, int num_kv_heads, int head_size, int block_size, int64_t num_blocks, int total_k,
+    void* out_key, void* out_value, qkv_stream_t stream) {
+  using namespace qkv;
+  QKV_CHECK_ARG(batch >= 0 && total_k >= 0 && num_kv_heads > 0 && num_blocks > 0 && block_size > 0,
+                "qkv_int8_dequant_gather: bad sizes");
+  QKV_CHECK_ARG(head_size > 0 && head_size % 16 == 0, "qkv_int8_dequant_gather: head_size must be a multiple of 16");
+  if (batch == 0 || total_k == 0) return QKV_OK;
+  QKV_CHECK_ARG(key_cache && value_cache && k_aq_scale && v_aq_scale && block_table && seq_lens && cu_seqlens_k &&
+                    out_key && out_value,
+                "qkv_int8_dequant_gather: null pointer");
+  const auto al16 = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15u) == 0; };
+  QKV_CHECK_ARG(al16(key_cache) && al16(value_cache) && al16(k_aq_scale) && al16(v_aq_scale) && al16(out_key) &&
+                    al16(out_value),
+                "qkv_int8_dequant_gather: caches, scales and outputs must be 16-byte aligned");
+  DecodeParams p{};
+  p.kc = key_cache;
+  p.vc = value_cache;
+  p.k_aq = static_cast<const __nv_bfloat16*>(k_aq_scale);
+  p.v_aq = static_cast<const __nv_bfloat16*>(v_aq_scale);
+  p.bt = block_table;
+  p.bt_stride = bt_stride;
+  p.seq_lens = seq_lens;
+  p.num_reqs = batch;
+  p.batch = batch;
+  p.kvh = num_kv_heads;
+  p.head_size = head_size;
+  p.blk = block_size;
+  p.num_blocks = num_blocks;
+  p.err = device_error_ptr();
+  return launch_int8_gather(p, cu_seqlens_k, total_k, static_cast<__nv_bfloat16*>(out_key),
                             static_cast<__nv_bfloat16*>(out_value), reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -140,6 +140,8 @@ class AscendInt8AttentionBackendMixin:
         return self._int8_paged(query, attn_metadata.block_tables, seq_lens, output, layer)
 
     def _int8_paged(self, query, block_table, seq_lens, output, layer, rows_req=None):
+        """Decode rows: query row i of ``query`` over ``seq_lens[i]`` keys of
+        request ``rows_req[i]`` (row i itself when ``rows_req`` is None)."""
         from ...ops.int8 import int8_paged_decode
 
         B = len(seq_lens)
@@ -157,21 +159,46 @@ class AscendInt8AttentionBackendMixin:
         return output
 
     def _int8_history_rows(self, query, block_table, seq_lens, qlen, output, layer, causal=True):
-        """Multi-token rows over the int8 pages: one decode row per query token
-        with its causal length (the dequantise-then-attend path of
-        ``_dequant_int8_paged_kv_to_dense`` + FIA sparse_mode 3)."""
-        rows_req, rows_len = [], []
-        prev = 0
-        for b, q_end in enumerate(qlen):
-            ql = int(q_end) - prev
-            L = int(seq_lens[b])
-            for i in range(ql):
-                rows_req.append(b)
-                rows_len.append(max(0, min(L, L - ql + i + 1)) if causal else L)
-            prev = int(q_end)
-        if not rows_req:
+        """Rows over the int8 pages (the dequantise-then-attend path of
+        ``_dequant_int8_paged_kv_to_dense`` + FIA sparse_mode 3,
+        attention_backend.py:282-302, :346-368). Requests with several query
+        tokens gather their K/V densely and run the tensor-core prompt
+        attention aligned to the end of their keys; single-token rows run the
+        paged decode kernel with their causal length."""
+        from ..history_rows import RowView, dense_prefill_geometry_ok, plan_history_rows
+
+        B = len(qlen)
+        plan = plan_history_rows(qlen, seq_lens[:B], causal,
+                                 dense_prefill_geometry_ok(self.head_size, self.num_heads, self.num_kv_heads))
+        if plan.num_tokens == 0:
             return output
-        return self._int8_paged(query, block_table, rows_len, output, layer, rows_req=rows_req)
+        if plan.dense:
+            self._int8_dense_history(query, block_table, plan, causal, output, layer)
+        if not plan.rows_req:
+            return output
+        rows = RowView(query, output, plan.rows_q)
+        self._int8_paged(rows.query, block_table, plan.rows_len, rows.output, layer, rows_req=plan.rows_req)
+        rows.commit()
+        return output
+
+    def _int8_dense_history(self, query, block_table, plan, causal, output, layer):
+        """Dense chunks of ``plan``: one gather of their int8 K/V and one
+        prompt-attention launch over all of them."""
+        from ...ops.int8 import int8_dequant_gather
+        from ...ops.prefill import dense_prefill
+        from ..history_rows import RowView
+
+        reqs = plan.dense
+        k_aq, v_aq = self._aq(layer)
+        bt = self._int8_table(block_table, max(reqs) + 1)
+        sel = torch.tensor(reqs, dtype=torch.long).to(bt.device, non_blocking=True)
+        kv_lens = [plan.seq_lens[b] for b in reqs]
+        dk, dv = int8_dequant_gather(self.key_cache, self.value_cache, k_aq, v_aq,
+                                     bt.index_select(0, sel).contiguous(), kv_lens)
+        rows = RowView(query, output, [plan.starts[b] + i for b in reqs for i in range(plan.q_lens[b])])
+        dense_prefill(rows.query.contiguous(), dk, dv, [plan.q_lens[b] for b in reqs], kv_lens, self.scale,
+                      rows.output, causal=causal)
+        rows.commit()
 
     def _forward_int8_dense(self, query, key, value, attn_metadata, output, causal=True):
         from ...ops.prefill import dense_prefill

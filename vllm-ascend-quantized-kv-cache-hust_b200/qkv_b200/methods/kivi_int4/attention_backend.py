@@ -717,86 +717,49 @@ class AscendKiviInt4AttentionBackendMixin:
         aligned to the end of their keys; single-token rows run the paged
         decode kernel, each with its causal length."""
         from ...ops.kivi_decode import kivi_paged_decode
+        from ..history_rows import RowView, dense_prefill_geometry_ok, plan_history_rows
 
         B = len(seq_lens)
+        plan = plan_history_rows(qlen[:B], seq_lens, causal,
+                                 dense_prefill_geometry_ok(self.head_size, self.num_heads, self.num_kv_heads))
+        if plan.num_tokens == 0:
+            return output
         keys = self._get_kivi_req_keys(req_ids, B)
-        lens = [int(s) for s in seq_lens]
-        starts, ql = [], []
-        prev = 0
-        for b in range(B):
-            q_end = int(qlen[b])
-            starts.append(prev)
-            ql.append(q_end - prev)
-            prev = q_end
-        if prev == 0:
-            return output
         self._ensure_kivi_residual_buffers()
-        st_all = self._kivi_res_state(keys, lens)
+        st_all = self._kivi_res_state(keys, plan.seq_lens)
         bt_full = self._kivi_table(block_table, B)
-        dense = [b for b in range(B) if ql[b] > 1 and lens[b] > 0] if self._kivi_dense_prefill_ok() else []
-        if dense:
-            self._kivi_dense_history(query, bt_full, st_all, lens, starts, ql, dense, causal, output)
-        dense_set = set(dense)
-        rows_req, rows_len, rows_q = [], [], []
-        for b in range(B):
-            if b in dense_set:
-                continue
-            L = lens[b]
-            for i in range(ql[b]):
-                rows_req.append(b)
-                rows_len.append(max(0, min(L, L - ql[b] + i + 1)) if causal else L)
-                rows_q.append(starts[b] + i)
-        R = len(rows_req)
-        if R == 0:
+        if plan.dense:
+            self._kivi_dense_history(query, bt_full, st_all, plan, causal, output)
+        if not plan.rows_req:
             return output
-        dev = bt_full.device
-        sel = torch.tensor(rows_req, dtype=torch.long).to(dev, non_blocking=True)
-        bt = bt_full.index_select(0, sel).contiguous()
-        contiguous = rows_q == list(range(rows_q[0], rows_q[0] + R))
-        if contiguous:
-            q_rows, o_rows = query[rows_q[0]:rows_q[0] + R], output[rows_q[0]:rows_q[0] + R]
-        else:
-            qsel = torch.tensor(rows_q, dtype=torch.long).to(dev, non_blocking=True)
-            q_rows, o_rows = query.index_select(0, qsel).contiguous(), torch.empty_like(output[:R])
+        sel = torch.tensor(plan.rows_req, dtype=torch.long).to(bt_full.device, non_blocking=True)
+        rows = RowView(query, output, plan.rows_q)
         kivi_paged_decode(
-            q_rows, self._kivi_views(), self.kivi_residual_key_cache, self.kivi_residual_value_cache,
-            bt, self._kivi_device_i32(rows_len), self._kivi_device_i32(st_all[rows_req]), self.kivi_group_size,
-            self.scale, o_rows, max(max(rows_len), 1),
+            rows.query, self._kivi_views(), self.kivi_residual_key_cache, self.kivi_residual_value_cache,
+            bt_full.index_select(0, sel).contiguous(), self._kivi_device_i32(plan.rows_len),
+            self._kivi_device_i32(st_all[plan.rows_req]), self.kivi_group_size, self.scale, rows.output,
+            max(max(plan.rows_len), 1),
         )
-        if not contiguous:
-            output.index_copy_(0, qsel, o_rows)
+        rows.commit()
         return output
 
-    def _kivi_dense_prefill_ok(self) -> bool:
-        """The tensor-core prompt attention takes head 128 and 1-8 query heads
-        per KV head (a power of two)."""
-        g = self.num_heads // self.num_kv_heads
-        return self.head_size == 128 and g in (1, 2, 4, 8)
-
-    def _kivi_dense_history(self, query, bt_full, st_all, lens, starts, ql, reqs, causal, output):
+    def _kivi_dense_history(self, query, bt_full, st_all, plan, causal, output):
+        """Dense chunks of ``plan``: one gather of their K/V (int4 history +
+        window) and one prompt-attention launch over all of them."""
         from ...ops.kivi_gather import kivi_dequant_gather
         from ...ops.prefill import dense_prefill
+        from ..history_rows import RowView
 
-        dev = bt_full.device
-        sel = torch.tensor(reqs, dtype=torch.long).to(dev, non_blocking=True)
-        bt = bt_full.index_select(0, sel).contiguous()
-        st = self._kivi_device_i32(st_all[reqs])
-        kv_lens = [lens[b] for b in reqs]
+        reqs = plan.dense
+        sel = torch.tensor(reqs, dtype=torch.long).to(bt_full.device, non_blocking=True)
+        kv_lens = [plan.seq_lens[b] for b in reqs]
         dk, dv = kivi_dequant_gather(self._kivi_views(), self.kivi_residual_key_cache,
-                                     self.kivi_residual_value_cache, bt, kv_lens, st, self.kivi_group_size)
-        q_lens = [ql[b] for b in reqs]
-        rows = [starts[b] + i for b in reqs for i in range(ql[b])]
-        contiguous = rows == list(range(rows[0], rows[0] + len(rows)))
-        if contiguous:
-            q_sub = query[rows[0]:rows[0] + len(rows)]
-            o_sub = output[rows[0]:rows[0] + len(rows)]
-        else:
-            qsel = torch.tensor(rows, dtype=torch.long).to(dev, non_blocking=True)
-            q_sub = query.index_select(0, qsel).contiguous()
-            o_sub = torch.empty_like(q_sub)
-        dense_prefill(q_sub.contiguous(), dk, dv, q_lens, kv_lens, self.scale, o_sub, causal=causal)
-        if not contiguous:
-            output.index_copy_(0, qsel, o_sub)
+                                     self.kivi_residual_value_cache, bt_full.index_select(0, sel).contiguous(),
+                                     kv_lens, self._kivi_device_i32(st_all[reqs]), self.kivi_group_size)
+        rows = RowView(query, output, [plan.starts[b] + i for b in reqs for i in range(plan.q_lens[b])])
+        dense_prefill(rows.query.contiguous(), dk, dv, [plan.q_lens[b] for b in reqs], kv_lens, self.scale,
+                      rows.output, causal=causal)
+        rows.commit()
 
     def _forward_kivi_prefill_fia(self, query, key, value, attn_metadata, output):
         """Causal prompt attention over the raw prompt K/V

@@ -5,7 +5,7 @@ launches one of the sm_100a kernels on the current CUDA stream; none has a CPU
 fallback.
 """
 
-from .int8 import int8_calc_scales, int8_paged_decode, int8_quant_store
+from .int8 import int8_calc_scales, int8_dequant_gather, int8_paged_decode, int8_quant_store
 from .kivi_decode import kivi_paged_decode
 from .kivi_gather import kivi_dequant_gather
 from .kivi_pack import kivi_pack_key_cache, kivi_pack_value_cache
@@ -14,6 +14,7 @@ from .prefill import dense_prefill
 __all__ = [
     "dense_prefill",
     "int8_calc_scales",
+    "int8_dequant_gather",
     "int8_paged_decode",
     "int8_quant_store",
     "kivi_dequant_gather",

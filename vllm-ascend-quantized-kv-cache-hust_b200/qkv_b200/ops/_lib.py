@@ -94,6 +94,13 @@ SIGNATURES: dict[str, tuple] = {
             c_int, c_int, c_int, c_int, c_i64, c_int, c_vp, c_vp, c_vp,
         ],
     ),
+    "qkv_int8_dequant_gather": (
+        c_int,
+        [
+            c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp,
+            c_int, c_int, c_int, c_int, c_i64, c_int, c_vp, c_vp, c_vp,
+        ],
+    ),
 }
 
 

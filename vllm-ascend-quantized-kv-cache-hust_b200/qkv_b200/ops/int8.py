@@ -88,4 +88,57 @@ def int8_paged_decode(
     return out
 
 
-__all__ = ["int8_calc_scales", "int8_paged_decode", "int8_quant_store"]
+def int8_dequant_gather(
+    key_cache: torch.Tensor,
+    value_cache: torch.Tensor,
+    k_aq: torch.Tensor,
+    v_aq: torch.Tensor,
+    block_table: torch.Tensor,
+    seq_lens: list[int],
+    out_key: torch.Tensor | None = None,
+    out_value: torch.Tensor | None = None,
+    cu_seqlens: torch.Tensor | None = None,
+    seq_lens_device: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Dense bf16 ``[sum(seq_lens), KVH, D]`` K/V from the int8 pages
+    (``_dequant_int8_paged_kv_to_dense``, attention_backend.py:370-404): row
+    ``sum(seq_lens[:b]) + t`` is position ``t`` of request ``b``, dequantised
+    as ``code * aq`` in bf16. ``seq_lens`` on the host; ``cu_seqlens`` /
+    ``seq_lens_device`` (int32, already on the device) make the call
+    capturable in a CUDA graph."""
+    require_cuda("int8_dequant_gather", key_cache, value_cache, block_table)
+    nb, blk, H, D = key_cache.shape
+    B = len(seq_lens)
+    total = sum(int(n) for n in seq_lens)
+    dev = key_cache.device
+    if out_key is None:
+        out_key = torch.empty(total, H, D, dtype=torch.bfloat16, device=dev)
+    if out_value is None:
+        out_value = torch.empty(total, H, D, dtype=torch.bfloat16, device=dev)
+    if B == 0 or total == 0:
+        return out_key, out_value
+    cu_t = cu_seqlens
+    if cu_t is None:
+        cu = [0]
+        for n in seq_lens:
+            cu.append(cu[-1] + int(n))
+        cu_t = torch.tensor(cu, dtype=torch.int32).to(dev, non_blocking=True)
+    sl = seq_lens_device
+    if sl is None:
+        sl = torch.tensor([int(n) for n in seq_lens], dtype=torch.int32).to(dev, non_blocking=True)
+    for name, t, n in (("cu_seqlens", cu_t, B + 1), ("seq_lens_device", sl, B)):
+        if t.dtype != torch.int32 or t.numel() != n or t.device != dev:
+            raise RuntimeError(f"int8_dequant_gather: {name} must be int32 [{n}] on the cache's device")
+    for name, t in (("out_key", out_key), ("out_value", out_value)):
+        if t.dtype != torch.bfloat16 or not t.is_contiguous() or t.shape[0] < total or tuple(t.shape[1:]) != (H, D):
+            raise RuntimeError(f"int8_dequant_gather: {name} must be contiguous bf16 [>= {total}, {H}, {D}]")
+    bt = (block_table if block_table.dtype == torch.int32 else block_table.to(torch.int32)).contiguous()
+    rc = _lib.load().qkv_int8_dequant_gather(
+        ptr(key_cache), ptr(value_cache), ptr(k_aq.contiguous()), ptr(v_aq.contiguous()), ptr(bt), bt.stride(0),
+        ptr(sl), ptr(cu_t), B, H, D, blk, nb, total, ptr(out_key), ptr(out_value), stream_handle(dev),
+    )
+    _lib.check(rc, "int8_dequant_gather")
+    return out_key, out_value
+
+
+__all__ = ["int8_calc_scales", "int8_dequant_gather", "int8_paged_decode", "int8_quant_store"]
