@@ -7,7 +7,8 @@
 //   key:   t >= k_begin(r) ? window_k[row][(k_start + t - k_begin) % cap][h][d]
 //                          : bf16(code * k_scale + k_mn)     (fp32, rounded once)
 //   value: the same with the value window and v_scale / v_mn.
-// One thread writes 8 consecutive channels (16 bytes) of one (token, head).
+// One thread writes 8 consecutive channels (16 bytes) of one (token, head);
+// geometries the tiled kernel below does not take use this generic form.
 #include "decode_common.cuh"
 
 namespace qkv {
@@ -100,12 +101,142 @@ __global__ void kivi_gather_kernel(const DecodeParams p, const int32_t* cu_k, in
   *reinterpret_cast<uint4*>(dense_v + o) = make_uint4(outv[0], outv[1], outv[2], outv[3]);
 }
 
+// Tiled form: one CTA per (chunk of `ch` positions of one request, KV head).
+// The key codes are channel-major in the pages ([D][blk / 8] words per page
+// and head), the dense rows token-major, so the chunk's code words and group
+// scales are staged in shared memory transposed (word-major, channel-minor;
+// rows padded by 4 words so both the staging stores and the 16-byte reads
+// are conflict-free) and every thread then writes 16 contiguous bytes of one
+// token row. Values are token-major already and are read directly. `ch`
+// divides the block size and is a multiple or a divisor of the group, so a
+// chunk lies in one page and its groups do not straddle chunks.
+__global__ void __launch_bounds__(256) kivi_gather_tiled_kernel(const DecodeParams p, const int32_t* cu_k, int ch,
+                                                                __nv_bfloat16* dense_k, __nv_bfloat16* dense_v) {
+  extern __shared__ __align__(16) uint32_t gsm[];
+  // ---- chunk -> (request, first position): chunks never straddle requests
+  int b = -1, t0 = 0;
+  {
+    int acc = 0;
+    for (int r = 0; r < p.num_reqs; ++r) {
+      const int nc = (max(p.seq_lens[r], 0) + ch - 1) / ch;
+      if (static_cast<int>(blockIdx.x) < acc + nc) {
+        b = r;
+        t0 = (blockIdx.x - acc) * ch;
+        break;
+      }
+      acc += nc;
+    }
+  }
+  if (b < 0) return;  // uniform: past the last chunk
+  const int h = blockIdx.y;
+  const int L = max(p.seq_lens[b], 0);
+  const int n = min(ch, L - t0);
+  const int D = p.head_size, kvh = p.kvh, words = D >> 3;
+  const int cw = ch >> 3, pitch = D + 4;
+  const int ng = ch >= p.group ? ch / p.group : 1;
+  uint32_t* codes = gsm;                                          // [cw][pitch]
+  float* gscale = reinterpret_cast<float*>(gsm + cw * pitch);     // [ng][D]
+  float* gmin = gscale + ng * D;
+  const TailState ts = load_tail_state(p, b, L);
+  const int64_t page = t0 < ts.k_begin || t0 < ts.v_begin ? page_of(p, b, t0) : -1;
+  const int off0 = t0 % p.blk;
+  const int g0 = off0 / p.group;
+  if (page >= 0 && t0 < ts.k_begin) {
+    const int wpb = p.blk >> 3;
+    const int32_t* src = p.kq + (page * kvh + h) * static_cast<int64_t>(D) * wpb + (off0 >> 3);
+    for (int i = threadIdx.x; i < D * cw; i += blockDim.x) {
+      const int d = i / cw, w = i - d * cw;
+      codes[w * pitch + d] = static_cast<uint32_t>(__ldg(src + static_cast<int64_t>(d) * wpb + w));
+    }
+    const int ngk = p.blk / p.group;
+    const int64_t sb = (page * kvh + h) * static_cast<int64_t>(D) * ngk + g0;
+    for (int i = threadIdx.x; i < D * ng; i += blockDim.x) {
+      const int d = i / ng, gi = i - d * ng;
+      gscale[gi * D + d] = __ldg(p.ks + sb + static_cast<int64_t>(d) * ngk + gi);
+      gmin[gi * D + d] = __ldg(p.km + sb + static_cast<int64_t>(d) * ngk + gi);
+    }
+  }
+  __syncthreads();
+  const int64_t row0 = static_cast<int64_t>(cu_k[b]) + t0;
+  for (int i = threadIdx.x; i < n * words; i += blockDim.x) {
+    const int tl = i / words, c = i - tl * words;
+    const int t = t0 + tl;
+    uint32_t ok[4], ov[4];
+    // ---- key
+    if (t >= ts.k_begin) {
+      const int slot = (ts.k_start + (t - ts.k_begin)) % p.res_cap;
+      const uint4 raw = *reinterpret_cast<const uint4*>(
+          p.rk + ((static_cast<int64_t>(ts.row) * p.res_cap + slot) * kvh + h) * D + 8 * c);
+      ok[0] = raw.x; ok[1] = raw.y; ok[2] = raw.z; ok[3] = raw.w;
+    } else if (page < 0) {
+      ok[0] = ok[1] = ok[2] = ok[3] = 0u;
+    } else {
+      const uint32_t* cr = codes + (tl >> 3) * pitch + 8 * c;
+      const uint4 w0 = *reinterpret_cast<const uint4*>(cr);
+      const uint4 w1 = *reinterpret_cast<const uint4*>(cr + 4);
+      const int gi = (off0 + tl) / p.group - g0;
+      const float4 s0 = *reinterpret_cast<const float4*>(gscale + gi * D + 8 * c);
+      const float4 s1 = *reinterpret_cast<const float4*>(gscale + gi * D + 8 * c + 4);
+      const float4 m0 = *reinterpret_cast<const float4*>(gmin + gi * D + 8 * c);
+      const float4 m1 = *reinterpret_cast<const float4*>(gmin + gi * D + 8 * c + 4);
+      const int sh = 4 * (tl & 7);
+      const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+      const float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        ok[j] = pack_bf16x2(kivi_value((wv[2 * j] >> sh) & 0xFu, sv[2 * j], mv[2 * j]),
+                            kivi_value((wv[2 * j + 1] >> sh) & 0xFu, sv[2 * j + 1], mv[2 * j + 1]));
+    }
+    // ---- value (token-major in the pages)
+    if (t >= ts.v_begin) {
+      const int slot = (ts.v_start + (t - ts.v_begin)) % p.res_cap;
+      const uint4 raw = *reinterpret_cast<const uint4*>(
+          p.rv + ((static_cast<int64_t>(ts.row) * p.res_cap + slot) * kvh + h) * D + 8 * c);
+      ov[0] = raw.x; ov[1] = raw.y; ov[2] = raw.z; ov[3] = raw.w;
+    } else if (page < 0) {
+      ov[0] = ov[1] = ov[2] = ov[3] = 0u;
+    } else {
+      const int64_t vrow = (page * p.blk + off0 + tl) * kvh + h;
+      const uint32_t word = static_cast<uint32_t>(__ldg(p.vq + vrow * words + c));
+      const int64_t si = vrow * (D / p.group) + (8 * c) / p.group;
+      const float sc = __ldg(p.vs + si), mn = __ldg(p.vm + si);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        ov[j] = pack_bf16x2(kivi_value((word >> (8 * j)) & 0xFu, sc, mn),
+                            kivi_value((word >> (8 * j + 4)) & 0xFu, sc, mn));
+    }
+    const int64_t o = ((row0 + tl) * kvh + h) * D + 8 * c;
+    *reinterpret_cast<uint4*>(dense_k + o) = make_uint4(ok[0], ok[1], ok[2], ok[3]);
+    *reinterpret_cast<uint4*>(dense_v + o) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
+  }
+}
+
+// Chunk length of the tiled kernel for this geometry, or 0 (generic kernel).
+int tiled_chunk(int blk, int group) {
+  const int ch = blk % 64 == 0 ? 64 : blk;
+  if (ch > 128 || ch % 8 != 0) return 0;
+  if (ch % group != 0 && group % ch != 0) return 0;
+  return ch;
+}
+
 }  // namespace
 
 int launch_kivi_gather(const DecodeParams& p, const int32_t* cu_k, int total_k, __nv_bfloat16* dense_k,
                        __nv_bfloat16* dense_v, cudaStream_t stream) {
   const int64_t threads = static_cast<int64_t>(total_k) * p.kvh * (p.head_size / 8);
   if (threads <= 0) return QKV_OK;
+  const int ch = tiled_chunk(p.blk, p.group);
+  const int ng = ch >= p.group ? ch / p.group : 1;
+  const size_t smem = ch > 0 ? (static_cast<size_t>(ch / 8) * (p.head_size + 4) + 2 * ng * p.head_size) * 4 : 0;
+  if (ch > 0 && smem <= 48 * 1024) {
+    const int64_t chunks = (static_cast<int64_t>(total_k) + ch - 1) / ch + p.num_reqs;  // upper bound
+    if (chunks > 0x7FFFFFFFll) return set_error(QKV_ERR_INVALID, "qkv_kivi_dequant_gather: too many chunks");
+    kivi_gather_tiled_kernel<<<dim3(static_cast<unsigned>(chunks), p.kvh), 256, smem, stream>>>(
+        p, cu_k, ch, dense_k, dense_v);
+    QKV_CHECK_LAUNCH("kivi_gather_tiled_kernel");
+    return QKV_OK;
+  }
   const int block = 256;
   const int64_t grid = (threads + block - 1) / block;
   if (grid > 0x7FFFFFFFll) return set_error(QKV_ERR_INVALID, "qkv_kivi_dequant_gather: too many elements");
