@@ -68,6 +68,7 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=30, help="0 skips the end-to-end leg")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-int8", action="store_true", help="skip the config-3 INT8 leg")
+    ap.add_argument("--no-config4", action="store_true", help="skip the config-4 chunked-prefill leg")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the request count (small cases for ncu captures)")
     ap.add_argument("--only", choices=("kivi", "int8", "config4"), default=None,
@@ -846,6 +847,9 @@ def main():
     int8 = None
     if not args.no_int8:
         int8 = run_int8_leg(cfg3, rank, world, device, args)
+    config4 = None
+    if world == 1 and not args.no_config4:
+        config4 = run_config4_leg(device, args)
     e2e_dt, h2d, d2h = (None, 0, 0)
     if args.e2e_steps > 0:
         e2e_dt, h2d, d2h = run_e2e(w, device, args.e2e_steps, 3, world, rank)
@@ -897,6 +901,7 @@ def main():
                          "bytes_per_launch": by, "kernel_ms": decode_ms},
             "pack": pack,
             "int8_config3": int8,
+            "config4": config4,
             "e2e": None if e2e_dt is None else {
                 "value": w.B / e2e_dt, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_dt * 1e3, "api": "AscendKiviInt4AttentionBackendMixin.forward (DecodeOnly)"},

@@ -191,23 +191,33 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmap_
     uint32_t sv[2][32];
     tc::tmem_ld32(t_row + kSCol, sv[0]);
     tc::tmem_ld32(t_row + kSCol + 32, sv[1]);
+    // raw scores; only a tile that reaches past some row's causal end masks
     float sc[64];
     float mx = -CUDART_INF_F;
+    const bool tile_full = (j + 1) * kKTile <= row_end;
+    if (__all_sync(0xffffffffu, tile_full)) {
 #pragma unroll
-    for (int c = 0; c < 64; ++c) {
-      const int kpos = j * kKTile + c;
-      const float v = __uint_as_float(sv[c >> 5][c & 31]) * a.scale_log2;
-      sc[c] = kpos < row_end ? v : -CUDART_INF_F;
-      mx = fmaxf(mx, sc[c]);
+      for (int c = 0; c < 64; ++c) {
+        sc[c] = __uint_as_float(sv[c >> 5][c & 31]);
+        mx = fmaxf(mx, sc[c]);
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float v = __uint_as_float(sv[c >> 5][c & 31]);
+        sc[c] = j * kKTile + c < row_end ? v : -CUDART_INF_F;
+        mx = fmaxf(mx, sc[c]);
+      }
     }
+    mx *= a.scale_log2;  // the scale is positive: max commutes with it
     const bool grow = mx > m_run + kLazyMax;
     if (__any_sync(0xffffffffu, grow) && j > 0) {
-      const float alpha = grow ? exp2f(m_run - mx) : 1.0f;  // m_run finite once j > 0 and grow
+      const float alpha = grow ? fast_exp2(m_run - mx) : 1.0f;  // m_run finite once j > 0 and grow
 #pragma unroll
       for (int cb = 0; cb < 4; ++cb) {
         uint32_t ov[32];
         tc::tmem_ld32(t_row + kOCol + 32 * cb, ov);
-    #pragma unroll
+#pragma unroll
         for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
         tc::tmem_st32(t_row + kOCol + 32 * cb, ov);
       }
@@ -215,11 +225,13 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmap_
       l_run *= alpha;
     }
     if (grow) m_run = mx;
-    const float m_use = m_run == -CUDART_INF_F ? 0.0f : m_run;
+    // p = 2^(s * scale * log2(e) - m): one FFMA and one ex2 per score
+    const float neg_m = m_run == -CUDART_INF_F ? 0.0f : -m_run;
     uint32_t pk[32];
 #pragma unroll
     for (int c = 0; c < 64; c += 2) {
-      const float p0 = exp2f(sc[c] - m_use), p1 = exp2f(sc[c + 1] - m_use);
+      const float p0 = fast_exp2(fmaf(sc[c], a.scale_log2, neg_m));
+      const float p1 = fast_exp2(fmaf(sc[c + 1], a.scale_log2, neg_m));
       l_run += p0 + p1;
       pk[c >> 1] = pack_bf16x2(p0, p1);
     }
