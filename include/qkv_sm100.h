@@ -60,8 +60,9 @@ QKV_API int qkv_last_error(char* buf, int len);
 /* Synchronises `stream`, then reads and clears the device error word of the
  * current device. *code receives 0 or the first recorded kernel error
  * (1 = slot out of range, 2 = block id out of range, 3 = residual row out of
- * range, 4 = block-table entry negative for a live token). Returns QKV_OK or
- * QKV_ERR_CUDA. */
+ * range, 4 = block-table entry negative for a live token, 5 = a bounded wait
+ * on an in-kernel copy gave up, 6 = window plan source or lane out of
+ * range). Returns QKV_OK or QKV_ERR_CUDA. */
 QKV_API int qkv_device_error(int* code, qkv_stream_t stream);
 
 /* ------------------------------------------------------------------------
@@ -286,6 +287,87 @@ QKV_API int qkv_int8_dequant_gather(
     const int32_t* seq_lens, const int32_t* cu_seqlens_k, int batch,
     int num_kv_heads, int head_size, int block_size, int64_t num_blocks,
     int total_k, void* out_key, void* out_value, qkv_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * KIVI residual windows: host planner and device apply
+ * ---------------------------------------------------------------------- */
+
+/* Host-side planner of the residual windows (no GPU): the reference's state
+ * machine _store_kivi_residual_entries / _flush_kivi_residual_prefix /
+ * _set_kivi_residual_window (methods/kivi_int4/attention_backend.py:377-462,
+ * :813-836) over caller-owned int64 state arrays: per side, slots
+ * [rows, capacity] (-1 = empty lane), FIFO start [rows] and length [rows].
+ * Returns an opaque handle (NULL on bad arguments); the arrays must outlive
+ * it. A plan collects flushes and ring writes between qkv_window_begin and
+ * qkv_window_plan_export; source codes s >= 0 name ring lane s (row *
+ * capacity + lane), s < 0 new token -1 - s. */
+QKV_API void* qkv_window_create(int rows, int capacity, int group_size,
+                                int64_t* key_slots, int64_t* key_start,
+                                int64_t* key_length, int64_t* value_slots,
+                                int64_t* value_start, int64_t* value_length);
+QKV_API void qkv_window_destroy(void* window);
+QKV_API void qkv_window_begin(void* window);
+/* Appends n tokens (slots[i] holds new token tokens[i]) to one row's window:
+ * a held slot is overwritten in place; at capacity a key window flushes whole
+ * (gated by is_aligned_key_window, semantics.py:254-283, when
+ * gate_block_size > 0; a misaligned window returns QKV_ERR_INVALID), a value
+ * window evicts its oldest lane. */
+QKV_API int qkv_window_store(void* window, int row, int n, const int64_t* slots,
+                             const int64_t* tokens, int is_key,
+                             int gate_block_size);
+/* One token for each of n distinct rows (a decode step). */
+QKV_API int qkv_window_store_one_each(void* window, int n, const int64_t* rows,
+                                      const int64_t* slots,
+                                      const int64_t* tokens, int is_key,
+                                      int gate_block_size);
+/* Tokens that go straight to the int4 history (bulk prompt write,
+ * attention_backend.py:608-674). */
+QKV_API int qkv_window_flush_direct(void* window, int n, const int64_t* slots,
+                                    const int64_t* tokens, int is_key);
+/* Drops lanes whose slot is not among live_slots; survivors move to lanes
+ * 0.. in FIFO order. */
+QKV_API int qkv_window_prune(void* window, int row, int n_live,
+                             const int64_t* live_slots, int is_key);
+QKV_API int qkv_window_reset_row(void* window, int row);
+/* Sizes of the open plan of one side after deduplication (the last flush of
+ * a slot, for keys of a whole group, is kept). */
+QKV_API int qkv_window_plan_counts(void* window, int is_key, int64_t* n_flush,
+                                   int64_t* n_writes);
+/* flush_src / flush_slots [n_flush], write_lanes / write_src [n_writes]
+ * (lanes ascending). */
+QKV_API int qkv_window_plan_export(void* window, int is_key, int64_t* flush_src,
+                                   int64_t* flush_slots, int64_t* write_lanes,
+                                   int64_t* write_src);
+/* ok[i] = 1 when both windows of rows[i] hold exactly the last positions of a
+ * request of seq_lens[i] tokens (block-table row i of table [n, table_cols]);
+ * the fast check of _sync_kivi_residual_windows. */
+QKV_API int qkv_window_expected_live(void* window, int n, const int64_t* rows,
+                                     const int64_t* seq_lens,
+                                     const int64_t* table, int table_cols,
+                                     int block_size, uint8_t* ok);
+
+/* Device side of a plan, both sides in one launch: out_k[i] = the token row
+ * named by k_src[i] (ring_key lane or new_key row), likewise for values.
+ * Rings [ring_lanes, row_bytes], new tokens [n_new, row_bytes] (new_key may
+ * be NULL when no source names a new token), row_bytes a multiple of 16. A
+ * source out of range writes zeros and sets the device error word. Replaces
+ * the index_select calls of the reference's window writes
+ * (methods/kivi_int4/attention_backend.py:411-462). */
+QKV_API int qkv_kivi_window_gather(const void* ring_key, const void* ring_value,
+                                   int64_t ring_lanes, const void* new_key,
+                                   const void* new_value, int64_t n_new,
+                                   const int64_t* k_src, int64_t nk,
+                                   const int64_t* v_src, int64_t nv,
+                                   int64_t row_bytes, void* out_k, void* out_v,
+                                   qkv_stream_t stream);
+/* ring_key[k_lanes[i]] = k_data[i], ring_value[v_lanes[i]] = v_data[i]; a
+ * lane out of range is skipped and sets the device error word. */
+QKV_API int qkv_kivi_window_scatter(void* ring_key, void* ring_value,
+                                    int64_t ring_lanes, const int64_t* k_lanes,
+                                    int64_t nk, const void* k_data,
+                                    const int64_t* v_lanes, int64_t nv,
+                                    const void* v_data, int64_t row_bytes,
+                                    qkv_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -46,7 +46,37 @@ def make_impl(group=8, residual=16, block=16, rows=4, nb=40):
     impl.launches = []
     impl._launch_kivi_key_pack = lambda k, s: impl.launches.append((True, k.clone(), s.clone()))
     impl._launch_kivi_value_pack = lambda v, s: impl.launches.append((False, v.clone(), s.clone()))
+    impl._launch_kivi_window_apply = _cpu_window_apply(impl)
     return impl
+
+
+def _cpu_window_apply(impl):
+    """The device apply of a plan restated with torch on CPU tensors (the
+    GPU path is qkv_kivi_window_gather / qkv_kivi_window_scatter): every
+    source is read before any ring lane is written, then packs, then the
+    ring scatter."""
+
+    def apply(exports, new_tokens):
+        (kfs, kfl, kwl, kws), (vfs, vfl, vwl, vws) = exports
+        rings = (impl.kivi_residual_key_cache, impl.kivi_residual_value_cache)
+        taken = []
+        for ring, new, fs, ws in ((rings[0], new_tokens[0], kfs, kws), (rings[1], new_tokens[1], vfs, vws)):
+            flat = ring.view(-1, *ring.shape[2:])
+
+            def take(src):
+                rows = [flat[s].clone() if s >= 0 else new[-1 - s].clone() for s in src.tolist()]
+                return torch.stack(rows) if rows else flat[:0].clone()
+
+            taken.append((take(fs), take(ws)))
+        if kfs.size:
+            impl._write_kivi_key_quant_cache(taken[0][0], torch.from_numpy(kfl), _host_slots=kfl.tolist())
+        if vfs.size:
+            impl._write_kivi_value_quant_cache(taken[1][0], torch.from_numpy(vfl))
+        for ring, wl, (_, data) in ((rings[0], kwl, taken[0]), (rings[1], vwl, taken[1])):
+            if wl.size:
+                ring.view(-1, *ring.shape[2:])[torch.from_numpy(wl)] = data
+
+    return apply
 
 
 def views_of(impl):
@@ -211,8 +241,7 @@ def test_forward_guards():
 
 
 def _plans_equal(a, b):
-    return (a.flush_src == b.flush_src and a.flush_slots == b.flush_slots
-            and a.ring_writes == b.ring_writes and a.compactions == b.compactions)
+    return all(np.array_equal(x, y) for x, y in zip(a.export(), b.export()))
 
 
 @pytest.mark.parametrize("seed", range(6))
@@ -267,6 +296,25 @@ def test_batched_liveness_matches_per_row(seed):
             for i, v in enumerate(ids):
                 side.slots[r, (st + i) % cap] = v
             side.start[r], side.length[r] = st, ids.size
-    want = [pl.expected_live(r, int(lens[r]), table[r], blk) for r in range(rows)]
+    want = [_expected_live_py(pl, r, int(lens[r]), table[r], blk) for r in range(rows)]
     got = pl.expected_live_rows(np.arange(rows), lens, table, blk)
     assert got.tolist() == want
+
+
+def _expected_live_py(pl, row, seq_len, table_row, blk):
+    """Python restatement of the liveness check: window entry i of a window of
+    n slots holds position seq_len - n + i."""
+    for side in (pl.key, pl.value):
+        lanes = side.lanes(row)
+        n = len(lanes)
+        if n == 0:
+            continue
+        if n > seq_len:
+            return False
+        pos = np.arange(seq_len - n, seq_len)
+        if np.any(pos // blk >= table_row.size):
+            return False
+        blocks = table_row[pos // blk].astype(np.int64)
+        if np.any(blocks < 0) or not np.array_equal(blocks * blk + pos % blk, side.slots[row, lanes]):
+            return False
+    return True

@@ -1,6 +1,7 @@
 """Builds libqkv_sm100.so (the sm_100a kernels behind qkv_b200) in-tree.
 
-Every ``csrc/*.cu`` file is compiled by nvcc for ``sm_100a`` into
+Every ``csrc/*.cu`` file (and host-only ``csrc/*.cpp``) is compiled by nvcc
+for ``sm_100a`` into
 ``_build/*.o`` (incrementally, in parallel) and linked into
 ``qkv_b200/libqkv_sm100.so`` with the CUDA runtime linked statically, so the
 library only needs the NVIDIA driver at run time.
@@ -72,7 +73,7 @@ def _compile(src: Path, obj: Path, verbose: bool, ptxas_verbose: bool) -> str:
 def build_library(verbose: bool = False, force: bool = False, ptxas_verbose: bool = False) -> Path:
     """Compiles stale objects and (re)links the shared library; returns its path."""
     BUILD_DIR.mkdir(exist_ok=True)
-    sources = sorted(CSRC.glob("*.cu"))
+    sources = sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cpp"))
     if not sources:
         raise RuntimeError(f"no CUDA sources under {CSRC}")
     headers = _headers()

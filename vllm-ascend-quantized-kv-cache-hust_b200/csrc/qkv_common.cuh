@@ -45,6 +45,7 @@ enum DeviceError : int {
   kErrResidualRow = 3,
   kErrNegativeBlock = 4,
   kErrPipelineTimeout = 5,  // a bounded wait on an in-kernel copy gave up
+  kErrWindowSource = 6,     // a window plan source or lane out of range
 };
 
 // Device address of this device's error word (a __device__ int defined in

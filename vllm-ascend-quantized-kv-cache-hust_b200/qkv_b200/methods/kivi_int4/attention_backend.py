@@ -269,28 +269,8 @@ class AscendKiviInt4AttentionBackendMixin:
                          *, req_key: str, is_key: bool) -> None:
         row = self._get_kivi_residual_row(req_key, create=True)
         plan = self._kivi_plan[0 if is_key else 1]
-        self._kivi_planner.store(
-            plan, row, slots, token_index, is_key=is_key,
-            on_flush=self._kivi_key_flush_gate if is_key else None,
-        )
-
-    def _kivi_gather_sources(self, sources: list, ring: torch.Tensor, src: torch.Tensor | None) -> torch.Tensor:
-        flat = ring.view(-1, *ring.shape[2:])
-        ring_pos = [i for i, s in enumerate(sources) if s[0] == "ring"]
-        new_pos = [i for i, s in enumerate(sources) if s[0] == "new"]
-        dev = ring.device
-
-        def idx(vals):
-            return torch.tensor(vals, dtype=torch.long).to(dev, non_blocking=True)
-
-        if not new_pos:
-            return flat.index_select(0, idx([sources[i][1] for i in ring_pos]))
-        if not ring_pos:
-            return src.index_select(0, idx([sources[i][1] for i in new_pos]))
-        out = torch.empty((len(sources), *ring.shape[2:]), dtype=ring.dtype, device=dev)
-        out[idx(ring_pos)] = flat.index_select(0, idx([sources[i][1] for i in ring_pos]))
-        out[idx(new_pos)] = src.index_select(0, idx([sources[i][1] for i in new_pos]))
-        return out
+        self._kivi_planner.store(plan, row, slots, token_index, is_key=is_key,
+                                 gate_block_size=self._get_kivi_block_size() if is_key else 0)
 
     def _kivi_execute_plan(self) -> None:
         """Applies the open plan: pack every flushed token (one launch per
@@ -299,44 +279,32 @@ class AscendKiviInt4AttentionBackendMixin:
             return
         plans, srcs = self._kivi_plan, self._kivi_plan_src
         self._kivi_plan = None
-        for is_key, plan, src in ((True, plans[0], srcs[0]), (False, plans[1], srcs[1])):
-            ring = self.kivi_residual_key_cache if is_key else self.kivi_residual_value_cache
-            if plan.flush_src:
-                sources, slots = self._kivi_dedupe_flush(plan.flush_src, plan.flush_slots, is_key)
-                data = self._kivi_gather_sources(sources, ring, src)
-                slot_t = torch.tensor(slots, dtype=torch.long).to(ring.device, non_blocking=True)
-                if is_key:
-                    self._write_kivi_key_quant_cache(data, slot_t, _host_slots=slots)
-                else:
-                    self._write_kivi_value_quant_cache(data, slot_t)
-            if plan.ring_writes:
-                lanes = sorted(plan.ring_writes)
-                data = self._kivi_gather_sources([plan.ring_writes[l] for l in lanes], ring, src)
-                lanes_t = torch.tensor(lanes, dtype=torch.long).to(ring.device, non_blocking=True)
-                ring.view(-1, *ring.shape[2:]).index_copy_(0, lanes_t, data)
+        exports = [p.export() for p in plans]
+        if all(f.size == 0 and w.size == 0 for f, _, w, _ in exports):
+            return
+        self._launch_kivi_window_apply(exports, srcs)
 
-    def _kivi_dedupe_flush(self, sources: list, slots: list[int], is_key: bool):
-        """Keeps the last flush of a slot (keys: of a whole group): a batched
-        launch has no write order, the reference's sequential flushes do."""
-        if is_key:
-            g = self.kivi_group_size
-            seen: set[int] = set()
-            keep: list[int] = []
-            for gi in range(len(slots) // g - 1, -1, -1):
-                first = slots[gi * g]
-                if first not in seen:
-                    seen.add(first)
-                    keep.append(gi)
-            keep.reverse()
-            idx = [gi * g + j for gi in keep for j in range(g)]
-        else:
-            last: dict[int, int] = {}
-            for i, s in enumerate(slots):
-                last[s] = i
-            idx = sorted(last.values())
-        if len(idx) == len(slots):
-            return sources, slots
-        return [sources[i] for i in idx], [slots[i] for i in idx]
+    def _launch_kivi_window_apply(self, exports, new_tokens) -> None:
+        """Device side of a plan (tests may replace it): one upload of the
+        plan's index lists, one gather of every flushed and written token (ring
+        lanes or new tokens), the pack launches, one scatter into the rings."""
+        from ...ops.kivi_window import kivi_window_gather, kivi_window_scatter
+
+        (kfs, kfl, kwl, kws), (vfs, vfl, vwl, vws) = exports
+        rk, rv = self.kivi_residual_key_cache, self.kivi_residual_value_cache
+        dev = rk.device
+        host = np.concatenate([kfs, kws, vfs, vws, kfl, vfl, kwl, vwl])
+        idx = torch.from_numpy(host).pin_memory().to(dev, non_blocking=True)
+        nfk, nwk, nfv, nwv = kfs.size, kws.size, vfs.size, vws.size
+        o = np.cumsum([0, nfk + nwk, nfv + nwv, nfk, nfv, nwk, nwv])
+        k_src, v_src = idx[o[0]:o[1]], idx[o[1]:o[2]]
+        k_fl, v_fl, k_wl, v_wl = idx[o[2]:o[3]], idx[o[3]:o[4]], idx[o[4]:o[5]], idx[o[5]:o[6]]
+        gk, gv = kivi_window_gather(rk, rv, new_tokens[0], new_tokens[1], k_src, v_src)
+        if nfk:
+            self._write_kivi_key_quant_cache(gk[:nfk], k_fl, _host_slots=kfl.tolist())
+        if nfv:
+            self._write_kivi_value_quant_cache(gv[:nfv], v_fl)
+        kivi_window_scatter(rk, rv, k_wl, gk[nfk:], v_wl, gv[nfv:])
 
     def _kivi_set_plan_source(self, key: torch.Tensor, value: torch.Tensor) -> None:
         dt = self.kivi_residual_dtype
@@ -378,7 +346,7 @@ class AscendKiviInt4AttentionBackendMixin:
             rows = [self._get_kivi_residual_row(k, create=True) for k in keys[:n]]
             tok = list(range(n))
             self._kivi_planner.store_one_each(self._kivi_plan[0], rows, slots_all, tok, is_key=True,
-                                              on_flush=self._kivi_key_flush_gate)
+                                              gate_block_size=self._get_kivi_block_size())
             self._kivi_planner.store_one_each(self._kivi_plan[1], rows, slots_all, tok, is_key=False)
             self._kivi_execute_plan()
             return

@@ -13,19 +13,21 @@ Semantics are the reference's residual state machine
 
 What differs is execution. The reference walks tokens in Python and launches a
 pack per flush, reading slot ids back from the device. Here the slot ids live
-in host memory; a ``WindowPlan`` records, without touching device data, where
-every token goes and which lanes each flush reads — the lane's content at plan
-start, or a token written earlier in the same plan. ``execute`` then does one
-gather of the flush inputs, one pack launch per side and one scatter of the
-new tokens into the ring, so a decode step costs a constant number of
-launches whatever the batch size.
+in host memory (numpy arrays shared with the native planner,
+``qkv_window_*`` in libqkv_sm100.so); a plan records, without touching device
+data, where every token goes and which lanes each flush reads — the lane's
+content at plan start, or a token written earlier in the same plan. The mixin
+then applies it with one gather, one pack launch per side and one scatter, so
+a decode step costs a constant number of launches whatever the batch size.
 """
 
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+import ctypes
 
 import numpy as np
+
+from ...ops import _lib
 
 
 def is_aligned_key_window(slots, group_size: int, block_size: int) -> bool:
@@ -86,25 +88,47 @@ class RingSide:
         self.length[row] = 0
 
 
-# A flush/scatter source: ("ring", flat lane index) or ("new", token index).
-Source = tuple
+KEY_FLUSH_ERROR = "KIVI key flush requires contiguous aligned token groups."
 
 
-@dataclass
+def _p(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+def _i64(x) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(x, dtype=np.int64).reshape(-1))
+
+
 class SidePlan:
-    """Pending work of one side for one forward."""
+    """Handle on one side (keys or values) of the planner's open plan."""
 
-    flush_src: list = field(default_factory=list)    # Source per flushed token
-    flush_slots: list = field(default_factory=list)  # its slot
-    ring_writes: dict = field(default_factory=dict)  # flat lane -> Source
-    compactions: list = field(default_factory=list)  # (row, [old lanes in FIFO order])
+    def __init__(self, planner: WindowPlanner, is_key: bool) -> None:
+        self._planner = planner
+        self.is_key = is_key
+
+    def export(self) -> tuple[np.ndarray, np.ndarray, np.ndarray, np.ndarray]:
+        """(flush sources, flush slots, write lanes, write sources), int64.
+        Source s >= 0 is ring lane s (row * capacity + lane), s < 0 new token
+        -1 - s; only the last flush of a slot (keys: of a whole group) is
+        kept, write lanes ascend."""
+        lib = _lib.load()
+        nf, nw = ctypes.c_int64(0), ctypes.c_int64(0)
+        h = self._planner._handle
+        _lib.check(lib.qkv_window_plan_counts(h, int(self.is_key), ctypes.byref(nf), ctypes.byref(nw)),
+                   "qkv_window_plan_counts")
+        out = [np.empty(nf.value, np.int64), np.empty(nf.value, np.int64), np.empty(nw.value, np.int64),
+               np.empty(nw.value, np.int64)]
+        _lib.check(lib.qkv_window_plan_export(h, int(self.is_key), *(_p(a) for a in out)), "qkv_window_plan_export")
+        return tuple(out)
 
     def empty(self) -> bool:
-        return not (self.flush_src or self.ring_writes or self.compactions)
+        f, _, w, _ = self.export()
+        return f.size == 0 and w.size == 0
 
 
 class WindowPlanner:
-    """Plans residual-window updates for both sides on the host mirror."""
+    """Plans residual-window updates for both sides on the host mirror; the
+    state machine runs in the native planner over this object's arrays."""
 
     def __init__(self, rows: int, capacity: int, group_size: int) -> None:
         self.rows = rows
@@ -112,142 +136,68 @@ class WindowPlanner:
         self.group_size = group_size
         self.key = RingSide(rows, capacity)
         self.value = RingSide(rows, capacity)
-        # lane -> Source of its current content within the open plan
-        self._lane_src: dict[tuple[bool, int], Source] = {}
+        self._lib = _lib.load()
+        self._handle = self._lib.qkv_window_create(
+            rows, capacity, group_size, _p(self.key.slots), _p(self.key.start), _p(self.key.length),
+            _p(self.value.slots), _p(self.value.start), _p(self.value.length))
+        if not self._handle:
+            raise RuntimeError(f"qkv_window_create failed (rows={rows}, capacity={capacity}, group={group_size})")
+
+    def __del__(self) -> None:
+        h, self._handle = getattr(self, "_handle", None), None
+        if h:
+            self._lib.qkv_window_destroy(h)
 
     def side(self, is_key: bool) -> RingSide:
         return self.key if is_key else self.value
 
     def begin(self) -> tuple[SidePlan, SidePlan]:
-        self._lane_src = {}
-        return SidePlan(), SidePlan()
+        self._lib.qkv_window_begin(self._handle)
+        return SidePlan(self, True), SidePlan(self, False)
 
-    def _src_of(self, is_key: bool, flat: int) -> Source:
-        return self._lane_src.get((is_key, flat), ("ring", flat))
+    def _gate_rc(self, rc: int, what: str) -> None:
+        if rc == _lib.QKV_ERR_INVALID:
+            raise RuntimeError(KEY_FLUSH_ERROR)
+        _lib.check(rc, what)
 
-    def store(self, plan: SidePlan, row: int, slots, token_index, *, is_key: bool,
-              on_flush=None) -> None:
+    def store(self, plan: SidePlan, row: int, slots, token_index, *, is_key: bool, gate_block_size: int = 0) -> None:
         """Appends tokens (``slots[i]`` holding new token ``token_index[i]``) to
-        ``row``; records flushes and the final lane contents in ``plan``.
-        ``on_flush(slots)`` may veto a key flush by raising (alignment gate)."""
-        side = self.side(is_key)
-        cap = self.capacity
-        rs = side.slots[row]
-        if len(slots) <= 4:  # decode-sized: search the row instead of indexing it
-            lane_of = {}
-            for slot in slots:
-                hit = np.flatnonzero(rs == int(slot))
-                if hit.size:
-                    lane_of[int(slot)] = int(hit[0])
-        else:
-            lane_of = {int(s): lane for lane, s in enumerate(rs.tolist()) if s >= 0}
-        base = row * cap
-        for slot, t in zip(slots, token_index):
-            slot = int(slot)
-            lane = lane_of.get(slot)
-            if lane is not None:
-                self._lane_src[(is_key, base + lane)] = ("new", int(t))
-                plan.ring_writes[base + lane] = ("new", int(t))
-                continue
-            while side.length[row] >= cap:
-                count = cap if is_key else 1
-                evicted = side.lanes(row)[:count]
-                ev_slots = [int(rs[l]) for l in evicted]
-                if on_flush is not None:
-                    on_flush(ev_slots)
-                for l, s in zip(evicted, ev_slots):
-                    plan.flush_src.append(self._src_of(is_key, base + l))
-                    plan.flush_slots.append(s)
-                    lane_of.pop(s, None)
-                    rs[l] = -1
-                side.length[row] -= count
-                side.start[row] = 0 if side.length[row] == 0 else (side.start[row] + count) % cap
-            tail = (side.start[row] + side.length[row]) % cap
-            rs[tail] = slot
-            side.length[row] += 1
-            lane_of[slot] = tail
-            self._lane_src[(is_key, base + tail)] = ("new", int(t))
-            plan.ring_writes[base + tail] = ("new", int(t))
+        ``row``; records flushes and the final lane contents in the open plan.
+        A key flush of a window that is not whole aligned groups of
+        ``gate_block_size`` blocks raises the reference's RuntimeError."""
+        s, t = _i64(slots), _i64(token_index)
+        if not 0 <= row < self.rows:
+            raise RuntimeError(f"residual row {row} out of range")
+        rc = self._lib.qkv_window_store(self._handle, int(row), s.size, _p(s), _p(t), int(is_key),
+                                        int(gate_block_size) if is_key else 0)
+        self._gate_rc(rc, "qkv_window_store")
 
     def store_one_each(self, plan: SidePlan, rows, slots, token_index, *, is_key: bool,
-                       on_flush=None) -> None:
+                       gate_block_size: int = 0) -> None:
         """``store`` of one token per row for a batch of distinct rows (a
-        decode step), vectorised: in-place hits, appends and one-lane value
-        evictions are array operations; a key window that must flush (a full
-        row) takes the per-row path with its alignment gate."""
-        rows = np.asarray(rows, dtype=np.int64)
-        slots = np.asarray(slots, dtype=np.int64)
-        tokens = np.asarray(token_index, dtype=np.int64)
-        if rows.size == 0:
-            return
-        side = self.side(is_key)
-        cap = self.capacity
-        rs = side.slots[rows]                            # [n, cap] (copy)
-        eq = rs == slots[:, None]
-        hit = eq.any(axis=1)
-        full = side.length[rows] >= cap
-        slow = ~hit & full if is_key else np.zeros_like(hit)
-        for i in np.flatnonzero(slow):                   # whole-window key flush
-            self.store(plan, int(rows[i]), [int(slots[i])], [int(tokens[i])], is_key=True, on_flush=on_flush)
-        fast = ~slow
-        # in-place overwrites
-        hit_lane = eq.argmax(axis=1)
-        # value windows at capacity drop their oldest lane first
-        ev = fast & ~hit & full
-        if ev.any():
-            er = rows[ev]
-            ev_lane = side.start[er] % cap
-            ev_slot = side.slots[er, ev_lane]
-            for r, l, sl in zip(er.tolist(), ev_lane.tolist(), ev_slot.tolist()):
-                plan.flush_src.append(self._src_of(is_key, r * cap + l))
-                plan.flush_slots.append(int(sl))
-            side.slots[er, ev_lane] = -1
-            side.length[er] -= 1
-            side.start[er] = np.where(side.length[er] == 0, 0, (side.start[er] + 1) % cap)
-        app = fast & ~hit
-        ar = rows[app]
-        tail = (side.start[ar] + side.length[ar]) % cap
-        side.slots[ar, tail] = slots[app]
-        side.length[ar] += 1
-        lane = np.where(hit, hit_lane, 0)
-        lane[app] = tail
-        for r, l, t in zip(rows[fast].tolist(), lane[fast].tolist(), tokens[fast].tolist()):
-            flat = r * cap + l
-            self._lane_src[(is_key, flat)] = ("new", t)
-            plan.ring_writes[flat] = ("new", t)
+        decode step)."""
+        r, s, t = _i64(rows), _i64(slots), _i64(token_index)
+        if r.size and (r.min() < 0 or r.max() >= self.rows):
+            raise RuntimeError("residual row out of range")
+        rc = self._lib.qkv_window_store_one_each(self._handle, r.size, _p(r), _p(s), _p(t), int(is_key),
+                                                 int(gate_block_size) if is_key else 0)
+        self._gate_rc(rc, "qkv_window_store_one_each")
 
     def flush_direct(self, plan: SidePlan, slots, token_index) -> None:
         """Records tokens that go straight to the int4 history (bulk prefill)."""
-        for slot, t in zip(slots, token_index):
-            plan.flush_src.append(("new", int(t)))
-            plan.flush_slots.append(int(slot))
+        s, t = _i64(slots), _i64(token_index)
+        _lib.check(self._lib.qkv_window_flush_direct(self._handle, s.size, _p(s), _p(t), int(plan.is_key)),
+                   "qkv_window_flush_direct")
 
-    def prune(self, plan: SidePlan, row: int, live: set, *, is_key: bool) -> None:
+    def prune(self, plan: SidePlan, row: int, live, *, is_key: bool) -> None:
         """Drops lanes whose slot is not in ``live``; survivors move to lanes
         0.. in FIFO order (the reference's ``_set_kivi_residual_window``)."""
-        side = self.side(is_key)
-        lanes = side.lanes(row)
-        if not lanes:
-            return
-        rs = side.slots[row]
-        keep = [l for l in lanes if int(rs[l]) in live]
-        if len(keep) == len(lanes):
-            return
-        kept_slots = [int(rs[l]) for l in keep]
-        base = row * self.capacity
-        srcs = [self._src_of(is_key, base + l) for l in keep]
-        rs.fill(-1)
-        rs[: len(keep)] = kept_slots
-        side.start[row] = 0
-        side.length[row] = len(keep)
-        # the compaction reads the kept lanes' sources (captured above) before
-        # anything of this plan lands; it replaces every pending write of the row
-        for l in range(self.capacity):
-            plan.ring_writes.pop(base + l, None)
-            self._lane_src.pop((is_key, base + l), None)
-        for new_lane, src in enumerate(srcs):
-            plan.ring_writes[base + new_lane] = src
-            self._lane_src[(is_key, base + new_lane)] = src
+        lv = _i64(sorted(live))
+        _lib.check(self._lib.qkv_window_prune(self._handle, int(row), lv.size, _p(lv), int(is_key)),
+                   "qkv_window_prune")
+
+    def reset(self, row: int) -> None:
+        _lib.check(self._lib.qkv_window_reset_row(self._handle, int(row)), "qkv_window_reset_row")
 
     def window(self, row: int, *, is_key: bool) -> tuple[list[int], list[int]]:
         """(slots in FIFO order, lanes) of a row."""
@@ -256,47 +206,20 @@ class WindowPlanner:
         return [int(side.slots[row, l]) for l in lanes], lanes
 
     def expected_live_rows(self, rows, seq_lens, table: np.ndarray, block_size: int) -> np.ndarray:
-        """``expected_live`` for many rows at once; ``table[i]`` is the block
-        table row of ``rows[i]``'s request."""
-        rows = np.asarray(rows, dtype=np.int64)
-        L = np.asarray(seq_lens, dtype=np.int64)
-        ok = np.ones(rows.size, dtype=bool)
-        if rows.size == 0:
-            return ok
-        cap = self.capacity
-        ar = np.arange(cap, dtype=np.int64)
-        table = np.asarray(table, dtype=np.int64)
-        for side in (self.key, self.value):
-            n = side.length[rows]
-            ok &= n <= L
-            valid = ar[None, :] < n[:, None]
-            pos = np.clip(L[:, None] - n[:, None] + ar[None, :], 0, None)
-            col = np.minimum(pos // block_size, table.shape[1] - 1)
-            blocks = np.take_along_axis(table, col, axis=1)
-            want = blocks * block_size + pos % block_size
-            got = side.slots[rows[:, None], (side.start[rows][:, None] + ar[None, :]) % cap]
-            good = (want == got) & (blocks >= 0) & (pos // block_size < table.shape[1])
-            ok &= np.all(good | ~valid, axis=1)
-        return ok
+        """For each ``rows[i]``: both windows hold exactly the last positions of
+        a request of ``seq_lens[i]`` tokens (``table[i]`` its block-table
+        row); window entry j of a window of n slots is position L - n + j."""
+        r, L = _i64(rows), _i64(seq_lens)
+        ok = np.ones(r.size, dtype=np.uint8)
+        if r.size == 0:
+            return ok.astype(bool)
+        tb = np.ascontiguousarray(np.asarray(table, dtype=np.int64).reshape(r.size, -1))
+        _lib.check(self._lib.qkv_window_expected_live(self._handle, r.size, _p(r), _p(L), _p(tb), tb.shape[1],
+                                                      int(block_size), _p(ok)), "qkv_window_expected_live")
+        return ok.astype(bool)
 
     def expected_live(self, row: int, seq_len: int, table_row: np.ndarray, block_size: int) -> bool:
-        """Fast check that both windows hold exactly the request's last
-        positions (the normal case): window entry i of a window of n slots is
-        position seq_len - n + i."""
-        for side in (self.key, self.value):
-            lanes = side.lanes(row)
-            n = len(lanes)
-            if n == 0:
-                continue
-            if n > seq_len:
-                return False
-            pos = np.arange(seq_len - n, seq_len)
-            blocks = table_row[pos // block_size].astype(np.int64)
-            want = blocks * block_size + pos % block_size
-            got = side.slots[row, lanes]
-            if np.any(blocks < 0) or not np.array_equal(want, got):
-                return False
-        return True
+        return bool(self.expected_live_rows([row], [seq_len], np.asarray(table_row)[None, :], block_size)[0])
 
 
-__all__ = ["RingSide", "SidePlan", "WindowPlanner", "is_aligned_key_window", "ordered_slots"]
+__all__ = ["KEY_FLUSH_ERROR", "RingSide", "SidePlan", "WindowPlanner", "is_aligned_key_window", "ordered_slots"]

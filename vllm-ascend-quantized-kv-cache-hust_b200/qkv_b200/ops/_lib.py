@@ -94,6 +94,23 @@ SIGNATURES: dict[str, tuple] = {
             c_int, c_int, c_int, c_int, c_i64, c_int, c_vp, c_vp, c_vp,
         ],
     ),
+    "qkv_window_create": (c_vp, [c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "qkv_window_destroy": (None, [c_vp]),
+    "qkv_window_begin": (None, [c_vp]),
+    "qkv_window_store": (c_int, [c_vp, c_int, c_int, c_vp, c_vp, c_int, c_int]),
+    "qkv_window_store_one_each": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int]),
+    "qkv_window_flush_direct": (c_int, [c_vp, c_int, c_vp, c_vp, c_int]),
+    "qkv_window_prune": (c_int, [c_vp, c_int, c_int, c_vp, c_int]),
+    "qkv_window_reset_row": (c_int, [c_vp, c_int]),
+    "qkv_window_plan_counts": (c_int, [c_vp, c_int, c_vp, c_vp]),
+    "qkv_window_plan_export": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, c_vp]),
+    "qkv_window_expected_live": (c_int, [c_vp, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_vp]),
+    "qkv_kivi_window_gather": (
+        c_int, [c_vp, c_vp, c_i64, c_vp, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp],
+    ),
+    "qkv_kivi_window_scatter": (
+        c_int, [c_vp, c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_i64, c_vp, c_i64, c_vp],
+    ),
     "qkv_int8_dequant_gather": (
         c_int,
         [
@@ -163,6 +180,8 @@ DEVICE_ERRORS = {
     2: "block id out of range",
     3: "residual row out of range",
     4: "block table entry negative for a live token",
+    5: "a bounded wait on an in-kernel copy gave up",
+    6: "window plan source or lane out of range",
 }
 
 
