@@ -369,6 +369,42 @@ QKV_API int qkv_kivi_window_scatter(void* ring_key, void* ring_value,
                                     const void* v_data, int64_t row_bytes,
                                     qkv_stream_t stream);
 
+/* A whole KIVI decode step (one new token per request) in one call: the
+ * DecodeOnly branch of AscendKiviInt4AttentionBackendMixin.forward
+ * (methods/kivi_int4/attention_backend.py:1006-1040): _write_kivi_cache
+ * (:562-606) through the window planner, _sync_kivi_residual_windows
+ * (:813-836), then _forward_kivi_paged_decode_attention (:1193-1230). Every
+ * index the device needs is staged in one pinned buffer and copied once; the
+ * gather, packs, ring scatter and decode launch on `stream` with no host
+ * sync. qkv_kivi_step_create returns the runtime (staging buffers) of one
+ * caller; destroy releases it.
+ *   window            a qkv_window_create handle (its state is updated)
+ *   rows, slots       int64 [batch] host: residual row and new-token slot
+ *   seq_lens          int32 [batch] host, including the new token
+ *   block_table_host  int64 [batch, table_cols] host (liveness check)
+ *   block_table       int32 device [batch, >= max blocks], row stride bt_stride
+ *   query, out        bf16 [batch, num_heads, head_size], row strides in elements
+ *   new_key/new_value bf16 [batch, num_kv_heads, head_size] device, contiguous
+ *   k_quant..v_mn     the six KIVI views; res_key/res_value the bf16 rings
+ *                     [rows, capacity, num_kv_heads, head_size]
+ *   workspace         qkv_kivi_paged_decode_workspace bytes for this batch
+ * A key window that must flush but is not whole aligned groups returns
+ * QKV_ERR_INVALID with the reference's message. */
+QKV_API void* qkv_kivi_step_create(void);
+QKV_API void qkv_kivi_step_destroy(void* step);
+QKV_API int qkv_kivi_decode_step(
+    void* step, void* window, int batch, const int64_t* rows,
+    const int64_t* slots, const int32_t* seq_lens,
+    const int64_t* block_table_host, int table_cols,
+    const int32_t* block_table, int64_t bt_stride, const void* query,
+    int64_t q_stride, const void* new_key, const void* new_value,
+    int32_t* k_quant, float* k_scale, float* k_mn, int32_t* v_quant,
+    float* v_scale, float* v_mn, void* res_key, void* res_value,
+    int num_heads, int num_kv_heads, int head_size, int group_size,
+    int block_size, int64_t num_blocks, float scale, void* workspace,
+    size_t workspace_bytes, void* out, int64_t out_stride,
+    qkv_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -264,3 +264,67 @@ def test_int8_dequant_gather_bit_exact():
     wk, wv = O.int8_dequant_gather(kc, vc, aq[0], aq[1], bt, lens, target_bf16=True)
     assert np.array_equal(dk.float().cpu().numpy().view(np.uint32), wk.astype(np.float32).view(np.uint32))
     assert np.array_equal(dv.float().cpu().numpy().view(np.uint32), wv.astype(np.float32).view(np.uint32))
+
+
+def test_native_decode_step_matches_general_path():
+    """qkv_kivi_decode_step (planning, sync and launches in one native call)
+    against the general Python-planned path on the same decode sequence:
+    bulk prompt writes, 140 decode steps crossing key-window flushes, value
+    evictions, a roll-back of 3 tokens and a finished request. Outputs, int4
+    pages and windows must be identical bit for bit."""
+    dev = torch.device("cuda", 0)
+    head, kvh, group, block, residual, nb, num_heads = 128, 8, 64, 128, 128, 40, 32
+    geo = {"geometry": np.array([head, kvh, group, block, residual, nb, num_heads])}
+    native, six_a = make_impl(geo, dev)
+    general, six_b = make_impl(geo, dev)
+    general._kivi_native_decode = lambda *a, **k: False
+    calls = []
+    orig = native._kivi_native_decode
+    native._kivi_native_decode = lambda *a, **k: calls.append(orig(*a, **k)) or calls[-1]
+    rng = np.random.default_rng(21)
+    reqs, prompt = ["a", "b", "c"], [250, 127, 300]
+    bt = torch.arange(36, dtype=torch.int32).reshape(3, 12)
+    bf = lambda *s: torch.from_numpy(rng.standard_normal(s).astype(np.float32)).to(dev).bfloat16()
+
+    def slot(b, p):
+        return int(bt[b, p // block]) * block + p % block
+
+    for impl, six in ((native, six_a), (general, six_b)):
+        impl._bind_kivi_cache(six)
+    for b, n in enumerate(prompt):
+        k, v = bf(n, kvh, head), bf(n, kvh, head)
+        sl = torch.tensor([slot(b, p) for p in range(n)], device=dev)
+        for impl in (native, general):
+            impl._write_kivi_prefill_cache(k, v, sl, [reqs[b]], [n])
+    lens = list(prompt)
+    live = [0, 1, 2]
+    for step in range(140):
+        if step == 70:
+            lens[1] -= 3  # roll back request b by 3 tokens
+        if step == 100:
+            live = [0, 2]  # request b finishes
+        for b in live:
+            lens[b] += 1
+        B = len(live)
+        q, k, v = bf(B, num_heads, head), bf(B, kvh, head), bf(B, kvh, head)
+        outs = []
+        for impl, six in ((native, six_a), (general, six_b)):
+            md = SimpleNamespace(
+                attn_state=SimpleNamespace(name="DecodeOnly"), actual_seq_lengths_q=list(range(1, B + 1)),
+                seq_lens_list=[lens[b] for b in live],
+                slot_mapping=torch.tensor([slot(b, lens[b] - 1) for b in live], device=dev),
+                block_tables=bt[live].to(dev), req_ids=[reqs[b] for b in live], num_actual_tokens=B, causal=True,
+                finished_req_ids={"b"} if step == 100 else None,
+            )
+            out = torch.zeros(B, num_heads, head, dtype=torch.bfloat16, device=dev)
+            impl.forward(None, q, k, v, six, md, out)
+            outs.append(out)
+        assert torch.equal(outs[0], outs[1]), step
+    assert calls and all(calls)
+    for ta, tb in zip(six_a, six_b):
+        assert torch.equal(ta, tb)
+    for r in ("a", "c"):
+        for is_key in (True, False):
+            sa, da = native._collect_kivi_residual_window(r, is_key=is_key)
+            sb, db = general._collect_kivi_residual_window(r, is_key=is_key)
+            assert sa == sb and torch.equal(da, db), (r, is_key)

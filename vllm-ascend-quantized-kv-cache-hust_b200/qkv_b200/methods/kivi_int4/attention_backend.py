@@ -41,6 +41,17 @@ def _attn_state_name(attn_metadata: Any) -> str:
     return getattr(state, "name", None) or str(state)
 
 
+def _host_i64(x, n: int) -> np.ndarray:
+    """First ``n`` entries of an index tensor / list as host int64 (a device
+    tensor is read back, as the reference's ``.tolist()`` does)."""
+    if isinstance(x, torch.Tensor):
+        t = x[:n]
+        if t.is_cuda:
+            t = t.cpu()
+        return t.numpy().astype(np.int64, copy=False).reshape(-1)
+    return np.asarray(x, dtype=np.int64).reshape(-1)[:n]
+
+
 def _host_list(x) -> list[int]:
     if isinstance(x, torch.Tensor):
         return [int(v) for v in x.tolist()]
@@ -121,6 +132,11 @@ class AscendKiviInt4AttentionBackendMixin:
             )
         if len(kv_cache) == 0:
             return
+        # the host passes the same buffers every step: bind once
+        bound = tuple((t.data_ptr(), tuple(t.shape), t.dtype) if isinstance(t, torch.Tensor) else id(t)
+                      for t in kv_cache)
+        if bound == getattr(self, "_kivi_bound", None) and self.k_quant_cache is not None:
+            return
         if len(kv_cache) == 2:
             kv_cache = kivi_caches_from_byte_tensors(
                 *kv_cache,
@@ -138,6 +154,7 @@ class AscendKiviInt4AttentionBackendMixin:
             self.k_quant_cache, self.k_scale_cache, self.k_mn_cache,
             self.v_quant_cache, self.v_scale_cache, self.v_mn_cache,
         ) = kv_cache
+        self._kivi_bound = bound
         self._ensure_kivi_residual_buffers()
 
     # ------------------------------------------------------------------
@@ -589,6 +606,9 @@ class AscendKiviInt4AttentionBackendMixin:
         history = state == "ChunkedPrefill" and not self._is_kivi_chunked_prefill_all_new(attn_metadata)
 
         if state == "DecodeOnly":
+            if key is not None and value is not None and self._kivi_native_decode(
+                    query, key, value, attn_metadata, seq_lens, req_ids, output):
+                return output
             if key is not None and value is not None:
                 n = min(getattr(attn_metadata, "num_actual_tokens", key.shape[0]), key.shape[0])
                 if n > 0:
@@ -628,6 +648,42 @@ class AscendKiviInt4AttentionBackendMixin:
                                                     causal, output)
 
     # -- kernel calls ---------------------------------------------------
+
+    def _kivi_native_decode(self, query, key, value, attn_metadata, seq_lens, req_ids, output) -> bool:
+        """The whole DecodeOnly step (window writes, window sync, decode
+        attention) as one native call, ``qkv_kivi_decode_step``; False when
+        the batch is not one new token per request with valid slots (the
+        general path then runs)."""
+        from ...ops.kivi_step import KiviDecodeStep
+
+        B = len(seq_lens)
+        n = min(getattr(attn_metadata, "num_actual_tokens", key.shape[0]), key.shape[0])
+        if B == 0 or n != B or self.kivi_residual_dtype != torch.bfloat16 or query.shape[0] < B:
+            return False
+        slots = _host_i64(attn_metadata.slot_mapping, B)
+        if slots.size != B or slots.min() < 0:
+            return False
+        self._ensure_kivi_residual_buffers()
+        keys = self._get_kivi_req_keys(req_ids, B)
+        rows = np.fromiter((self._get_kivi_residual_row(k, create=True) for k in keys), dtype=np.int64, count=B)
+        bt = attn_metadata.block_tables
+        if isinstance(bt, torch.Tensor):
+            bt_host = (bt[:B].cpu() if bt.is_cuda else bt[:B]).numpy()
+        else:
+            bt_host = np.asarray(bt)[:B]
+        dev = self.kivi_residual_key_cache.device
+        k = key[:B] if key.dtype == torch.bfloat16 and key.device == dev else key[:B].to(dev, torch.bfloat16)
+        v = value[:B] if value.dtype == torch.bfloat16 and value.device == dev else value[:B].to(dev, torch.bfloat16)
+        step = getattr(self, "_kivi_step", None)
+        if step is None:
+            step = self._kivi_step = KiviDecodeStep()
+        step.run(
+            self._kivi_planner._handle, rows, slots, np.asarray(seq_lens, dtype=np.int32), bt_host,
+            self._kivi_table(bt, B), query[:B], k.contiguous(), v.contiguous(), self._kivi_views(),
+            self.kivi_residual_key_cache, self.kivi_residual_value_cache, self.kivi_group_size, self.scale,
+            output[:B],
+        )
+        return True
 
     def _kivi_res_state(self, req_keys: list[str], ends: list[int]) -> np.ndarray:
         st = np.zeros((len(req_keys), 6), dtype=np.int32)

@@ -111,6 +111,16 @@ SIGNATURES: dict[str, tuple] = {
     "qkv_kivi_window_scatter": (
         c_int, [c_vp, c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_i64, c_vp, c_i64, c_vp],
     ),
+    "qkv_kivi_step_create": (c_vp, []),
+    "qkv_kivi_step_destroy": (None, [c_vp]),
+    "qkv_kivi_decode_step": (
+        c_int,
+        [
+            c_vp, c_vp, c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_vp, c_i64, c_vp, c_i64, c_vp, c_vp,
+            c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
+            c_int, c_int, c_int, c_int, c_int, c_i64, c_float, c_vp, c_size, c_vp, c_i64, c_vp,
+        ],
+    ),
     "qkv_int8_dequant_gather": (
         c_int,
         [
