@@ -680,6 +680,7 @@ def run_e2e(w, device, steps, warmup, world=1, rank=0):
     runs (window planning, packs, decode), N > 1 gathers every rank's heads
     with ``qkv_b200.distributed.gather_heads``, and the full output comes back
     to the host."""
+    import numpy as np
     import torch
     import torch.distributed as dist
 
@@ -700,20 +701,24 @@ def run_e2e(w, device, steps, warmup, world=1, rank=0):
     bt_pinned = w.bt.clone().pin_memory()
     lens = [w.L] * B
     names = [f"req{b}" for b in range(B)]
+    # the runner's host copy of each step's slot mapping (pinned), as it has
+    # one for q / k / v: the plugin reads it without a device round trip
+    pos = w.L + np.arange(total)[:, None]  # position of each step's new token
+    slots_h = torch.from_numpy(bt_host[np.arange(B)[None, :], pos // w.blk].astype(np.int64) * w.blk
+                               + pos % w.blk).pin_memory()
+    q_lens = list(range(1, B + 1))
 
     def step(i):
         for b in range(B):
             lens[b] += 1
-        slots = [int(bt_host[b, (lens[b] - 1) // w.blk]) * w.blk + (lens[b] - 1) % w.blk for b in range(B)]
         q = q_h[i].to(device, non_blocking=True)
         k = k_h[i].to(device, non_blocking=True)
         v = v_h[i].to(device, non_blocking=True)
         md = SimpleNamespace(
-            attn_state=SimpleNamespace(name="DecodeOnly"), actual_seq_lengths_q=list(range(1, B + 1)),
-            seq_lens_list=list(lens), slot_mapping=torch.tensor(slots, dtype=torch.int64).pin_memory(),
-            block_tables=bt_pinned, req_ids=names, num_actual_tokens=B, causal=True, finished_req_ids=None,
+            attn_state=SimpleNamespace(name="DecodeOnly"), actual_seq_lengths_q=q_lens,
+            seq_lens_list=list(lens), slot_mapping=slots_h[i], block_tables=bt_pinned, req_ids=names,
+            num_actual_tokens=B, causal=True, finished_req_ids=None,
         )
-        md.slot_mapping = md.slot_mapping.to(device, non_blocking=True)
         out = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=device)
         impl.forward(None, q, k, v, (w.kbuf, w.vbuf), md, out)
         res = gather_heads(out, shard, gathered=g_buf, out=full)
