@@ -203,3 +203,26 @@ def test_byte_cache_rejects_bad_buffers():
     dense = torch.zeros(4, 16, 2, 32, dtype=torch.float16)
     with pytest.raises(RuntimeError, match="must hold|whole number of pages"):
         kivi_byte_cache_layout(dense, dense.clone(), num_kv_heads=2, head_size=32, group_size=8)
+
+
+def test_mixin_binds_one_host_allocation_of_both_sides():
+    """The host allocator's single (2, NB, block, KVH, S) uint8 tensor binds
+    like the 2-tuple of its halves: the six views alias it."""
+    from types import SimpleNamespace
+
+    from qkv_b200.methods.kivi_int4.attention_backend import AscendKiviInt4AttentionBackendMixin
+
+    class Impl(AscendKiviInt4AttentionBackendMixin):
+        num_heads, num_kv_heads, head_size, num_queries_per_kv, scale = 4, 2, 32, 2, 0.125
+
+    impl = Impl()
+    impl._init_kivi_state("kivi_int4", SimpleNamespace(
+        cache_config=SimpleNamespace(kivi_group_size=8, kivi_residual_length=16),
+        scheduler_config=SimpleNamespace(max_num_seqs=2)))
+    lay = KiviByteCacheLayout(num_blocks=3, block_size=16, num_kv_heads=2, head_size=32, group_size=8)
+    raw = torch.zeros((2, 3, 16, 2, lay.bytes_per_token_head), dtype=torch.uint8)
+    impl._bind_kivi_cache(raw)
+    assert impl.k_quant_cache.shape == (3, 2, 32, 2) and impl.v_quant_cache.shape == (3, 16, 2, 4)
+    impl.v_quant_cache[0, 0, 0, 0] = 0x01020304
+    assert raw[1].reshape(-1)[:4].tolist() == [4, 3, 2, 1]
+    assert lay.page_size_bytes() * 3 == raw.numel()

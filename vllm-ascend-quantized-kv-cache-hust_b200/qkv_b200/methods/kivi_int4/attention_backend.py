@@ -125,6 +125,9 @@ class AscendKiviInt4AttentionBackendMixin:
         views (no copy); a 6-tuple is taken as is (attention_backend.py:135-175)."""
         if kv_cache is None:
             return
+        if isinstance(kv_cache, torch.Tensor) and kv_cache.dim() == 5 and kv_cache.shape[0] == 2:
+            # one host allocation of shape (2, NB, block, KVH, S): its two halves
+            kv_cache = (kv_cache[0], kv_cache[1])
         if not isinstance(kv_cache, list | tuple):
             raise RuntimeError(
                 "KIVI INT4 kv_cache must be a 2-tuple of byte buffers or a "
