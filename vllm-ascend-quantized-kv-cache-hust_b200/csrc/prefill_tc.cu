@@ -188,27 +188,31 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmap_
     // ---- S row -> P (bf16, swizzled), lazy O rescale
     if (!mbar_wait(&sm.s_full, static_cast<uint32_t>(j & 1))) timed_out = true;
     tc::fence_after_sync();
-    uint32_t sv[2][32];
-    tc::tmem_ld32(t_row + kSCol, sv[0]);
-    tc::tmem_ld32(t_row + kSCol + 32, sv[1]);
-    // raw scores; only a tile that reaches past some row's causal end masks
+    uint32_t sv[64];
+    tc::tmem_ld64(t_row + kSCol, sv);
+    // raw scores; only a tile that reaches past some row's causal end masks.
+    // Max and sum use 8 independent partials: a 64-long dependent chain per
+    // row would leave the two warps per scheduler waiting on latency.
     float sc[64];
-    float mx = -CUDART_INF_F;
+    float pm[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) pm[i] = -CUDART_INF_F;
     const bool tile_full = (j + 1) * kKTile <= row_end;
     if (__all_sync(0xffffffffu, tile_full)) {
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
-        sc[c] = __uint_as_float(sv[c >> 5][c & 31]);
-        mx = fmaxf(mx, sc[c]);
+        sc[c] = __uint_as_float(sv[c]);
+        pm[c & 7] = fmaxf(pm[c & 7], sc[c]);
       }
     } else {
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
-        const float v = __uint_as_float(sv[c >> 5][c & 31]);
+        const float v = __uint_as_float(sv[c]);
         sc[c] = j * kKTile + c < row_end ? v : -CUDART_INF_F;
-        mx = fmaxf(mx, sc[c]);
+        pm[c & 7] = fmaxf(pm[c & 7], sc[c]);
       }
     }
+    float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])), fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
     mx *= a.scale_log2;  // the scale is positive: max commutes with it
     const bool grow = mx > m_run + kLazyMax;
     if (__any_sync(0xffffffffu, grow) && j > 0) {
@@ -228,13 +232,17 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmap_
     // p = 2^(s * scale * log2(e) - m): one FFMA and one ex2 per score
     const float neg_m = m_run == -CUDART_INF_F ? 0.0f : -m_run;
     uint32_t pk[32];
+    float ps[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ps[i] = 0.0f;
 #pragma unroll
     for (int c = 0; c < 64; c += 2) {
       const float p0 = fast_exp2(fmaf(sc[c], a.scale_log2, neg_m));
       const float p1 = fast_exp2(fmaf(sc[c + 1], a.scale_log2, neg_m));
-      l_run += p0 + p1;
+      ps[(c >> 1) & 7] += p0 + p1;
       pk[c >> 1] = pack_bf16x2(p0, p1);
     }
+    l_run += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
     // 8 chunks of 16 B; chunk c of row r sits at chunk c ^ (r & 7)
     unsigned char* prow = reinterpret_cast<unsigned char*>(&sm.k[s][0][0][0]) + row * 128;
 #pragma unroll
