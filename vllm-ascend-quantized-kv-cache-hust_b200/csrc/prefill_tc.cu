@@ -7,21 +7,27 @@
 //
 // One CTA per SM owns TWO q-tiles of one request and one KV head. A q-tile is
 // the G query heads of the KV head times 128 / G tokens: the M = 128 rows of
-// an MMA. Per 64-key tile j and q-tile t:
-//     S_t[128 x 64]  = Q_t . K_j^T   tcgen05.mma kind::f16, fp32 in TMEM
-//     P_t = softmax row pieces       one thread per row (TMEM lane = row)
-//     O_t[128 x 128] += P_t . V_j    A = P_t (K-major, shared memory),
-//                                    B = V_j (MN-major)
+// an MMA. Per 128-key tile j and q-tile t:
+//     S_t[128 x 128] = Q_t . K_j^T   tcgen05.mma kind::f16, A and B from
+//                                    shared memory, fp32 in tensor memory
+//     P_t = softmax row pieces       one thread per row (TMEM lane = row);
+//                                    bf16 P written back over the first 64
+//                                    columns of S_t
+//     O_t[128 x 128] += P_t . V_j    A = P_t from TENSOR memory, B = V_j
+//                                    (MN-major) from shared memory
+// Keeping P in tensor memory leaves the tensor core only Q, K and V to read
+// from shared memory (about 94 B per cycle at full rate, under the SM's 128);
+// a 64-key tile with P in shared memory needed about 190.
 // Warp roles: warps 0-3 run the softmax of q-tile 0, warps 4-7 of q-tile 1,
-// warp 8 issues the TMA copies (Q once, K/V tiles into a 3-stage ring), warp 9
-// issues the MMAs. The MMA warp ping-pongs: while warpgroup 1 turns S_1(j)
-// into P_1(j), the tensor core runs P_0(j).V_j and S_0(j+1), and the other
-// way round, so the exponentials of one q-tile overlap the MMAs of the other,
-// and each K/V tile read from L2 serves 256 query rows. The running max moves
-// lazily (8 log2 units); O is rescaled in TMEM only then. tcgen05.commit
-// arrives on mbarriers (S ready, stage free, O final); every wait is bounded,
-// and a wait that gives up ends the CTA's loops, drains what is in flight,
-// frees TMEM, skips the store and records device error 5.
+// warp 8 issues the TMA copies (Q once; K and V tiles into separate 2-stage
+// rings, so K_{j+2} loads as soon as both S MMAs of tile j are done), warp 9
+// issues the MMAs, ping-ponging: while warpgroup 1 turns S_1(j) into P_1(j),
+// the tensor core runs P_0(j).V_j and S_0(j+1), and the other way round. A
+// CTA's MMAs execute in issue order, so S_t(j+1) may overwrite the columns
+// P_t(j).V_j reads. The running max moves lazily (8 log2 units); O is
+// rescaled in TMEM only then. tcgen05.commit arrives on mbarriers; every wait
+// is bounded, and a wait that gives up ends the CTA's loops, drains what is
+// in flight, frees TMEM, skips the store and records device error 5.
 #include <math_constants.h>
 
 #include <atomic>
@@ -37,23 +43,22 @@ using namespace tma;
 
 constexpr int kD = 128;
 constexpr int kRows = 128;     // MMA M: q tokens x query heads of one KV head
-constexpr int kKTile = 64;     // keys per tile (MMA N of S, K of P.V)
-constexpr int kStages = 3;     // K/V ring
+constexpr int kKTile = 128;    // keys per tile (MMA N of S, K of P.V)
+constexpr int kStages = 2;     // K ring and V ring
 constexpr int kSoftmaxThreads = 256;
 constexpr int kProducerWarp = 8, kMmaWarp = 9;
 constexpr int kThreads = 320;
 constexpr float kLazyMax = 8.0f;
-constexpr uint32_t kTmemCols = 512;  // S_0 at 0, S_1 at 64, O_0 at 128, O_1 at 256
-__host__ __device__ constexpr uint32_t s_col(int t) { return t == 0 ? 0u : 64u; }
-__host__ __device__ constexpr uint32_t o_col(int t) { return t == 0 ? 128u : 256u; }
+constexpr uint32_t kTmemCols = 512;  // S_t (P_t in its first 64) at 128 t, O_t at 256 + 128 t
+__host__ __device__ constexpr uint32_t s_col(int t) { return 128u * t; }
+__host__ __device__ constexpr uint32_t o_col(int t) { return 256u + 128u * t; }
 
 struct __align__(1024) PrefillSmem {
-  __nv_bfloat16 q[2][2][kRows][64];        // [q-tile][64-dim block][row][dims], 128-B rows
+  __nv_bfloat16 q[2][2][kRows][64];         // [q-tile][64-dim block][row][dims], 128-B rows
   __nv_bfloat16 k[kStages][2][kKTile][64];  // [stage][64-dim block][key][dims]
   __nv_bfloat16 v[kStages][2][kKTile][64];  // [stage][64-dim block][key][dims]
-  __nv_bfloat16 p[2][kRows][64];            // [q-tile][row][key], 128-B rows
   unsigned long long q_full;
-  unsigned long long kv_full[kStages], kv_empty[kStages];
+  unsigned long long k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
   unsigned long long s_full[2], p_ready[2], o_done[2];
   uint32_t tmem_base;
 };
@@ -109,10 +114,11 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmap_
   if (r < 0) return;  // uniform: past the last pair
   const int q_begin = a.cu_q[r], q_len = a.cu_q[r + 1] - q_begin;
   const int k_begin = a.cu_k[r], k_len = a.cu_k[r + 1] - k_begin;
-  const int tile0 = 2 * pair;                        // q-tile index of warpgroup 0
-  const bool has1 = (tile0 + 1) * TPT < q_len;       // q-tile 1 holds live queries
-  const int off = k_len - q_len;                     // causal alignment
-  const int last_qi = min((tile0 + (has1 ? 2 : 1)) * TPT, q_len) - 1;
+  const int tile0 = 2 * pair;                   // q-tile index of warpgroup 0
+  const bool has1 = (tile0 + 1) * TPT < q_len;  // q-tile 1 holds live queries
+  const int nq = has1 ? 2 : 1;
+  const int off = k_len - q_len;                // causal alignment
+  const int last_qi = min((tile0 + nq) * TPT, q_len) - 1;
   const int kv_end = a.causal ? max(0, min(k_len, off + last_qi + 1)) : max(k_len, 0);
   const int n_tiles = (kv_end + kKTile - 1) / kKTile;
 
@@ -124,8 +130,10 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmap_
   if (tid == 0) {
     mbar_init(&sm.q_full, 1);
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&sm.kv_full[s], 1);
-      mbar_init(&sm.kv_empty[s], 1);
+      mbar_init(&sm.k_full[s], 1);
+      mbar_init(&sm.k_empty[s], 1);
+      mbar_init(&sm.v_full[s], 1);
+      mbar_init(&sm.v_empty[s], 1);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&sm.s_full[t], 1);
@@ -145,29 +153,36 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmap_
     // ================================================= TMA producer (one lane)
     if (lane == 0 && n_tiles > 0) {
       const int q0 = q_begin + tile0 * TPT;
-      mbar_expect_tx(&sm.q_full, static_cast<uint32_t>(sizeof(sm.q[0]) * (has1 ? 2 : 1)));
-      for (int t = 0; t < (has1 ? 2 : 1); ++t)
+      mbar_expect_tx(&sm.q_full, static_cast<uint32_t>(sizeof(sm.q[0]) * nq));
+      for (int t = 0; t < nq; ++t)
         for (int b = 0; b < 2; ++b)
           tma_load_3d(&sm.q[t][b][0][0], &tmap_q, 64 * b, h * G, q0 + t * TPT, &sm.q_full);
-      constexpr uint32_t kKvBytes = 2 * 2 * kKTile * 64 * 2;
-      int issued = 0;
-      for (int j = 0; j < n_tiles; ++j) {
+      constexpr uint32_t kTileBytes = 2 * kKTile * 64 * 2;
+      int issued_k = 0, issued_v = 0;
+      for (int j = 0; j < n_tiles && !timed_out; ++j) {
         const int s = j % kStages;
-        if (j >= kStages && !mbar_wait(&sm.kv_empty[s], static_cast<uint32_t>((j / kStages - 1) & 1))) {
+        const uint32_t par = static_cast<uint32_t>((j / kStages - 1) & 1);
+        const int z = k_begin + j * kKTile;
+        if (j >= kStages && !mbar_wait(&sm.k_empty[s], par)) {
           timed_out = true;
           break;
         }
-        mbar_expect_tx(&sm.kv_full[s], kKvBytes);
-        const int z = k_begin + j * kKTile;
-        for (int b = 0; b < 2; ++b) {
-          tma_load_3d(&sm.k[s][b][0][0], &tmap_k, 64 * b, h, z, &sm.kv_full[s]);
-          tma_load_3d(&sm.v[s][b][0][0], &tmap_v, 64 * b, h, z, &sm.kv_full[s]);
+        mbar_expect_tx(&sm.k_full[s], kTileBytes);
+        for (int b = 0; b < 2; ++b) tma_load_3d(&sm.k[s][b][0][0], &tmap_k, 64 * b, h, z, &sm.k_full[s]);
+        issued_k = j + 1;
+        if (j >= kStages && !mbar_wait(&sm.v_empty[s], par)) {
+          timed_out = true;
+          break;
         }
-        issued = j + 1;
+        mbar_expect_tx(&sm.v_full[s], kTileBytes);
+        for (int b = 0; b < 2; ++b) tma_load_3d(&sm.v[s][b][0][0], &tmap_v, 64 * b, h, z, &sm.v_full[s]);
+        issued_v = j + 1;
       }
       // every copy this CTA started lands before the CTA leaves
-      for (int j = max(0, issued - kStages); j < issued; ++j)
-        if (!mbar_wait(&sm.kv_full[j % kStages], static_cast<uint32_t>((j / kStages) & 1))) timed_out = true;
+      for (int j = max(0, issued_k - kStages); j < issued_k; ++j)
+        if (!mbar_wait(&sm.k_full[j % kStages], static_cast<uint32_t>((j / kStages) & 1))) timed_out = true;
+      for (int j = max(0, issued_v - kStages); j < issued_v; ++j)
+        if (!mbar_wait(&sm.v_full[j % kStages], static_cast<uint32_t>((j / kStages) & 1))) timed_out = true;
     }
   } else if (warp == kMmaWarp) {
     // ================================================= MMA issuer (one lane)
@@ -182,34 +197,34 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmap_
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks)
             tc::mma_ss(tbase + s_col(t), tc::smem_desc_sw128(q_addr + kb * 16384 + ks * 32, 16, 1024),
-                       tc::smem_desc_sw128(k_addr + kb * 8192 + ks * 32, 16, 1024), id_qk,
+                       tc::smem_desc_sw128(k_addr + kb * 16384 + ks * 32, 16, 1024), id_qk,
                        (kb | ks) != 0 ? 1u : 0u);
         tc::mma_commit(&sm.s_full[t]);
       };
       auto issue_pv = [&](int t, int j) {
         const uint32_t v_addr = smem_u32(&sm.v[j % kStages][0][0][0]);
-        const uint32_t p_addr = smem_u32(&sm.p[t][0][0]);
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
-          tc::mma_ss(tbase + o_col(t), tc::smem_desc_sw128(p_addr + ks * 32, 16, 1024),
-                     tc::smem_desc_sw128(v_addr + ks * 16 * 128, 8192, 1024), id_pv,
+        for (int ks = 0; ks < 8; ++ks)  // 16 keys per step: 8 columns of packed bf16 P
+          tc::mma_ts(tbase + o_col(t), tbase + s_col(t) + 8 * ks,
+                     tc::smem_desc_sw128(v_addr + ks * 16 * 128, 16384, 1024), id_pv,
                      (j > 0 || ks > 0) ? 1u : 0u);
       };
-      bool ok = mbar_wait(&sm.q_full, 0) && mbar_wait(&sm.kv_full[0], 0);
+      bool ok = mbar_wait(&sm.q_full, 0) && mbar_wait(&sm.k_full[0], 0);
       tc::fence_after_sync();
       if (ok) {
-        issue_s(0, 0);
-        if (has1) issue_s(1, 0);
+        for (int t = 0; t < nq; ++t) issue_s(t, 0);
+        tc::mma_commit(&sm.k_empty[0]);  // K_0 read by both S MMAs
       }
       for (int j = 0; ok && j < n_tiles; ++j) {
         const bool next = j + 1 < n_tiles;
+        if (!(ok = mbar_wait(&sm.v_full[j % kStages], static_cast<uint32_t>((j / kStages) & 1)))) break;
         // q-tile 0: P_0(j).V_j, then S_0(j + 1) while warpgroup 1 works
         if (!(ok = mbar_wait(&sm.p_ready[0], static_cast<uint32_t>(j & 1)))) break;
         tc::fence_after_sync();
         issue_pv(0, j);
         if (next) {
           const int s1 = (j + 1) % kStages;
-          if (!(ok = mbar_wait(&sm.kv_full[s1], static_cast<uint32_t>(((j + 1) / kStages) & 1)))) break;
+          if (!(ok = mbar_wait(&sm.k_full[s1], static_cast<uint32_t>(((j + 1) / kStages) & 1)))) break;
           tc::fence_after_sync();
           issue_s(0, j + 1);
         }
@@ -218,8 +233,11 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmap_
           tc::fence_after_sync();
           issue_pv(1, j);
         }
-        tc::mma_commit(&sm.kv_empty[j % kStages]);  // K_j, V_j and both P buffers consumed
-        if (has1 && next) issue_s(1, j + 1);
+        tc::mma_commit(&sm.v_empty[j % kStages]);  // V_j read by both P.V MMAs
+        if (next) {
+          if (has1) issue_s(1, j + 1);
+          tc::mma_commit(&sm.k_empty[(j + 1) % kStages]);  // K_{j+1} read by both S MMAs
+        }
       }
       if (!ok) timed_out = true;
       tc::mma_commit(&sm.o_done[0]);
@@ -240,67 +258,84 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmap_
         break;
       }
       tc::fence_after_sync();
-      uint32_t sv[64];
-      tc::tmem_ld64(t_row + s_col(t), sv);
-      float sc[64];
-      float pm[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) pm[i] = -CUDART_INF_F;
-      const bool tile_full = (j + 1) * kKTile <= row_end;
-      if (__all_sync(0xffffffffu, tile_full)) {
-#pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          sc[c] = __uint_as_float(sv[c]);
-          pm[c & 7] = fmaxf(pm[c & 7], sc[c]);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const float v = __uint_as_float(sv[c]);
-          sc[c] = j * kKTile + c < row_end ? v : -CUDART_INF_F;
-          pm[c & 7] = fmaxf(pm[c & 7], sc[c]);
-        }
-      }
-      float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                       fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
-      mx *= a.scale_log2;  // the scale is positive: max commutes with it
-      const bool grow = mx > m_run + kLazyMax;
-      // S_t(j) is complete, so is every earlier MMA of this q-tile: O_t and
-      // the P_t buffer are free to touch
-      if (__any_sync(0xffffffffu, grow) && j > 0) {
-        const float alpha = grow ? fast_exp2(m_run - mx) : 1.0f;
-#pragma unroll
-        for (int cb = 0; cb < 4; ++cb) {
-          uint32_t ov[32];
-          tc::tmem_ld32(t_row + o_col(t) + 32 * cb, ov);
-#pragma unroll
-          for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
-          tc::tmem_st32(t_row + o_col(t) + 32 * cb, ov);
-        }
-        tc::tmem_wait_st();
-        l_run *= alpha;
-      }
-      if (grow) m_run = mx;
-      const float neg_m = m_run == -CUDART_INF_F ? 0.0f : -m_run;
-      uint32_t pk[32];
+      // One pass over S_t in 32-column chunks, the next chunk's load in
+      // flight while this one is turned into P. A chunk whose max passes the
+      // running max by more than kLazyMax (log2 units) rescales O (earlier
+      // tiles) and the P chunks of this tile already written; after the first
+      // chunks of a row that is rare. Only a tile that reaches past some row's
+      // causal end masks.
+      const bool full_tile = __all_sync(0xffffffffu, (j + 1) * kKTile <= row_end);
       float ps[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) ps[i] = 0.0f;
+      uint32_t buf[2][32];
+      tc::tmem_ld32_async(t_row + s_col(t), buf[0]);
+      tc::tmem_wait_ld_into(buf[0]);
 #pragma unroll
-      for (int c = 0; c < 64; c += 2) {
-        const float p0 = fast_exp2(fmaf(sc[c], a.scale_log2, neg_m));
-        const float p1 = fast_exp2(fmaf(sc[c + 1], a.scale_log2, neg_m));
-        ps[(c >> 1) & 7] += p0 + p1;
-        pk[c >> 1] = pack_bf16x2(p0, p1);
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t(&sv)[32] = buf[ch & 1];
+        if (ch < 3) tc::tmem_ld32_async(t_row + s_col(t) + 32 * (ch + 1), buf[(ch + 1) & 1]);
+        float cm[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F};
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          float v = __uint_as_float(sv[c]);
+          if (!full_tile && j * kKTile + 32 * ch + c >= row_end) v = -CUDART_INF_F;
+          sv[c] = __float_as_uint(v);
+          cm[c & 3] = fmaxf(cm[c & 3], v);
+        }
+        const float cmax = fmaxf(fmaxf(cm[0], cm[1]), fmaxf(cm[2], cm[3])) * a.scale_log2;
+        const bool grow = cmax > m_run + kLazyMax;
+        if (__any_sync(0xffffffffu, grow)) {
+          // m_run = -inf (nothing seen yet) gives alpha = 0: nothing to keep
+          const float alpha = grow ? fast_exp2(m_run - cmax) : 1.0f;
+          // S_t(j) is complete, so is every earlier MMA of this q-tile: O_t
+          // is free to touch
+          if (j > 0) {
+#pragma unroll
+            for (int cb = 0; cb < 4; ++cb) {
+              uint32_t ov[32];
+              tc::tmem_ld32(t_row + o_col(t) + 32 * cb, ov);
+#pragma unroll
+              for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
+              tc::tmem_st32(t_row + o_col(t) + 32 * cb, ov);
+            }
+          }
+          if (ch > 0) {
+            tc::tmem_wait_st();
+            for (int pc = 0; pc < ch; ++pc) {
+              uint32_t pw[16];
+              tc::tmem_ld16(t_row + s_col(t) + 16 * pc, pw);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&pw[i]);
+                pw[i] = pack_bf16x2(__low2float(b2) * alpha, __high2float(b2) * alpha);
+              }
+              tc::tmem_st16(t_row + s_col(t) + 16 * pc, pw);
+            }
+          }
+          tc::tmem_wait_st();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) ps[i] *= alpha;
+          l_run *= alpha;
+          if (grow) m_run = cmax;
+        }
+        // p = 2^(s * scale * log2(e) - m): one FFMA and one ex2 per score;
+        // bf16 pairs go back over S_t's first 64 columns (this row's own
+        // lane; chunk ch lands on columns 16 ch.., read two chunks ago)
+        const float neg_m = m_run == -CUDART_INF_F ? 0.0f : -m_run;
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = fast_exp2(fmaf(__uint_as_float(sv[2 * i]), a.scale_log2, neg_m));
+          const float p1 = fast_exp2(fmaf(__uint_as_float(sv[2 * i + 1]), a.scale_log2, neg_m));
+          ps[i & 7] += p0 + p1;
+          pk[i] = pack_bf16x2(p0, p1);
+        }
+        tc::tmem_st16(t_row + s_col(t) + 16 * ch, pk);
+        if (ch < 3) tc::tmem_wait_ld_into(buf[(ch + 1) & 1]);
       }
       l_run += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
-      // 8 chunks of 16 B; chunk c of row r sits at chunk c ^ (r & 7)
-      unsigned char* prow = reinterpret_cast<unsigned char*>(&sm.p[t][0][0]) + row * 128;
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) =
-            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // P visible to the tensor core
+      tc::tmem_wait_st();
       tc::fence_before_sync();
       mbar_arrive_local(&sm.p_ready[t]);
     }
