@@ -289,6 +289,59 @@ QKV_API int qkv_int8_dequant_gather(
     int total_k, void* out_key, void* out_value, qkv_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * FP8 per-token-head (E4M3 codes + one fp32 scale per (token, head))
+ * ---------------------------------------------------------------------- */
+
+/* Quantise K/V per (token, head) and scatter into the paged views: the
+ * store of the fp8_per_token_head method (reference
+ * ops/triton/per_token_head_store.py:262-294 with the numerics of
+ * methods/fp8_per_token_head/semantics.py:52-66): scale = max(amax / 448,
+ * 1e-6), code = E4M3(clamp(x / scale, -448, 448)), round to nearest even.
+ *   key, value   kv_dtype [num_tokens, num_kv_heads, head_size] (head % 4 == 0)
+ *   slot_mapping slot_dtype [num_tokens]; slot < 0 skipped
+ *   k_data/v_data uint8 [num_blocks, block_size, num_kv_heads, head_size]
+ *   k_scale/v_scale f32 [num_blocks, block_size, num_kv_heads, 1] */
+QKV_API int qkv_fp8_store(const void* key, const void* value, int kv_dtype,
+                          const void* slot_mapping, int slot_dtype,
+                          int64_t num_tokens, int num_kv_heads, int head_size,
+                          int block_size, int64_t num_blocks, uint8_t* k_data,
+                          float* k_scale, uint8_t* v_data, float* v_scale,
+                          qkv_stream_t stream);
+
+/* Bytes of workspace qkv_fp8_paged_decode needs for this batch shape. */
+QKV_API size_t qkv_fp8_paged_decode_workspace(int batch, int num_heads,
+                                              int num_kv_heads, int head_size,
+                                              int block_size, int max_seq_len);
+
+/* GQA decode attention over the FP8 pages, per-token-head scales applied in
+ * the kernel (the read path the reference's method lacks): numerically the
+ * dequantise-then-attend of semantics.dequantize + fp32 softmax attention.
+ * Query / out / block table / seq_lens as for qkv_int8_paged_decode. */
+QKV_API int qkv_fp8_paged_decode(const void* query, int64_t q_stride,
+                                 const uint8_t* k_data, const float* k_scale,
+                                 const uint8_t* v_data, const float* v_scale,
+                                 const int32_t* block_table, int64_t bt_stride,
+                                 const int32_t* seq_lens, int batch,
+                                 int num_heads, int num_kv_heads, int head_size,
+                                 int block_size, int64_t num_blocks,
+                                 int max_seq_len, float scale, void* workspace,
+                                 size_t workspace_bytes, void* out,
+                                 int64_t out_stride, qkv_stream_t stream);
+
+/* Dense bf16 K/V of whole requests from the FP8 pages: bf16(code * scale)
+ * (the product rounded to fp32 first, as semantics.dequantize computes it),
+ * rows laid out as for qkv_int8_dequant_gather; head_size % 16 == 0. */
+QKV_API int qkv_fp8_dequant_gather(const uint8_t* k_data, const float* k_scale,
+                                   const uint8_t* v_data, const float* v_scale,
+                                   const int32_t* block_table, int64_t bt_stride,
+                                   const int32_t* seq_lens,
+                                   const int32_t* cu_seqlens_k, int batch,
+                                   int num_kv_heads, int head_size,
+                                   int block_size, int64_t num_blocks,
+                                   int total_k, void* out_key, void* out_value,
+                                   qkv_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * KIVI residual windows: host planner and device apply
  * ---------------------------------------------------------------------- */
 

@@ -122,6 +122,98 @@ def int8_dequant_gather(key_cache, value_cache, k_aq, v_aq, block_table, seq_len
 
 
 # ---------------------------------------------------------------------------
+# FP8 per-token-head (methods/fp8_per_token_head/semantics.py:36-72,
+# byte_cache.py:1-196)
+# ---------------------------------------------------------------------------
+
+E4M3_MAX = F32(448.0)
+FP8_SCALE_FLOOR = F32(1e-6)
+
+
+def e4m3_encode(x) -> np.ndarray:
+    """float32 -> E4M3 (fn: 1 sign, 4 exponent bits with bias 7, 3 mantissa
+    bits, subnormals, no infinities, 0x7F/0xFF NaN, max normal 448) bytes,
+    round to nearest even — the conversion torch's ``.to(float8_e4m3fn)``
+    performs. Inputs must lie in [-448, 448] (the semantics clamp first)."""
+    x = np.asarray(x, F32)
+    a = np.abs(x).astype(np.float64)
+    if np.any(a > 448.0) or np.any(np.isnan(a)):
+        raise ValueError("e4m3_encode expects finite inputs within [-448, 448]")
+    sign = (np.signbit(x)).astype(np.uint8) << 7
+    mant, exp = np.frexp(a)  # a = mant * 2^exp, mant in [0.5, 1)
+    e = exp.astype(np.int64) - 1  # a = (2 mant) * 2^e, 2 mant in [1, 2)
+    normal = (a > 0) & (e >= -6)
+    # normal: 3 mantissa bits of (a / 2^e - 1); rounding may carry into the exponent
+    frac = np.where(normal, (a / np.ldexp(1.0, np.clip(e, -6, 8)) - 1.0) * 8.0, 0.0)
+    m = np.round(frac)  # half to even
+    e_adj = np.where(m >= 8, e + 1, e)
+    m = np.where(m >= 8, 0, m)
+    norm_bits = ((e_adj + 7) << 3) | m.astype(np.int64)
+    # subnormal: units of 2^-9
+    sub = np.round(a / 2.0 ** -9).astype(np.int64)  # 8 -> 0b0001000 = 2^-6, the smallest normal
+    bits = np.where(normal, norm_bits, sub)
+    return (bits.astype(np.uint8) | sign).reshape(x.shape)
+
+
+def e4m3_decode(b) -> np.ndarray:
+    """E4M3 bytes -> float32 (exact)."""
+    b = np.asarray(b, np.uint8).astype(np.int64)
+    sign = np.where(b & 0x80, -1.0, 1.0)
+    e = (b >> 3) & 0xF
+    m = b & 0x7
+    val = np.where(e == 0, m * 2.0 ** -9, (1.0 + m / 8.0) * np.ldexp(1.0, e - 7))
+    val = np.where((e == 15) & (m == 7), np.nan, val)
+    return (sign * val).astype(F32)
+
+
+def fp8_quantize(x):
+    """``Fp8PerTokenHeadSemantics.quantize`` (semantics.py:61-66): per
+    (token, head) ``scale = max(amax / 448, 1e-6)``, ``e4m3(clamp(x / scale,
+    -448, 448))``; x ``[T, H, D]`` -> (bytes ``[T, H, D]`` uint8, scale
+    ``[T, H, 1]`` float32)."""
+    x = np.asarray(x, F32)
+    amax = np.abs(x).max(axis=-1, keepdims=True)
+    scale = np.maximum(amax / E4M3_MAX, FP8_SCALE_FLOOR).astype(F32)
+    q = np.clip(x / scale, -E4M3_MAX, E4M3_MAX).astype(F32)
+    return e4m3_encode(q), scale
+
+
+def fp8_dequantize(codes, scale):
+    """``Fp8PerTokenHeadSemantics.dequantize`` (semantics.py:68-70)."""
+    return (e4m3_decode(codes) * np.asarray(scale, F32)).astype(F32)
+
+
+def fp8_store(key, value, slots, k_data, k_scale, v_data, v_scale):
+    """Per-token-head store into the paged views (data ``[NB, blk, H, D]``
+    uint8, scale ``[NB, blk, H, 1]`` float32); slots < 0 are skipped."""
+    blk = k_data.shape[1]
+    for x, data, sc in ((key, k_data, k_scale), (value, v_data, v_scale)):
+        q, s = fp8_quantize(x)
+        for t, slot in enumerate(np.asarray(slots).tolist()):
+            if slot < 0:
+                continue
+            data[slot // blk, slot % blk] = q[t]
+            sc[slot // blk, slot % blk] = s[t]
+
+
+def fp8_dequant_gather(k_data, k_scale, v_data, v_scale, block_table, seq_lens, target_bf16: bool = True):
+    """Dense K, V ``[sum L, H, D]`` of whole requests from the fp8 pages
+    (``code * scale`` in fp32, then bf16 as the attention inputs are)."""
+    blk = k_data.shape[1]
+    ks, vs = [], []
+    bt = np.asarray(block_table)
+    for b, L in enumerate(seq_lens):
+        pos = np.arange(int(L))
+        pages, off = bt[b, pos // blk], pos % blk
+        ks.append(fp8_dequantize(k_data[pages, off], k_scale[pages, off]))
+        vs.append(fp8_dequantize(v_data[pages, off], v_scale[pages, off]))
+    H, D = k_data.shape[2:]
+    k = np.concatenate(ks) if ks else np.zeros((0, H, D), F32)
+    v = np.concatenate(vs) if vs else np.zeros((0, H, D), F32)
+    return (bf16_round(k), bf16_round(v)) if target_bf16 else (k, v)
+
+
+# ---------------------------------------------------------------------------
 # KIVI INT4 arithmetic (methods/kivi_int4/semantics.py:63-111;
 # ops/triton/kivi_pack.py:61-226)
 # ---------------------------------------------------------------------------

@@ -14,6 +14,10 @@ pin, so this script imports it read-only (``REFERENCE_ROOT``, default
   ``GEOMETRIES`` (tests/test_kivi_int4.py:1658-1664), plus tie and
   near-constant-group edge cases and ``kivi_dequant_gather_cache``
   (ops/kivi_gather.py:36-156) over the packed pages.
+* ``fp8.npz`` — ``Fp8PerTokenHeadSemantics`` quantise / dequantise / fake
+  quant (methods/fp8_per_token_head/semantics.py:52-76) and a store through the
+  reference's byte-buffer views (byte_cache.py), with a zero (token, head) and
+  E4M3 ties.
 * ``kivi_pipeline.npz`` — a multi-request write -> flush -> sync -> gather ->
   attention sequence through ``AscendKiviInt4AttentionBackendMixin.forward``
   (generic branch, methods/kivi_int4/attention_backend.py:1157-1191): bulk
@@ -331,12 +335,66 @@ def make_kivi_pipeline(kt) -> dict:
     return rec
 
 
+def make_fp8() -> dict:
+    """``Fp8PerTokenHeadSemantics`` (methods/fp8_per_token_head/semantics.py)
+    on bf16 K/V with per-(token, head) magnitudes spanning 1e-3..50, an
+    all-zero (token, head) (the 1e-6 scale floor) and exact E4M3 ties, stored
+    through the reference's byte-buffer views (byte_cache.py)."""
+    from vllm_ascend_quantized_kv_cache.methods.fp8_per_token_head.byte_cache import (
+        Fp8PerTokenHeadLayout,
+        fp8_caches_from_byte_tensors,
+    )
+    from vllm_ascend_quantized_kv_cache.methods.fp8_per_token_head.semantics import Fp8PerTokenHeadSemantics
+
+    gen = torch.Generator().manual_seed(1006)
+    T, H, D, blk, nb = 40, 4, 64, 16, 4
+    mag = torch.exp(torch.empty(T, H, 1).uniform_(-7.0, 4.0, generator=gen))
+    key = (torch.randn(T, H, D, generator=gen) * mag).to(torch.bfloat16)
+    value = (torch.randn(T, H, D, generator=gen) * mag).to(torch.bfloat16)
+    key[5, 1] = 0.0
+    # a row whose max is 448 * 2^-k scaled so x / scale lands on E4M3 midpoints
+    key[7, 2, :8] = torch.tensor([448.0, 1.0625, 3.0625, 13.0, 0.0029296875, -5.25, 0.5, 2.0 ** -10])
+    sem = Fp8PerTokenHeadSemantics(SimpleNamespace(head_size=D))
+    kq, ks = sem.quantize(key)
+    vq, vs = sem.quantize(value)
+    lay = Fp8PerTokenHeadLayout(num_blocks=nb, block_size=blk, num_kv_heads=H, head_size=D)
+    kbuf = torch.zeros(nb, blk, H, lay.bytes_per_token_head, dtype=torch.uint8)
+    vbuf = torch.zeros_like(kbuf)
+    kd, ksc, vd, vsc = fp8_caches_from_byte_tensors(kbuf, vbuf, lay)
+    slots = torch.randperm(nb * blk, generator=gen)[:T]
+    kd.view(nb * blk, H, D)[slots] = kq.view(torch.uint8)
+    ksc.view(nb * blk, H, 1)[slots] = ks
+    vd.view(nb * blk, H, D)[slots] = vq.view(torch.uint8)
+    vsc.view(nb * blk, H, 1)[slots] = vs
+    return {
+        "key": _bf16_bits(key),
+        "value": _bf16_bits(value),
+        "k_codes": kq.view(torch.uint8).numpy(),
+        "k_scale": ks.numpy(),
+        "v_codes": vq.view(torch.uint8).numpy(),
+        "v_scale": vs.numpy(),
+        "k_dequant": sem.dequantize(kq, ks).numpy(),
+        "v_fake": sem.fake_quant(value).float().numpy(),
+        "slots": slots.numpy(),
+        "k_buffer": kbuf.numpy(),
+        "v_buffer": vbuf.numpy(),
+        "geometry": np.array([T, H, D, blk, nb]),
+    }
+
+
 def main() -> None:
+    only = sys.argv[1:] and sys.argv[1] == "--only" and sys.argv[2:3]
+    if only and only[0] == "fp8":
+        _import_reference()
+        np.savez_compressed(HERE / "fp8.npz", **make_fp8())
+        print("fp8.npz", (HERE / "fp8.npz").stat().st_size)
+        return
     int8_ab, kt, gather = _import_reference()
     torch.manual_seed(0)
     np.savez_compressed(HERE / "int8.npz", **make_int8(int8_ab))
     np.savez_compressed(HERE / "kivi_pack.npz", **make_kivi_pack(kt, gather))
     np.savez_compressed(HERE / "kivi_pipeline.npz", **make_kivi_pipeline(kt))
+    np.savez_compressed(HERE / "fp8.npz", **make_fp8())
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
 

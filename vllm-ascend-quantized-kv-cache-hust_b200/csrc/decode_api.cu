@@ -28,6 +28,10 @@ int launch_kivi_gather(const DecodeParams& p, const int32_t* cu_k, int total_k, 
                        __nv_bfloat16* dense_v, cudaStream_t stream);
 int launch_int8_gather(const DecodeParams& p, const int32_t* cu_k, int total_k, __nv_bfloat16* dense_k,
                        __nv_bfloat16* dense_v, cudaStream_t stream);
+bool fp8_tma_geometry(const DecodeParams& p);
+bool fp8_tma_supported(const DecodeParams& p);
+SplitPlan plan_fp8_tma(int batch, int kvh, int max_seq_len, int sms);
+int launch_fp8_tma(const DecodeParams& p, cudaStream_t stream);
 
 namespace {
 
@@ -402,6 +406,78 @@ int qkv_int8_dequant_gather(
   p.err = device_error_ptr();
   return launch_int8_gather(p, cu_seqlens_k, total_k, static_cast<__nv_bfloat16*>(out_key),
                             static_cast<__nv_bfloat16*>(out_value), reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t qkv_fp8_paged_decode_workspace(int batch, int num_heads, int num_kv_heads, int head_size, int block_size,
+                                      int max_seq_len) {
+  using namespace qkv;
+  if (batch <= 0 || num_kv_heads <= 0 || block_size <= 0) return 0;
+  DecodeParams p{};
+  p.batch = batch;
+  p.num_heads = num_heads;
+  p.kvh = num_kv_heads;
+  p.head_size = head_size;
+  p.gqa = num_heads / num_kv_heads;
+  p.blk = block_size;
+  p.group = head_size;
+  size_t a = 0;
+  if (fp8_tma_geometry(p))
+    a = workspace_bytes(batch, num_heads, head_size, plan_fp8_tma(batch, num_kv_heads, max_seq_len, sm_count()).total);
+  const size_t b = workspace_bytes(batch, num_heads, head_size, plan_generic(p, false, max_seq_len).total);
+  return a > b ? a : b;
+}
+
+int qkv_fp8_paged_decode(const void* query, int64_t q_stride, const uint8_t* k_data, const float* k_scale,
+                         const uint8_t* v_data, const float* v_scale, const int32_t* block_table, int64_t bt_stride,
+                         const int32_t* seq_lens, int batch, int num_heads, int num_kv_heads, int head_size,
+                         int block_size, int64_t num_blocks, int max_seq_len, float scale, void* workspace,
+                         size_t workspace_bytes_, void* out, int64_t out_stride, qkv_stream_t stream) {
+  using namespace qkv;
+  int rc = check_decode_args("qkv_fp8_paged_decode", batch, num_heads, num_kv_heads, head_size, block_size,
+                             num_blocks, max_seq_len);
+  if (rc != QKV_OK) return rc;
+  if (batch == 0) return QKV_OK;
+  QKV_CHECK_ARG(query && k_data && k_scale && v_data && v_scale && block_table && seq_lens && out,
+                "qkv_fp8_paged_decode: null pointer");
+  DecodeParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(query);
+  p.q_stride = q_stride;
+  p.kc = reinterpret_cast<const int8_t*>(k_data);
+  p.vc = reinterpret_cast<const int8_t*>(v_data);
+  p.ks = k_scale;
+  p.vs = v_scale;
+  p.bt = block_table;
+  p.bt_stride = bt_stride;
+  p.seq_lens = seq_lens;
+  p.batch = batch;
+  p.num_heads = num_heads;
+  p.kvh = num_kv_heads;
+  p.head_size = head_size;
+  p.gqa = num_heads / num_kv_heads;
+  p.group = head_size;
+  p.blk = block_size;
+  p.num_blocks = num_blocks;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_stride = out_stride;
+  p.err = device_error_ptr();
+  const bool tma = fp8_tma_supported(p);
+  const SplitPlan plan =
+      tma ? plan_fp8_tma(batch, num_kv_heads, max_seq_len, sm_count()) : plan_generic(p, false, max_seq_len);
+  p.num_hist_splits = plan.hist_splits;
+  p.split_tokens = plan.split_tokens;
+  p.splits_total = plan.total;
+  const size_t need = workspace_bytes(batch, num_heads, head_size, plan.total);
+  if (need > 0) {
+    if (workspace == nullptr || workspace_bytes_ < need)
+      return set_error(QKV_ERR_WORKSPACE, "qkv_fp8_paged_decode: workspace needs " + std::to_string(need) +
+                                              " bytes");
+    p.ws_acc = static_cast<float*>(workspace);
+    p.ws_ml = p.ws_acc + static_cast<size_t>(batch) * num_heads * plan.total * head_size;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (tma) return launch_fp8_tma(p, s);
+  return launch_decode_generic(p, kFp8Pages, s);
 }
 
 }  // extern "C"

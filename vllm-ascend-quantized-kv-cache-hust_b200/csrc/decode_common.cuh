@@ -58,7 +58,7 @@ struct DecodeParams {
 };
 
 // Where a decode/prefill kernel reads K and V from.
-enum SourceMode : int { kInt8Pages = 0, kKiviPages = 1, kDense = 2 };
+enum SourceMode : int { kInt8Pages = 0, kKiviPages = 1, kDense = 2, kFp8Pages = 3 };
 
 struct SplitPlan {
   int hist_splits;

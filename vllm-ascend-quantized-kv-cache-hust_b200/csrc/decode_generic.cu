@@ -14,6 +14,8 @@
 
 #include <atomic>
 
+#include <cuda_fp8.h>
+
 #include "decode_common.cuh"
 
 namespace qkv {
@@ -98,6 +100,15 @@ __device__ __forceinline__ void stage_rows(float* tile, int ld, const DecodePara
             const int64_t si = vrow * (D / p.group) + d / p.group;
             dst[d] = kivi_dequant((w >> (4 * (d & 7))) & 0xFu, p.vs[si], p.vm[si]);
           }
+        }
+      } else if constexpr (MODE == kFp8Pages) {
+        // E4M3 codes [NB, blk, KVH, D] and one fp32 scale per (token, head)
+        const int64_t rowi = (page * p.blk + off) * kvh + h;
+        const uint8_t* row8 = reinterpret_cast<const uint8_t*>(IS_K ? p.kc : p.vc) + rowi * D;
+        const float sc8 = (IS_K ? p.ks : p.vs)[rowi];
+        for (int d = lane; d < D; d += 32) {
+          const __half_raw hr = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(row8[d]), __NV_E4M3);
+          dst[d] = __fmul_rn(__half2float(__half(hr)), sc8);
         }
       } else {
         const int8_t* row8 = (IS_K ? p.kc : p.vc) + ((page * p.blk + off) * kvh + h) * D;
@@ -300,12 +311,15 @@ int ensure_generic_smem(int mode, size_t bytes) {
   static std::atomic<uint64_t> done{0};
   int dev = 0;
   cudaGetDevice(&dev);
-  const uint64_t bit = 1ull << ((3 * dev + mode) & 63);
+  const uint64_t bit = 1ull << ((4 * dev + mode) & 63);
   if (done.load() & bit) return QKV_OK;
   cudaError_t e;
   const int limit = 160 * 1024;
   if (mode == kKiviPages)
     e = cudaFuncSetAttribute(decode_generic_kernel<kKiviPages>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, limit);
+  else if (mode == kFp8Pages)
+    e = cudaFuncSetAttribute(decode_generic_kernel<kFp8Pages>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, limit);
   else if (mode == kInt8Pages)
     e = cudaFuncSetAttribute(decode_generic_kernel<kInt8Pages>,
@@ -332,6 +346,8 @@ int launch_decode_generic_splits(const DecodeParams& p, int mode, int num_splits
   if (rc != QKV_OK) return rc;
   if (mode == kKiviPages)
     decode_generic_kernel<kKiviPages><<<grid, kGenThreads, smem, stream>>>(p);
+  else if (mode == kFp8Pages)
+    decode_generic_kernel<kFp8Pages><<<grid, kGenThreads, smem, stream>>>(p);
   else if (mode == kInt8Pages)
     decode_generic_kernel<kInt8Pages><<<grid, kGenThreads, smem, stream>>>(p);
   else

@@ -1,8 +1,9 @@
 """Quantized-KV dtype literal -> quantisation mode -> storage layout.
 
 The contract of the reference's layer 0 (dtypes.py:15-94 of
-vllm_ascend_quantized_kv_cache): the two CLI literals this package serves,
-``int8`` and ``kivi_int4``, and fail-closed resolution of everything else.
+vllm_ascend_quantized_kv_cache): the CLI literals this package serves,
+``int8``, ``kivi_int4`` and ``fp8_per_token_head``, and fail-closed resolution
+of everything else.
 Pure Python, importable anywhere.
 """
 
@@ -18,13 +19,17 @@ class KVQuantMode(IntEnum):
     NONE = 0
     INT8_PER_TENSOR = 8
     KIVI_INT4 = 9
+    FP8_PER_TOKEN_HEAD = 10
 
 
 def get_kv_quant_mode(dtype: str) -> KVQuantMode:
-    """``int8`` / ``kivi_int4`` -> their mode; any other literal -> NONE."""
-    return {"int8": KVQuantMode.INT8_PER_TENSOR, "kivi_int4": KVQuantMode.KIVI_INT4}.get(
-        dtype, KVQuantMode.NONE
-    )
+    """``int8`` / ``kivi_int4`` / ``fp8_per_token_head`` -> their mode; any
+    other literal -> NONE."""
+    return {
+        "int8": KVQuantMode.INT8_PER_TENSOR,
+        "kivi_int4": KVQuantMode.KIVI_INT4,
+        "fp8_per_token_head": KVQuantMode.FP8_PER_TOKEN_HEAD,
+    }.get(dtype, KVQuantMode.NONE)
 
 
 def is_quantized_kv_cache(dtype: str) -> bool:
@@ -51,7 +56,9 @@ class KVCacheLayout:
 
 def resolve_layout(dtype: str, head_size: int) -> KVCacheLayout:
     """``int8``: int8 storage, last dim = head_size; ``kivi_int4``: uint8,
-    head_size / 2; anything else raises ValueError."""
+    head_size / 2; ``fp8_per_token_head``: uint8 E4M3 bytes, head_size (a
+    multiple of 4; the fp32 scales are budgeted by the method's byte layout);
+    anything else raises ValueError."""
     mode = get_kv_quant_mode(dtype)
     if mode is KVQuantMode.INT8_PER_TENSOR:
         if head_size <= 0:
@@ -59,6 +66,13 @@ def resolve_layout(dtype: str, head_size: int) -> KVCacheLayout:
         return KVCacheLayout(dtype, head_size, "int8", head_size, mode)
     if mode is KVQuantMode.KIVI_INT4:
         return KVCacheLayout(dtype, head_size, "uint8", int4_packed_dim(head_size), mode)
+    if mode is KVQuantMode.FP8_PER_TOKEN_HEAD:
+        if head_size <= 0 or head_size % 4:
+            raise ValueError(
+                "fp8_per_token_head requires head_size positive and divisible "
+                f"by 4 (fp32 scale alignment), got {head_size}"
+            )
+        return KVCacheLayout(dtype, head_size, "uint8", head_size, mode)
     raise ValueError(f"dtype is not a registered quantized KV layout: {dtype}")
 
 

@@ -5,6 +5,7 @@ launches one of the sm_100a kernels on the current CUDA stream; none has a CPU
 fallback.
 """
 
+from .fp8 import fp8_dequant_gather, fp8_paged_decode, fp8_store
 from .int8 import int8_calc_scales, int8_dequant_gather, int8_paged_decode, int8_quant_store
 from .kivi_decode import kivi_paged_decode
 from .kivi_gather import kivi_dequant_gather
@@ -13,6 +14,9 @@ from .prefill import dense_prefill
 
 __all__ = [
     "dense_prefill",
+    "fp8_dequant_gather",
+    "fp8_paged_decode",
+    "fp8_store",
     "int8_calc_scales",
     "int8_dequant_gather",
     "int8_paged_decode",

@@ -121,6 +121,21 @@ SIGNATURES: dict[str, tuple] = {
             c_int, c_int, c_int, c_int, c_int, c_i64, c_float, c_vp, c_size, c_vp, c_i64, c_vp,
         ],
     ),
+    "qkv_fp8_store": (
+        c_int, [c_vp, c_vp, c_int, c_vp, c_int, c_i64, c_int, c_int, c_int, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp],
+    ),
+    "qkv_fp8_paged_decode_workspace": (c_size, [c_int, c_int, c_int, c_int, c_int, c_int]),
+    "qkv_fp8_paged_decode": (
+        c_int,
+        [
+            c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_int, c_int, c_int, c_int, c_int, c_i64,
+            c_int, c_float, c_vp, c_size, c_vp, c_i64, c_vp,
+        ],
+    ),
+    "qkv_fp8_dequant_gather": (
+        c_int,
+        [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_int, c_int, c_int, c_int, c_i64, c_int, c_vp, c_vp, c_vp],
+    ),
     "qkv_int8_dequant_gather": (
         c_int,
         [
