@@ -22,9 +22,11 @@ from qkv_b200.methods.base import MethodConfig
 
 
 def test_methods_and_dtypes():
-    assert kv_methods.list() == ["int8_dynamic", "kivi_int4"]
+    # the reference's methods package registers all three (methods/__init__.py)
+    assert kv_methods.list() == ["fp8_per_token_head", "int8_dynamic", "kivi_int4"]
     assert kv_methods.describe("int8_dynamic")["dtype"] == "int8"
     assert kv_methods.describe("kivi_int4")["dtype"] == "kivi_int4"
+    assert kv_methods.describe("fp8_per_token_head")["dtype"] == "fp8_per_token_head"
     with pytest.raises(ValueError, match="unknown quantized KV method"):
         kv_methods.get("fp8_e4m3")
 
@@ -147,6 +149,10 @@ def test_dispatch_selects_plugin_only_for_quantized_dtypes(host_stack):
     from qkv_b200.methods.int8_dynamic.attention_backend import AscendInt8AttentionBackendMixin
 
     assert issubclass(be.get_impl_cls(), AscendInt8AttentionBackendMixin)
+    host_stack.cc.cache_dtype = "fp8_per_token_head"
+    from qkv_b200.methods.fp8_per_token_head.attention_backend import AscendFp8PerTokenHeadAttentionBackendMixin
+
+    assert issubclass(be.get_impl_cls(), AscendFp8PerTokenHeadAttentionBackendMixin)
     # idempotent install
     kv_methods.activate("int8_dynamic", host="vllm_ascend_hust")
     host_stack.cc.cache_dtype = "auto"

@@ -133,3 +133,67 @@ def test_gather_bit_exact():
     assert np.array_equal(dk.float().cpu().numpy().view(np.uint32), wk.view(np.uint32))
     assert np.array_equal(dv.float().cpu().numpy().view(np.uint32), wv.view(np.uint32))
     assert_no_device_error()
+
+
+def test_fp8_mixin_prompts_chunks_and_decode_match_oracle():
+    """The FP8 mixin over the host's two byte buffers: a PrefillNoCache batch
+    (attention over the raw K/V), a ChunkedPrefill batch with two decode rows
+    and two chunks over cached tokens, a PrefillCacheHit batch and a
+    DecodeOnly batch over the pages; every row matches the oracle's
+    dequantise-then-attend over the pages after the write."""
+    from types import SimpleNamespace
+
+    from qkv_b200.methods.fp8_per_token_head.attention_backend import AscendFp8PerTokenHeadAttentionBackendMixin
+    from qkv_b200.methods.fp8_per_token_head.byte_cache import Fp8PerTokenHeadLayout
+
+    H, Hq, D, blk, nb = 8, 32, 128, 128, 64
+
+    class Impl(AscendFp8PerTokenHeadAttentionBackendMixin):
+        pass
+
+    impl = Impl()
+    impl.num_heads, impl.num_kv_heads, impl.head_size, impl.num_queries_per_kv = Hq, H, D, Hq // H
+    impl.scale = D ** -0.5
+    lay = Fp8PerTokenHeadLayout(num_blocks=nb, block_size=blk, num_kv_heads=H, head_size=D)
+    raw = torch.zeros(2, nb, blk, H, lay.bytes_per_token_head, dtype=torch.uint8, device=dev())
+    bt = torch.arange(48, dtype=torch.int32).reshape(4, 12)
+    rng = np.random.default_rng(81)
+    bf = lambda *s: torch.from_numpy(O.bf16_round(rng.standard_normal(s).astype(np.float32))).to(dev()).bfloat16()
+
+    def slots(b, lo, hi):
+        return torch.tensor([int(bt[b, p // blk]) * blk + p % blk for p in range(lo, hi)], device=dev())
+
+    before = [0, 0, 0, 0]
+
+    def run(state, reqs, ql, **extra):
+        lens = [before[b] + n for b, n in zip(reqs, ql)]
+        T = sum(ql)
+        q, k, v = bf(T, Hq, D), bf(T, H, D), bf(T, H, D)
+        md = SimpleNamespace(
+            attn_state=SimpleNamespace(name=state), actual_seq_lengths_q=np.cumsum(ql).tolist(),
+            seq_lens_list=lens, slot_mapping=torch.cat([slots(b, before[b], L) for b, L in zip(reqs, lens)]),
+            block_tables=bt[reqs].to(dev()), num_actual_tokens=T, causal=True, **extra,
+        )
+        out = torch.full((T, Hq, D), float("nan"), dtype=torch.bfloat16, device=dev())
+        impl.forward(None, q, k, v, raw, md, out)
+        for b, L in zip(reqs, lens):
+            before[b] = L
+        return q, k, v, out, lens
+
+    prompts = [700, 300, 1000, 129]
+    q, k, v, out, _ = run("PrefillNoCache", [0, 1, 2, 3], prompts)
+    want = O.dense_attention(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(),
+                             prompts, prompts, D ** -0.5, causal=True)
+    close(out.float().cpu().numpy(), want)
+    views = [t.cpu().numpy() for t in (impl.k_data, impl.k_scale, impl.v_data, impl.v_scale)]
+    for state, reqs, ql, extra in (
+        ("ChunkedPrefill", [0, 1, 2, 3], [1, 1, 64, 33], dict(num_decode_tokens=2, num_decodes=2, num_prefills=2)),
+        ("PrefillCacheHit", [2, 0], [50, 1], {}),
+        ("DecodeOnly", [0, 1, 2, 3], [1, 1, 1, 1], {}),
+    ):
+        q, _, _, out, lens = run(state, reqs, ql, **extra)
+        views = [t.cpu().numpy() for t in (impl.k_data, impl.k_scale, impl.v_data, impl.v_scale)]
+        dk, dv = O.fp8_dequant_gather(*views, bt[reqs].numpy(), lens, target_bf16=True)
+        want = O.dense_attention(q.float().cpu().numpy(), dk, dv, ql, lens, D ** -0.5, causal=True)
+        close(out.float().cpu().numpy(), want)
+    assert_no_device_error()

@@ -2,9 +2,10 @@
 adapters/vllm_ascend_hust/backend.py:127-158).
 
 Patches the host's ``AscendAttentionBackend.get_impl_cls`` once (idempotent,
-marker attribute): ``--kv-cache-dtype int8`` / ``kivi_int4`` select the
-B200 mixins composed over the live host implementation, every other dtype
-goes to the original factory. Context parallel is refused for both dtypes.
+marker attribute): ``--kv-cache-dtype int8`` / ``kivi_int4`` (and
+``fp8_per_token_head``, on hosts that accept that literal) select the B200
+mixins composed over the live host implementation, every other dtype goes to
+the original factory. Context parallel is refused for all of them.
 """
 
 from __future__ import annotations
@@ -17,6 +18,7 @@ _DISPATCH_MARKER = "_quantized_kv_plugin_dispatch_installed"
 _ORIGINAL_IMPL_GETTER = "_quantized_kv_original_get_impl_cls"
 _INT8_CACHE_DTYPE = "int8"
 _KIVI_CACHE_DTYPE = "kivi_int4"
+_FP8_CACHE_DTYPE = "fp8_per_token_head"
 
 
 def _require_cache_dtype(expected: str) -> None:
@@ -82,9 +84,21 @@ def _build_kivi_impl_cls() -> type:
     return AscendKiviInt4KvAttentionImpl
 
 
+@cache
+def _build_fp8_impl_cls() -> type:
+    HostImpl = _host_attention_v1().AscendAttentionBackendImpl
+    from ...methods.fp8_per_token_head.attention_backend import AscendFp8PerTokenHeadAttentionBackendMixin
+
+    class AscendFp8PerTokenHeadKvAttentionImpl(AscendFp8PerTokenHeadAttentionBackendMixin, HostImpl):
+        """FP8 per-token-head KV impl: B200 kernels over the live host surface."""
+
+    return AscendFp8PerTokenHeadKvAttentionImpl
+
+
 _IMPL_BUILDERS: dict[str, Callable[[], type]] = {
     _INT8_CACHE_DTYPE: _build_int8_impl_cls,
     _KIVI_CACHE_DTYPE: _build_kivi_impl_cls,
+    _FP8_CACHE_DTYPE: _build_fp8_impl_cls,
 }
 
 
@@ -131,6 +145,7 @@ def _build_backend_cls(cache_dtype: str, class_name: str) -> type:
 _BACKENDS_BY_CLASS_NAME = {
     "AscendInt8KvAttentionBackend": _INT8_CACHE_DTYPE,
     "AscendKiviInt4KvAttentionBackend": _KIVI_CACHE_DTYPE,
+    "AscendFp8PerTokenHeadKvAttentionBackend": _FP8_CACHE_DTYPE,
 }
 
 

@@ -1,5 +1,5 @@
 """Quantisation methods; importing this package registers their metadata only."""
 
-from . import int8_dynamic, kivi_int4  # noqa: F401  (registration side effect)
+from . import fp8_per_token_head, int8_dynamic, kivi_int4  # noqa: F401  (registration side effect)
 
 __all__ = ["int8_dynamic", "kivi_int4"]
