@@ -71,7 +71,7 @@ def parse():
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 chunked-prefill leg")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the request count (small cases for ncu captures)")
-    ap.add_argument("--only", choices=("kivi", "int8", "config4"), default=None,
+    ap.add_argument("--only", choices=("kivi", "int8", "config4", "fp8"), default=None,
                     help="run just one decode kernel loop (for ncu captures)")
     return ap.parse_args()
 
@@ -769,6 +769,11 @@ def main():
     if args.only == "config4":
         print(json.dumps({"only": "config4", **run_config4_leg(device, args)}), flush=True)
         return
+    if args.only == "fp8":
+        res = run_fp8_leg(cfg3, rank, world, device, args)
+        if rank == 0:
+            print(json.dumps({"only": "fp8", **res}), flush=True)
+        return
     w = build_workload(cfg, rank, world, device)
     out = torch.empty(w.B, w.Hql, w.D, dtype=torch.bfloat16, device=device)
     gathered = torch.empty(world, w.B, w.Hql, w.D, dtype=torch.bfloat16, device=device) if world > 1 else None
@@ -852,6 +857,9 @@ def main():
     int8 = None
     if not args.no_int8:
         int8 = run_int8_leg(cfg3, rank, world, device, args)
+    fp8 = None
+    if not args.no_int8:
+        fp8 = run_fp8_leg(cfg3, rank, world, device, args)
     config4 = None
     if world == 1 and not args.no_config4:
         config4 = run_config4_leg(device, args)
@@ -907,6 +915,7 @@ def main():
             "pack": pack,
             "int8_config3": int8,
             "config4": config4,
+            "fp8_decode": fp8,
             "e2e": None if e2e_dt is None else {
                 "value": w.B / e2e_dt, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_dt * 1e3, "api": "AscendKiviInt4AttentionBackendMixin.forward (DecodeOnly)"},
@@ -948,6 +957,58 @@ def run_int8_leg(cfg3, rank, world, device, args):
             "tokens_per_s_per_layer": cfg3["batch"] / (ms8 * 1e-3), "ms_per_step": ms8,
             "bytes_per_launch": by, "hbm_gbs": gbs, "frac_of_measured_hbm": gbs / peak,
             "frac_of_8tbs": gbs / 8000.0}
+
+
+def run_fp8_leg(cfg3, rank, world, device, args):
+    """FP8 per-token-head decode at config 3's shape (64 x 8192, Hq 32 / KVH
+    8, head 128; the reference has no read path for this method, so no
+    BASELINE config names it): K/V ~ N(0, 1) x a per-(token, head) magnitude
+    e^U(-1, 1), stored by ``fp8_store`` through a permuted block table."""
+    import torch
+    import torch.distributed as dist
+
+    from qkv_b200.ops import fp8_paged_decode, fp8_store
+
+    B, L, Hq, H, D, blk = (cfg3[k] for k in ("batch", "context", "num_heads", "num_kv_heads", "head_size",
+                                            "block_size"))
+    Hl, Hql = H // world, Hq // world
+    pages = L // blk
+    nb = B * pages
+    gen = torch.Generator(device=device).manual_seed(4322)
+    cpu_gen = torch.Generator().manual_seed(4322)
+    bt = torch.randperm(nb, generator=cpu_gen).view(B, pages).to(torch.int32)
+    kd = torch.empty(nb, blk, Hl, D, dtype=torch.uint8, device=device)
+    vd = torch.empty_like(kd)
+    ks = torch.empty(nb, blk, Hl, 1, dtype=torch.float32, device=device)
+    vs = torch.empty_like(ks)
+    pos = torch.arange(L, device=device)
+    for b in range(B):
+        mag = torch.exp(torch.rand(L, Hl, 1, generator=gen, device=device) * 2 - 1)
+        k = (torch.randn(L, Hl, D, generator=gen, device=device) * mag).to(torch.bfloat16)
+        v = (torch.randn(L, Hl, D, generator=gen, device=device) * mag).to(torch.bfloat16)
+        fp8_store(k, v, bt[b].to(device).long()[pos // blk] * blk + pos % blk, kd, ks, vd, vs)
+    q = torch.randn(B, Hql, D, generator=gen, device=device).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    bt_dev = bt.to(device)
+    sl = torch.full((B,), L, dtype=torch.int32, device=device)
+
+    def decode():
+        fp8_paged_decode(q, kd, ks, vd, vs, bt_dev, sl, D ** -0.5, out, L)
+
+    ms = time_loop(decode, args.steps, args.warmup, device)
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    peak = measured_peaks().get("hbm_gbs") or 6650.0
+    # codes + one fp32 scale per (token, head) and side, q, out, block table
+    by = B * (Hl * L * 2 * (D + 4) + 2 * Hql * D * 2 + 4 * pages)
+    gbs = by / (ms * 1e-3) / 1e9
+    del kd, vd, ks, vs
+    torch.cuda.empty_cache()
+    return {"workload": "FP8 per-token-head decode at config 3's shape: 64 x 8192, Hq 32 / KVH 8, head 128",
+            "tokens_per_s_per_layer": B / (ms * 1e-3), "ms_per_step": ms, "bytes_per_launch": by,
+            "hbm_gbs": gbs, "frac_of_measured_hbm": gbs / peak}
 
 
 def run_only_int8(cfg3, rank, world, device, args):
