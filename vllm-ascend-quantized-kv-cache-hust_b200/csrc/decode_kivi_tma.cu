@@ -55,7 +55,14 @@ constexpr int kHeads = 8;
 constexpr int kTokW = kBlk / kWarps;  // tokens per warp per page
 constexpr int kMaxPages = 64;         // pages per split (ids staged in smem)
 constexpr int kStages = 2;
-constexpr float kInv16 = 0.0625f;
+// The int4 codes enter the MMAs as fp16 SUBNORMALS: masking a nibble into the
+// low mantissa bits of an fp16 half gives n * 2^-24 exactly (n * 16 * 2^-24
+// for a high nibble), one AND per pair and no bias to remove. The tensor core
+// takes subnormal inputs exactly; the fp32 accumulators are scaled back once.
+constexpr float kUnsub = 16777216.0f;        // 2^24: low-nibble rows
+constexpr float kUnsubHi = 1048576.0f;       // 2^20: high-nibble rows (2^24 / 16)
+__device__ __forceinline__ uint32_t nib_lo_sub(uint32_t x) { return x & 0x000F000Fu; }
+__device__ __forceinline__ uint32_t nib_hi_sub(uint32_t x) { return x & 0x00F000F0u; }
 constexpr float kLazy = 4.0f;  // log2 headroom of the running max
 
 template <int NG>
@@ -490,8 +497,8 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
       for (int j = 0; j < 2; ++j) {
         const uint32_t x01 = prmt(w0, w1, ksel[j]);
         const uint32_t x23 = prmt(w2, w3, ksel[j]);
-        mma16816(sc[j], hsub2_1024(nib_lo(x01)), hsub2_1024(nib_hi(x01)), hsub2_1024(nib_lo(x23)),
-                 hsub2_1024(nib_hi(x23)), bq[kk][0], bq[kk][1]);
+        mma16816(sc[j], nib_lo_sub(x01), nib_hi_sub(x01), nib_lo_sub(x23), nib_hi_sub(x23), bq[kk][0],
+                 bq[kk][1]);
       }
     }
     // scores in log2 units: [j][0..1] low-nibble token, heads 2t, 2t+1; [j][2..3] its +1
@@ -499,8 +506,8 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
     for (int j = 0; j < 2; ++j)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        sc[j][e] += cmn[e];
-        sc[j][2 + e] = fmaf(sc[j][2 + e], kInv16, cmn[e]);
+        sc[j][e] = fmaf(sc[j][e], kUnsub, cmn[e]);
+        sc[j][2 + e] = fmaf(sc[j][2 + e], kUnsubHi, cmn[e]);
       }
     const bool partial = valid < kTokW;
     if (partial) {
@@ -621,8 +628,8 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
         const uint32_t x0 = prmt(wa0[hp], wb0[hp], sel);
         const uint32_t x1 = prmt(wa1[hp], wb1[hp], sel);
         const int gg = NG == 2 ? hp : 0;
-        mma16816(o[mt], hsub2_1024(nib_lo(x0)), hsub2_1024(nib_hi(x0)), hsub2_1024(nib_lo(x1)),
-                 hsub2_1024(nib_hi(x1)), pb[j][gg][0], pb[j][gg][1]);
+        mma16816(o[mt], nib_lo_sub(x0), nib_hi_sub(x0), nib_lo_sub(x1), nib_hi_sub(x1), pb[j][gg][0],
+                 pb[j][gg][1]);
       }
     }
   }
@@ -656,8 +663,8 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int head = 2 * t + e;
-      mo[(warp * kHeads + head) * kD + d_lo] = o[mt][e] + mn_acc[e][gg];
-      mo[(warp * kHeads + head) * kD + d_lo + 1] = fmaf(o[mt][2 + e], kInv16, mn_acc[e][gg]);
+      mo[(warp * kHeads + head) * kD + d_lo] = fmaf(o[mt][e], kUnsub, mn_acc[e][gg]);
+      mo[(warp * kHeads + head) * kD + d_lo + 1] = fmaf(o[mt][2 + e], kUnsubHi, mn_acc[e][gg]);
     }
   }
   if (g == 0) {
