@@ -92,20 +92,25 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmap_
   const uint32_t raw = smem_u32(smem_raw);
   PrefillSmem& sm = *reinterpret_cast<PrefillSmem*>(smem_raw + (((raw + 1023u) & ~1023u) - raw));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int h = blockIdx.y;
+  const int h = static_cast<int>(blockIdx.x % a.kvh);
   const int G = a.gqa, TPT = a.tokens_per_tile;
 
-  // ---- which request and pair of q-tiles (pairs never straddle requests)
+  // ---- which request and pair of q-tiles (pairs never straddle requests).
+  // Blocks start in index order: the KV head is the fastest-moving index and
+  // each request's pairs are taken last-first (causal: the last pairs see the
+  // most keys), so the longest work items start first and the last wave is
+  // made of short ones.
   int r = -1, pair = 0;
   {
+    const int rank = static_cast<int>(blockIdx.x / a.kvh);
     int acc = 0;
     for (int i = 0; i < a.num_reqs; ++i) {
       const int ql = a.cu_q[i + 1] - a.cu_q[i];
       const int nt = ql > 0 ? (ql + TPT - 1) / TPT : 0;
       const int np = (nt + 1) / 2;
-      if (static_cast<int>(blockIdx.x) < acc + np) {
+      if (rank < acc + np) {
         r = i;
-        pair = blockIdx.x - acc;
+        pair = np - 1 - (rank - acc);
         break;
       }
       acc += np;
@@ -440,8 +445,9 @@ int launch_prefill_tc(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv
   a.scale_log2 = scale * 1.4426950408889634f;
   a.out = out;
   a.err = device_error_ptr();
-  const int pairs_upper = ((total_q + tpt - 1) / tpt + num_reqs + 1) / 2 + num_reqs;
-  dim3 grid(pairs_upper, kvh);
+  const int64_t pairs_upper = ((total_q + tpt - 1) / tpt + num_reqs + 1) / 2 + num_reqs;
+  if (pairs_upper * kvh > 0x7FFFFFFFll) return set_error(QKV_ERR_INVALID, "qkv_dense_prefill: too many q-tiles");
+  dim3 grid(static_cast<unsigned>(pairs_upper * kvh));
   prefill_tc_kernel<<<grid, kThreads, kPrefillSmem, stream>>>(a, tq, tk, tv);
   QKV_CHECK_LAUNCH("prefill_tc_kernel");
   return QKV_OK;
