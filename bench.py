@@ -71,7 +71,7 @@ def parse():
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 chunked-prefill leg")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the request count (small cases for ncu captures)")
-    ap.add_argument("--only", choices=("kivi", "int8", "config4", "fp8"), default=None,
+    ap.add_argument("--only", choices=("kivi", "int8", "config4", "fp8", "small"), default=None,
                     help="run just one decode kernel loop (for ncu captures)")
     return ap.parse_args()
 
@@ -243,23 +243,17 @@ def build_workload(cfg, rank, world, device, seed=1234):
     )
 
 
-def build_config4(cfg, device, seed=1004):
-    """Config 4 (chunked prefill mixed with decode, KIVI g 64): 2 requests
-    whose 2048-token chunk lands on 6144 cached tokens (history 8192 after the
-    chunk's write) and 30 decode requests at L ~ U{2048..16384}, every cache
-    in the state the reference's writes leave (int4 history + bf16 window),
-    K/V ~ N(0,1) bf16 with x10 key outliers on 2% of (head, channel) pairs."""
+def build_kivi_requests(lens, H, D, g, r, blk, device, cpu_gen, gen, outlier_frac=0.02, factor=10.0):
+    """KIVI caches of requests with the given lengths in the state the
+    reference's writes leave: int4 history of the first ``((L - 1) // r) * r``
+    positions packed through ``kivi_pack_*`` over a permuted block table, the
+    rest in the bf16 windows (row b = request b). K/V ~ N(0,1) bf16 with
+    ``factor`` x key outliers on ``outlier_frac`` of (head, channel) pairs."""
     import torch
 
     from qkv_b200.methods.kivi_int4.byte_cache import KiviByteCacheLayout, kivi_caches_from_byte_tensors
     from qkv_b200.ops import kivi_pack_key_cache, kivi_pack_value_cache
 
-    Hq, H, D, g, r, blk = (cfg[k] for k in ("num_heads", "num_kv_heads", "head_size", "group_size", "residual",
-                                           "block_size"))
-    cpu_gen = torch.Generator().manual_seed(seed)
-    gen = torch.Generator(device=device).manual_seed(seed)
-    lens = [cfg["cached"] + cfg["chunk"]] * cfg["prefills"] + torch.randint(
-        cfg["decode_min"], cfg["decode_max"] + 1, (cfg["decodes"],), generator=cpu_gen).tolist()
     B = len(lens)
     pages = [(L + blk - 1) // blk for L in lens]
     maxp = max(pages)
@@ -271,7 +265,7 @@ def build_config4(cfg, device, seed=1004):
     perm = torch.randperm(nb, generator=cpu_gen)
     bt = torch.zeros(B, maxp, dtype=torch.int32)
     kscale = torch.ones(H * D)
-    kscale[torch.randperm(H * D, generator=cpu_gen)[:max(1, int(0.02 * H * D))]] = 10.0
+    kscale[torch.randperm(H * D, generator=cpu_gen)[:max(1, int(outlier_frac * H * D))]] = factor
     kscale = kscale.view(H, D).to(device)
     rk = torch.zeros(B + 1, r, H, D, dtype=torch.bfloat16, device=device)
     rv = torch.zeros_like(rk)
@@ -286,11 +280,36 @@ def build_config4(cfg, device, seed=1004):
         v = torch.randn(L, H, D, generator=gen, device=device).to(torch.bfloat16)
         pos = torch.arange(L, device=device)
         slots = bt[b].to(device).long()[pos // blk] * blk + pos % blk
-        kivi_pack_key_cache(k[:hist].contiguous(), slots[:hist].contiguous(), *views[:3], g, validate_slots=False)
-        kivi_pack_value_cache(v[:hist].contiguous(), slots[:hist].contiguous(), *views[3:], g)
+        if hist:
+            kivi_pack_key_cache(k[:hist].contiguous(), slots[:hist].contiguous(), *views[:3], g,
+                                validate_slots=False)
+            kivi_pack_value_cache(v[:hist].contiguous(), slots[:hist].contiguous(), *views[3:], g)
         rk[b, :res] = k[hist:]
         rv[b, :res] = v[hist:]
         state.append([b, 0, res, 0, res, L])
+    torch.cuda.synchronize(device)
+    return SimpleNamespace(views=views, rk=rk, rv=rv, bt=bt, state=torch.tensor(state, dtype=torch.int32),
+                           kbuf=kbuf, vbuf=vbuf)
+
+
+def build_config4(cfg, device, seed=1004):
+    """Config 4 (chunked prefill mixed with decode, KIVI g 64): 2 requests
+    whose 2048-token chunk lands on 6144 cached tokens (history 8192 after the
+    chunk's write) and 30 decode requests at L ~ U{2048..16384}, every cache
+    in the state the reference's writes leave (int4 history + bf16 window),
+    K/V ~ N(0,1) bf16 with x10 key outliers on 2% of (head, channel) pairs."""
+    import torch
+
+    Hq, H, D, g, r, blk = (cfg[k] for k in ("num_heads", "num_kv_heads", "head_size", "group_size", "residual",
+                                           "block_size"))
+    cpu_gen = torch.Generator().manual_seed(seed)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    lens = [cfg["cached"] + cfg["chunk"]] * cfg["prefills"] + torch.randint(
+        cfg["decode_min"], cfg["decode_max"] + 1, (cfg["decodes"],), generator=cpu_gen).tolist()
+    B = len(lens)
+    kv = build_kivi_requests(lens, H, D, g, r, blk, device, cpu_gen, gen)
+    views, rk, rv, bt = kv.views, kv.rk, kv.rv, kv.bt
+    state = kv.state.tolist()
     torch.cuda.synchronize(device)
     P, C = cfg["prefills"], cfg["chunk"]
     # query token i of a chunk attends to its causal length
@@ -396,6 +415,75 @@ def run_config4_leg(device, args):
             "decode_ms": ms_dec, "decode_bytes": c.decode_bytes, "decode_gbs": gbs, "decode_frac_of_hbm": gbs / hbm}
 
 
+def run_small_configs(device, args):
+    """Configs 1 and 2 (1 GPU): the small, latency-bound decode steps of
+    BASELINE.json. Config 1: INT8, 4 requests at 512 / 1024 / 1536 / 2048,
+    Hq 32 / KVH 8, K/V ~ N(0,1) with 4 fixed channels per head x20, scales
+    from the four prompts as one prefill batch. Config 2: KIVI INT4, 8
+    requests at L ~ U{1024..8192}, Hq 40 / KVH 8 (5 query heads per KV head),
+    g 128, r 128, keys with x10 outliers on 2% of (head, channel) pairs. Each
+    decode step is replayed from a CUDA graph and timed with CUDA events; both
+    caches fit in L2, so L2 is flushed before every timed step."""
+    import torch
+
+    from qkv_b200.ops import int8_calc_scales, int8_paged_decode, int8_quant_store, kivi_paged_decode
+
+    peak = measured_peaks().get("hbm_gbs") or 6650.0
+    out = {}
+    # ---- config 1
+    gen = torch.Generator(device=device).manual_seed(1001)
+    cpu_gen = torch.Generator().manual_seed(1001)
+    lens, Hq, H, D, blk = [512, 1024, 1536, 2048], 32, 8, 128, 128
+    scale = torch.ones(H, D)
+    for h in range(H):
+        scale[h, torch.randperm(D, generator=cpu_gen)[:4]] = 20.0
+    scale = scale.to(device)
+    T = sum(lens)
+    k = (torch.randn(T, H, D, generator=gen, device=device) * scale).to(torch.bfloat16)
+    v = (torch.randn(T, H, D, generator=gen, device=device) * scale).to(torch.bfloat16)
+    k_inv, v_inv, k_aq, v_aq = int8_calc_scales(k, v)
+    pages = [(L + blk - 1) // blk for L in lens]
+    nb = sum(pages)
+    bt = torch.zeros(len(lens), max(pages), dtype=torch.int32)
+    perm = torch.randperm(nb, generator=cpu_gen).to(torch.int32)
+    cur, slots = 0, []
+    for b, L in enumerate(lens):
+        bt[b, :pages[b]] = perm[cur:cur + pages[b]]
+        cur += pages[b]
+        slots += [int(bt[b, p // blk]) * blk + p % blk for p in range(L)]
+    kc = torch.zeros(nb, blk, H, D, dtype=torch.int8, device=device)
+    vc = torch.zeros_like(kc)
+    int8_quant_store(k, v, torch.tensor(slots, device=device), k_inv, v_inv, kc, vc)
+    q = torch.randn(len(lens), Hq, D, generator=gen, device=device).to(torch.bfloat16)
+    o = torch.empty_like(q)
+    bt_d, sl = bt.to(device), torch.tensor(lens, dtype=torch.int32, device=device)
+    ms = time_loop_flushed(lambda: int8_paged_decode(q, kc, vc, k_aq, v_aq, bt_d, sl, D ** -0.5, o, max(lens)),
+                   args.steps, args.warmup, device)
+    by = sum(L * H * D * 2 for L in lens) + 2 * H * D * 2 + 2 * len(lens) * Hq * D * 2 + 4 * sum(pages)
+    out["config1"] = {"workload": "BASELINE config 1: INT8, 4 requests at 512/1024/1536/2048, Hq 32 / KVH 8",
+                      "ms_per_step": ms, "tokens_per_s_per_layer": len(lens) / (ms * 1e-3), "bytes_per_launch": by,
+                      "hbm_gbs": by / (ms * 1e-3) / 1e9, "frac_of_measured_hbm": by / (ms * 1e-3) / 1e9 / peak,
+                      "l2": "256 MB buffer written before every timed step"}
+    # ---- config 2
+    gen = torch.Generator(device=device).manual_seed(1002)
+    cpu_gen = torch.Generator().manual_seed(1002)
+    Hq, H, D, g, r = 40, 8, 128, 128, 128
+    lens = torch.randint(1024, 8193, (8,), generator=cpu_gen).tolist()
+    kv = build_kivi_requests(lens, H, D, g, r, blk, device, cpu_gen, gen)
+    q = torch.randn(len(lens), Hq, D, generator=gen, device=device).to(torch.bfloat16)
+    o = torch.empty_like(q)
+    bt_d, sl, st = kv.bt.to(device), torch.tensor(lens, dtype=torch.int32, device=device), kv.state.to(device)
+    ms = time_loop_flushed(lambda: kivi_paged_decode(q, kv.views, kv.rk, kv.rv, bt_d, sl, st, g, D ** -0.5, o, max(lens)),
+                   args.steps, args.warmup, device)
+    by = sum(request_decode_bytes(L, H, Hq, D, g, r, blk) for L in lens)
+    out["config2"] = {"workload": "BASELINE config 2: KIVI INT4 decode, 8 requests at U{1024..8192}, Hq 40 / KVH 8",
+                      "lens": lens, "ms_per_step": ms, "tokens_per_s_per_layer": len(lens) / (ms * 1e-3),
+                      "bytes_per_launch": by, "hbm_gbs": by / (ms * 1e-3) / 1e9,
+                      "frac_of_measured_hbm": by / (ms * 1e-3) / 1e9 / peak,
+                      "l2": "256 MB buffer written before every timed step"}
+    return out
+
+
 def build_int8_workload(cfg, rank, world, device, seed=4321):
     """Config 3 on this rank's KV heads: 64 requests x 8192 tokens in int8
     pages (block tables a permutation of the physical blocks), K/V ~ N(0,1)
@@ -466,6 +554,36 @@ def time_loop(fn, steps, warmup, device):
     torch.cuda.synchronize(device)
     del graph
     return s.elapsed_time(e) / steps
+
+
+def time_loop_flushed(fn, steps, warmup, device):
+    """ms per call of ``fn`` for workloads that fit in L2: before every timed
+    replay a 256 MB buffer (twice the 126 MB L2) is written, and only the
+    replay itself sits between that step's CUDA events."""
+    import torch
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for _ in range(max(warmup, 3)):
+            fn()
+    torch.cuda.current_stream(device).wait_stream(side)
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    graph.replay()
+    torch.cuda.synchronize(device)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for s, e in ev:
+        flush.zero_()
+        s.record()
+        graph.replay()
+        e.record()
+    torch.cuda.synchronize(device)
+    del graph
+    return sum(s.elapsed_time(e) for s, e in ev) / steps
 
 
 def algorithmic_bytes(w) -> int:
@@ -769,6 +887,9 @@ def main():
     if args.only == "config4":
         print(json.dumps({"only": "config4", **run_config4_leg(device, args)}), flush=True)
         return
+    if args.only == "small":
+        print(json.dumps({"only": "small", **run_small_configs(device, args)}), flush=True)
+        return
     if args.only == "fp8":
         res = run_fp8_leg(cfg3, rank, world, device, args)
         if rank == 0:
@@ -860,6 +981,9 @@ def main():
     fp8 = None
     if not args.no_int8:
         fp8 = run_fp8_leg(cfg3, rank, world, device, args)
+    small = None
+    if world == 1 and not args.no_config4:
+        small = run_small_configs(device, args)
     config4 = None
     if world == 1 and not args.no_config4:
         config4 = run_config4_leg(device, args)
@@ -916,6 +1040,8 @@ def main():
             "int8_config3": int8,
             "config4": config4,
             "fp8_decode": fp8,
+            "config1": None if small is None else small["config1"],
+            "config2": None if small is None else small["config2"],
             "e2e": None if e2e_dt is None else {
                 "value": w.B / e2e_dt, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_dt * 1e3, "api": "AscendKiviInt4AttentionBackendMixin.forward (DecodeOnly)"},
