@@ -17,23 +17,27 @@
 // constant sum_d q k_mn) depend only on the page and group, so the CTA builds
 // them once per page into shared memory, already in B-fragment order.
 //
-// int4 -> fp16: PRMT gathers byte j of two 32-bit words into the low bytes of
-// a half pair; LOP3 ((x & 0x000F000F) | 0x64006400) yields 1024 + n and the
-// high-nibble mask 1024 + 16 n; one HSUB2 removes the 1024 exactly, so the MMA
-// accumulates the codes n (or 16 n, divided out in fp32). Scales fold into the
-// other operand:
+// int4 -> fp16: ldmatrix.trans reads the packed codes as 16-bit elements (4
+// nibbles each) and hands every lane the element of two adjacent rows in one
+// register, i.e. the (row, k) / (row, k + 1) pair of an A fragment; masking
+// nibble i of both halves (one AND) makes fp16 subnormals n * 2^-24 (16 n *
+// 2^-24 for nibble 1), which the MMA takes exactly. Nibbles 2 and 3 first
+// move down a byte (one PRMT per register). Scales fold into the other
+// operand:
 //     K: S = S' / f + sum_d q[h][d] k_mn[d][group]
 //     V: P'[t][h] = p[t][h] * v_scale[t][group],
 //        O = O' / f + sum_t p[t][h] v_mn[t][group]
 // so the dequantised values enter exactly (code * scale + min in real
 // arithmetic), without the bf16 rounding of a dense gather.
 //
-// Token placement inside a warp's 32 tokens (4 words x 4 bytes x 2 nibbles
-// per channel): score m-tile j, row g holds the low-nibble token of byte
-// B(g, j) = ((g >> 1) + 2j) & 3 of word W(g) = 2 (g >> 2) + (g & 1), row
-// g + 8 the high-nibble token. Each K word a thread loads feeds both m-tiles,
-// the K fragment loads are free of bank conflicts, and the V rows one PV
-// load touches spread over two bank groups.
+// Token placement inside a warp's 32 tokens: a 16-bit element of a key row
+// holds the 4 tokens 4e .. 4e + 3 of one channel, so score m-tile j, row g is
+// token 4g + 2j and row g + 8 token 4g + 2j + 1. The PV k-step j then takes
+// tokens {4r + 2j} (k 0..7) and {4r + 2j + 1} (k 8..15). The value tile's TMA
+// copy therefore views the page's tokens as [token % 4][token / 4] (a 4-D map
+// with the token-in-quad dimension outermost), so each such set is 8
+// consecutive 32-byte rows, and the 32-byte swizzle spreads them over all 8
+// bank groups.
 #include <math_constants.h>
 
 #include <atomic>
@@ -66,9 +70,9 @@ __device__ __forceinline__ uint32_t nib_hi_sub(uint32_t x) { return x & 0x00F000
 constexpr float kLazy = 4.0f;  // log2 headroom of the running max
 
 template <int NG>
-struct __align__(128) PageStage {
+struct __align__(1024) PageStage {
   uint32_t k[kWarps][kD][4];  // [token quarter][channel][word]
-  uint32_t v[2][kBlk][8];     // [dim half][token][word]
+  uint32_t v[2][kBlk][8];     // [dim half][token % 4][token / 4][word], 32-byte swizzle
   float ks[kD * NG];          // [channel][group]
   float km[kD * NG];
   float vs[kBlk * NG];        // [token][group]
@@ -76,13 +80,32 @@ struct __align__(128) PageStage {
 };
 
 template <int NG>
-struct __align__(128) PageShared {
+struct __align__(1024) PageShared {
   PageStage<NG> st[kStages];
   uint4 qf[2][NG][kWarps][32];     // Q' B fragments: [buffer][group][k-step pair][lane]
   float cmn[2][NG][kWarps][kHeads];  // partial sum_d q k_mn: [buffer][group][k-step pair][head]
   unsigned long long full[kStages];
   int pid[kMaxPages];
 };
+
+// the value tile of every stage starts on a 1024-byte boundary (a multiple of
+// the 256-byte period of the 32-byte swizzle)
+static_assert(sizeof(PageStage<1>) % 1024 == 0 && sizeof(PageStage<2>) % 1024 == 0, "stage size");
+static_assert(offsetof(PageStage<1>, v) % 1024 == 0 && offsetof(PageStage<2>, v) % 1024 == 0,
+              "value tile alignment");
+// dynamic shared memory of one CTA: the struct plus room to round its base up
+template <int NG>
+constexpr size_t kivi_smem_bytes() {
+  return sizeof(PageShared<NG>) + 1024;
+}
+
+// Byte offset of 16-byte chunk c (0 or 1) of page token `tok` in a value
+// tile: row 32 (tok % 4) + tok / 4 of 32 bytes, chunk c XOR bit 2 of the row
+// (the 32-byte swizzle: address bit 4 ^= address bit 7).
+__device__ __forceinline__ uint32_t vrow_off(int tok, int c) {
+  const int row = 32 * (tok & 3) + (tok >> 2);
+  return static_cast<uint32_t>(32 * row + 16 * (c ^ ((row >> 2) & 1)));
+}
 
 template <int NG>
 constexpr uint32_t stage_tx_bytes() {
@@ -303,11 +326,15 @@ static_assert(sizeof(float) * (kTailBlock * (kTailLd + kD + kHeads) + 3 * kHeads
 
 // ------------------------------------------------------------ the kernel
 
+// 5 CTAs per SM for group 128; group 64 fits 4 (shared memory), which leaves
+// its larger register state room
 template <int NG>
-__global__ void __launch_bounds__(kThreads, 5)
+__global__ void __launch_bounds__(kThreads, NG == 1 ? 5 : 4)
 kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tmap_k,
                        const __grid_constant__ CUtensorMap tmap_v) {
-  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  extern __shared__ unsigned char smem_dyn[];
+  const uint32_t raw = smem_u32(smem_dyn);
+  unsigned char* smem_raw = smem_dyn + (((raw + 1023u) & ~1023u) - raw);
   PageShared<NG>& sh = *reinterpret_cast<PageShared<NG>*>(smem_raw);
   const int n_tail = p.splits_total - p.num_hist_splits;  // window CTAs come first
   const int h = blockIdx.y, b = blockIdx.z;
@@ -339,7 +366,9 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
   }
 
   // q of the Q' entries this thread builds: head g, channels
-  // 16 (2 warp + e) + 4 r + t (k-steps 2 warp and 2 warp + 1)
+  // 16 (2 warp + e) + qch(r), qch = 2t, 2t + 1, 2t + 8, 2t + 9 (the B
+  // fragment of k-steps 2 warp and 2 warp + 1)
+  const auto qch = [t](int r) { return 2 * t + (r & 1) + 8 * (r >> 1); };
   float qv[8];
   {
     const __nv_bfloat16* qrow =
@@ -349,7 +378,7 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
 #pragma unroll
       for (int r = 0; r < 4; ++r)
         qv[4 * e + r] =
-            g < G ? __bfloat162float(qrow[16 * (2 * warp + e) + 4 * r + t]) * p.scale_log2 : 0.0f;
+            g < G ? __bfloat162float(qrow[16 * (2 * warp + e) + qch(r)]) * p.scale_log2 : 0.0f;
   }
   __syncthreads();
 
@@ -366,7 +395,7 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
         for (int w = 0; w < kWarps; ++w) tma_load_2d(&st.k[w][0][0], &tmap_k, 4 * w, krow, &sh.full[s]);
 #pragma unroll
         for (int hp = 0; hp < 2; ++hp)
-          tma_load_3d(&st.v[hp][0][0], &tmap_v, 8 * hp, h, pg * kBlk, &sh.full[s]);
+          tma_load_4d(&st.v[hp][0][0], &tmap_v, 8 * hp, h, pg * (kBlk / 4), 0, &sh.full[s]);
         const int64_t soff = (static_cast<int64_t>(pg) * kvh + h) * kD * NG;
         bulk_load(st.ks, p.ks + soff, sizeof(float) * kD * NG, &sh.full[s]);
         bulk_load(st.km, p.km + soff, sizeof(float) * kD * NG, &sh.full[s]);
@@ -398,19 +427,13 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
     for (int gg = 0; gg < NG; ++gg) mn_acc[e][gg] = 0.0f;
 
   // token placement (see the file comment)
-  const int W = 2 * (g >> 2) + (g & 1);
-  uint32_t ksel[2];
   int tok_j[2];  // local token of row g in m-tile j (row g + 8: + 1)
 #pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    const int B = ((g >> 1) + 2 * j) & 3;
-    ksel[j] = static_cast<uint32_t>(B | ((4 + B) << 8));
-    tok_j[j] = 8 * W + 2 * B;
-  }
-  // PV k-step j: rows 2t, 2t+1 of score m-tile j -> tokens va[j], va[j] + 8
-  int va[2];
-#pragma unroll
-  for (int j = 0; j < 2; ++j) va[j] = 16 * (t >> 1) + 2 * (t ^ (2 * j));
+  for (int j = 0; j < 2; ++j) tok_j[j] = 4 * g + 2 * j;
+  // ldmatrix row of this lane in the value tile: token 4 (lane & 7) + (lane >> 3)
+  // of the warp's 32 (matrix lane >> 3 = token set {4r + (lane >> 3)})
+  const int vtok = kTokW * warp + 4 * (lane & 7) + (lane >> 3);
+  const uint32_t voff0 = vrow_off(vtok, 0), voff1 = vrow_off(vtok, 1);
   const int grp = NG == 2 ? (warp >> 1) : 0;  // key group of this warp's tokens
 
   int consumed = 0;
@@ -433,7 +456,7 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
           float qq[4];
 #pragma unroll
           for (int r = 0; r < 4; ++r) {
-            const int ch = 16 * (2 * warp + e) + 4 * r + t;
+            const int ch = 16 * (2 * warp + e) + qch(r);
             qq[r] = qv[4 * e + r] * st.ks[ch * NG + gq];
             c = fmaf(qv[4 * e + r], st.km[ch * NG + gq], c);
           }
@@ -486,19 +509,18 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
     float sc[2][4];
 #pragma unroll
     for (int j = 0; j < 2; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
-    const uint32_t* kb = &st.k[warp][t][W];
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      const uint32_t w0 = kb[(16 * kk + 0) * 4];
-      const uint32_t w1 = kb[(16 * kk + 4) * 4];
-      const uint32_t w2 = kb[(16 * kk + 8) * 4];
-      const uint32_t w3 = kb[(16 * kk + 12) * 4];
+    for (int kp = 0; kp < 4; ++kp) {
+      // matrices m = 0..3: channels 32 kp + 8 m .. + 7 (rows), token quads (columns)
+      uint32_t kx[4];
+      ldsm_x4_t(kx, &st.k[warp][32 * kp + lane][0]);
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const uint32_t x01 = prmt(w0, w1, ksel[j]);
-        const uint32_t x23 = prmt(w2, w3, ksel[j]);
-        mma16816(sc[j], nib_lo_sub(x01), nib_hi_sub(x01), nib_lo_sub(x23), nib_hi_sub(x23), bq[kk][0],
-                 bq[kk][1]);
+      for (int e = 0; e < 2; ++e) {
+        const int kk = 2 * kp + e;
+        const uint32_t x0 = kx[2 * e], x1 = kx[2 * e + 1];
+        mma16816(sc[0], nib_lo_sub(x0), nib_hi_sub(x0), nib_lo_sub(x1), nib_hi_sub(x1), bq[kk][0], bq[kk][1]);
+        const uint32_t y0 = prmt(x0, x0, 0x0301u), y1 = prmt(x1, x1, 0x0301u);
+        mma16816(sc[1], nib_lo_sub(y0), nib_hi_sub(y0), nib_lo_sub(y1), nib_hi_sub(y1), bq[kk][0], bq[kk][1]);
       }
     }
     // scores in log2 units: [j][0..1] low-nibble token, heads 2t, 2t+1; [j][2..3] its +1
@@ -608,27 +630,22 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
       }
     }
 
-    // ---- O'^T += V^T . P'^T; k-step j: k (2t, 2t+1) = tokens (va, va + 8),
-    // k (2t+8, 2t+9) = their + 1; m-tile (jp, hp): byte jp of word 8 hp + g
+    // ---- O'^T += V^T . P'^T over 32-dim blocks db (dim half db >> 1, chunk
+    // db & 1): matrix d = tokens {4r + d} x 32 dims; k-step j takes matrices
+    // 2j (k 0..7) and 2j + 1 (k 8..15). m-tile 2 db + s: rows g / g + 8 =
+    // dims 32 db + 4g + 2s and + 1.
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const uint32_t* vb = &st.v[0][kTokW * warp + va[j]][g];
-      uint32_t wa0[2], wb0[2], wa1[2], wb1[2];
+    for (int db = 0; db < 4; ++db) {
+      uint32_t vx[4];
+      ldsm_x4_t(vx, reinterpret_cast<const unsigned char*>(&st.v[db >> 1][0][0]) + ((db & 1) ? voff1 : voff0));
+      const int gg = NG == 2 ? (db >> 1) : 0;
 #pragma unroll
-      for (int hp = 0; hp < 2; ++hp) {
-        wa0[hp] = vb[hp * kBlk * 8 + 0];
-        wb0[hp] = vb[hp * kBlk * 8 + 8 * 8];
-        wa1[hp] = vb[hp * kBlk * 8 + 1 * 8];
-        wb1[hp] = vb[hp * kBlk * 8 + 9 * 8];
-      }
-#pragma unroll
-      for (int mt = 0; mt < 8; ++mt) {
-        const int jp = mt & 3, hp = mt >> 2;
-        const uint32_t sel = static_cast<uint32_t>(jp | ((4 + jp) << 8));
-        const uint32_t x0 = prmt(wa0[hp], wb0[hp], sel);
-        const uint32_t x1 = prmt(wa1[hp], wb1[hp], sel);
-        const int gg = NG == 2 ? hp : 0;
-        mma16816(o[mt], nib_lo_sub(x0), nib_hi_sub(x0), nib_lo_sub(x1), nib_hi_sub(x1), pb[j][gg][0],
+      for (int j = 0; j < 2; ++j) {
+        const uint32_t x0 = vx[2 * j], x1 = vx[2 * j + 1];
+        mma16816(o[2 * db], nib_lo_sub(x0), nib_hi_sub(x0), nib_lo_sub(x1), nib_hi_sub(x1), pb[j][gg][0],
+                 pb[j][gg][1]);
+        const uint32_t y0 = prmt(x0, x0, 0x0301u), y1 = prmt(x1, x1, 0x0301u);
+        mma16816(o[2 * db + 1], nib_lo_sub(y0), nib_hi_sub(y0), nib_lo_sub(y1), nib_hi_sub(y1), pb[j][gg][0],
                  pb[j][gg][1]);
       }
     }
@@ -657,9 +674,8 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
   float* ml = mm + kWarps * kHeads;
 #pragma unroll
   for (int mt = 0; mt < 8; ++mt) {
-    const int jp = mt & 3, hp = mt >> 2;
-    const int d_lo = 8 * (8 * hp + g) + 2 * jp;
-    const int gg = NG == 2 ? hp : 0;
+    const int d_lo = 32 * (mt >> 1) + 4 * g + 2 * (mt & 1);
+    const int gg = NG == 2 ? (mt >> 2) : 0;
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int head = 2 * t + e;
@@ -718,15 +734,18 @@ int encode_maps(const DecodeParams& p, CUtensorMap* tk, CUtensorMap* tv) {
       return set_error(QKV_ERR_CUDA, "cuTensorMapEncodeTiled(k_quant) failed: " + std::to_string(r));
   }
   {
-    // v_quant as [NB * B tokens][KVH][D/8 words]
-    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD / 8), static_cast<cuuint64_t>(p.kvh),
-                                static_cast<cuuint64_t>(p.num_blocks) * kBlk};
-    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kD / 8) * 4,
-                                   static_cast<cuuint64_t>(kD / 8) * 4 * p.kvh};
-    const cuuint32_t box[3] = {8, 1, kBlk};
-    const cuuint32_t es[3] = {1, 1, 1};
-    const CUresult r = enc(tv, CU_TENSOR_MAP_DATA_TYPE_INT32, 3, const_cast<int32_t*>(p.vq), dims,
-                           strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+    // v_quant [NB * B tokens][KVH][D/8 words] viewed as
+    // [token % 4][token / 4][KVH][D/8 words]: the box {8 words, 1 head, B/4
+    // quads, 4} lands as [token % 4][token / 4][8 words], 32-byte rows with
+    // the 32-byte swizzle (see vrow_off)
+    const cuuint64_t row = static_cast<cuuint64_t>(kD / 8) * 4 * p.kvh;  // bytes per token
+    const cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD / 8), static_cast<cuuint64_t>(p.kvh),
+                                static_cast<cuuint64_t>(p.num_blocks) * (kBlk / 4), 4};
+    const cuuint64_t strides[3] = {static_cast<cuuint64_t>(kD / 8) * 4, 4 * row, row};
+    const cuuint32_t box[4] = {8, 1, kBlk / 4, 4};
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    const CUresult r = enc(tv, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, const_cast<int32_t*>(p.vq), dims,
+                           strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
       return set_error(QKV_ERR_CUDA, "cuTensorMapEncodeTiled(v_quant) failed: " + std::to_string(r));
@@ -743,7 +762,7 @@ int set_smem_attr() {
   if ((done.load() & bit) == 0) {
     const cudaError_t e = cudaFuncSetAttribute(kivi_decode_tma_kernel<NG>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(sizeof(PageShared<NG>)));
+                                               static_cast<int>(kivi_smem_bytes<NG>()));
     if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(kivi_decode_tma_kernel)");
     done.fetch_or(bit);
   }
@@ -764,14 +783,14 @@ bool kivi_tma_supported(const DecodeParams& p) {
          al(p.km, 16) && al(p.vs, 8) && al(p.vm, 8);
 }
 
-// CTAs of the page-pipelined kernel resident per SM: registers allow 5 (the
-// launch bound), shared memory 5 for group 128 and 4 for group 64.
+// CTAs of the page-pipelined kernel resident per SM: the launch bounds (5 for
+// group 128, 4 for group 64) or shared memory, whichever is lower.
 int kivi_tma_ctas_per_sm(int group) {
   constexpr int kSmemPerSm = 228 * 1024, kReservedPerCta = 1024;
-  const int per = static_cast<int>(group == 128 ? sizeof(PageShared<1>) : sizeof(PageShared<2>)) +
+  const int per = static_cast<int>(group == 128 ? kivi_smem_bytes<1>() : kivi_smem_bytes<2>()) +
                   kReservedPerCta;
-  const int by_smem = kSmemPerSm / per;
-  return by_smem < 5 ? by_smem : 5;
+  const int by_smem = kSmemPerSm / per, by_regs = group == 128 ? 5 : 4;
+  return by_smem < by_regs ? by_smem : by_regs;
 }
 
 // Splits chosen for whole waves: among split counts that keep each split
@@ -817,10 +836,10 @@ int launch_kivi_tma(const DecodeParams& p0, cudaStream_t stream) {
   dim3 grid(p.splits_total, p.kvh, p.batch);
   if (p.group == 128) {
     if ((rc = set_smem_attr<1>()) != QKV_OK) return rc;
-    kivi_decode_tma_kernel<1><<<grid, kThreads, sizeof(PageShared<1>), stream>>>(p, tk, tv);
+    kivi_decode_tma_kernel<1><<<grid, kThreads, kivi_smem_bytes<1>(), stream>>>(p, tk, tv);
   } else {
     if ((rc = set_smem_attr<2>()) != QKV_OK) return rc;
-    kivi_decode_tma_kernel<2><<<grid, kThreads, sizeof(PageShared<2>), stream>>>(p, tk, tv);
+    kivi_decode_tma_kernel<2><<<grid, kThreads, kivi_smem_bytes<2>(), stream>>>(p, tk, tv);
   }
   QKV_CHECK_LAUNCH("kivi_decode_tma_kernel");
   if (p.splits_total > 1) {
