@@ -2,13 +2,14 @@
 // 128, page size 128, group 64/128, up to 8 query heads per KV head).
 //
 // One CTA of 4 warps owns (request, kv head, history split) and streams the
-// split's pages through an S-stage ring in shared memory. One thread issues
-// each page's copies with the Tensor Memory Accelerator:
-//     k_quant  4 boxes {4 words, 128 channels}   (one token quarter each)
-//     v_quant  2 boxes {8 words, 1 head, 128 tokens} (one dim half each)
+// split's pages through an S-stage ring in shared memory. Per page, one lane
+// issues the copies with the Tensor Memory Accelerator:
+//     k_quant  one box {16 words, 128 channels} (8 KB, 64-byte rows)
+//     v_quant  one box {16 words, 1 head, 32 quads, 4} (8 KB, 64-byte rows)
 //     k_scale, k_mn  one bulk copy each (contiguous per page and head)
-// and every thread copies the v_scale / v_mn of one token with cp.async; all
-// of it completes on the stage's mbarrier. Warp w computes tokens
+// and the lanes of the same warp (warp = page % 4) copy the v_scale / v_mn of
+// 4 tokens each with cp.async; all of it completes on the stage's mbarrier.
+// Both code tiles use the 64-byte swizzle. Warp w computes tokens
 // [32w, 32w + 32) of every page:
 //     S^T[token][head] = K[token][channel] . Q'^T[channel][head]
 //     O^T[dim][head]  += V^T[dim][token]   . P'^T[token][head]
@@ -36,8 +37,8 @@
 // tokens {4r + 2j} (k 0..7) and {4r + 2j + 1} (k 8..15). The value tile's TMA
 // copy therefore views the page's tokens as [token % 4][token / 4] (a 4-D map
 // with the token-in-quad dimension outermost), so each such set is 8
-// consecutive 32-byte rows, and the 32-byte swizzle spreads them over all 8
-// bank groups.
+// consecutive 64-byte rows, and the 64-byte swizzle spreads them over all 8
+// bank groups (likewise 8 consecutive key channels).
 #include <math_constants.h>
 
 #include <atomic>
@@ -71,8 +72,8 @@ constexpr float kLazy = 4.0f;  // log2 headroom of the running max
 
 template <int NG>
 struct __align__(1024) PageStage {
-  uint32_t k[kWarps][kD][4];  // [token quarter][channel][word]
-  uint32_t v[2][kBlk][8];     // [dim half][token % 4][token / 4][word], 32-byte swizzle
+  uint32_t k[kD][16];         // [channel][word], 64-byte swizzle (see koff)
+  uint32_t v[kBlk][16];       // [token % 4][token / 4][word], 64-byte swizzle (see voff)
   float ks[kD * NG];          // [channel][group]
   float km[kD * NG];
   float vs[kBlk * NG];        // [token][group]
@@ -88,28 +89,33 @@ struct __align__(1024) PageShared {
   int pid[kMaxPages];
 };
 
-// the value tile of every stage starts on a 1024-byte boundary (a multiple of
-// the 256-byte period of the 32-byte swizzle)
+// the code tiles of every stage start on 1024-byte boundaries (a multiple of
+// the 512-byte period of the 64-byte swizzle)
 static_assert(sizeof(PageStage<1>) % 1024 == 0 && sizeof(PageStage<2>) % 1024 == 0, "stage size");
-static_assert(offsetof(PageStage<1>, v) % 1024 == 0 && offsetof(PageStage<2>, v) % 1024 == 0,
-              "value tile alignment");
+static_assert(offsetof(PageStage<1>, v) % 1024 == 0 && offsetof(PageStage<2>, v) % 1024 == 0 &&
+                  offsetof(PageStage<1>, k) == 0 && offsetof(PageStage<2>, k) == 0,
+              "code tile alignment");
 // dynamic shared memory of one CTA: the struct plus room to round its base up
 template <int NG>
 constexpr size_t kivi_smem_bytes() {
   return sizeof(PageShared<NG>) + 1024;
 }
 
-// Byte offset of 16-byte chunk c (0 or 1) of page token `tok` in a value
-// tile: row 32 (tok % 4) + tok / 4 of 32 bytes, chunk c XOR bit 2 of the row
-// (the 32-byte swizzle: address bit 4 ^= address bit 7).
-__device__ __forceinline__ uint32_t vrow_off(int tok, int c) {
+// The 64-byte swizzle (address bits [4,6) ^= bits [7,9)) on 64-byte rows:
+// 16-byte chunk c of row r sits at 64 r + 16 (c ^ ((r >> 1) & 3)).
+// Key tile: row = channel, chunk = token quarter (8 tokens per word).
+__device__ __forceinline__ uint32_t koff(int ch, int c) {
+  return static_cast<uint32_t>(64 * ch + 16 * (c ^ ((ch >> 1) & 3)));
+}
+// Value tile: row 32 (tok % 4) + tok / 4 for page token tok, chunk = 32 dims.
+__device__ __forceinline__ uint32_t voff(int tok, int c) {
   const int row = 32 * (tok & 3) + (tok >> 2);
-  return static_cast<uint32_t>(32 * row + 16 * (c ^ ((row >> 2) & 1)));
+  return static_cast<uint32_t>(64 * row + 16 * (c ^ ((row >> 1) & 3)));
 }
 
 template <int NG>
 constexpr uint32_t stage_tx_bytes() {
-  return static_cast<uint32_t>(sizeof(uint32_t) * (kWarps * kD * 4 + 2 * kBlk * 8) +
+  return static_cast<uint32_t>(sizeof(uint32_t) * (kD * (kBlk / 8) + kBlk * (kD / 8)) +
                                2 * sizeof(float) * kD * NG);
 }
 
@@ -360,7 +366,7 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
     sh.pid[i] = static_cast<int>(page_of(p, b, t0 + i * kBlk));
   if (tid == 0) {
 #pragma unroll
-    for (int s = 0; s < kStages; ++s) mbar_init(&sh.full[s], kThreads + 1);
+    for (int s = 0; s < kStages; ++s) mbar_init(&sh.full[s], 32 + 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
   }
@@ -382,30 +388,32 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
   }
   __syncthreads();
 
-  // Issues the copies of page ii into stage ii % kStages (all threads).
+  // Issues the copies of page ii into stage ii % kStages: warp ii % 4 only
+  // (the stage's barrier counts its 32 lanes plus the expect-tx arrival).
   auto issue = [&](int ii) {
+    if (warp != (ii & (kWarps - 1))) return;
     const int s = ii % kStages;
     PageStage<NG>& st = sh.st[s];
     const int pg = sh.pid[ii];
     if (pg >= 0) {
-      if (tid == 0) {
+      if (lane == 0) {
         mbar_expect_tx(&sh.full[s], stage_tx_bytes<NG>());
-        const int krow = (pg * kvh + h) * kD;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) tma_load_2d(&st.k[w][0][0], &tmap_k, 4 * w, krow, &sh.full[s]);
-#pragma unroll
-        for (int hp = 0; hp < 2; ++hp)
-          tma_load_4d(&st.v[hp][0][0], &tmap_v, 8 * hp, h, pg * (kBlk / 4), 0, &sh.full[s]);
+        tma_load_2d(&st.k[0][0], &tmap_k, 0, (pg * kvh + h) * kD, &sh.full[s]);
+        tma_load_4d(&st.v[0][0], &tmap_v, 0, h, pg * (kBlk / 4), 0, &sh.full[s]);
         const int64_t soff = (static_cast<int64_t>(pg) * kvh + h) * kD * NG;
         bulk_load(st.ks, p.ks + soff, sizeof(float) * kD * NG, &sh.full[s]);
         bulk_load(st.km, p.km + soff, sizeof(float) * kD * NG, &sh.full[s]);
       }
-      const int64_t voff = ((static_cast<int64_t>(pg) * kBlk + tid) * kvh + h) * NG;
-      cp_async_small<4 * NG>(&st.vs[tid * NG], p.vs + voff);
-      cp_async_small<4 * NG>(&st.vm[tid * NG], p.vm + voff);
+#pragma unroll
+      for (int k = 0; k < kBlk / 32; ++k) {
+        const int tk = lane + 32 * k;
+        const int64_t so = ((static_cast<int64_t>(pg) * kBlk + tk) * kvh + h) * NG;
+        cp_async_small<4 * NG>(&st.vs[tk * NG], p.vs + so);
+        cp_async_small<4 * NG>(&st.vm[tk * NG], p.vm + so);
+      }
       cp_async_arrive_noinc(&sh.full[s]);
     } else {
-      if (tid == 0) mbar_arrive(&sh.full[s]);
+      if (lane == 0) mbar_arrive(&sh.full[s]);
       mbar_arrive(&sh.full[s]);
     }
   };
@@ -430,10 +438,15 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
   int tok_j[2];  // local token of row g in m-tile j (row g + 8: + 1)
 #pragma unroll
   for (int j = 0; j < 2; ++j) tok_j[j] = 4 * g + 2 * j;
-  // ldmatrix row of this lane in the value tile: token 4 (lane & 7) + (lane >> 3)
-  // of the warp's 32 (matrix lane >> 3 = token set {4r + (lane >> 3)})
-  const int vtok = kTokW * warp + 4 * (lane & 7) + (lane >> 3);
-  const uint32_t voff0 = vrow_off(vtok, 0), voff1 = vrow_off(vtok, 1);
+  // ldmatrix rows of this lane: key channel 32 kp + lane (chunk = warp), value
+  // token 4 (lane & 7) + (lane >> 3) of the warp's 32 (matrix lane >> 3 = token
+  // set {4r + (lane >> 3)}), one offset per 32-dim block
+  uint32_t kro[4], vro[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    kro[i] = koff(32 * i + lane, warp);
+    vro[i] = voff(kTokW * warp + 4 * (lane & 7) + (lane >> 3), i);
+  }
   const int grp = NG == 2 ? (warp >> 1) : 0;  // key group of this warp's tokens
 
   int consumed = 0;
@@ -513,7 +526,7 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
     for (int kp = 0; kp < 4; ++kp) {
       // matrices m = 0..3: channels 32 kp + 8 m .. + 7 (rows), token quads (columns)
       uint32_t kx[4];
-      ldsm_x4_t(kx, &st.k[warp][32 * kp + lane][0]);
+      ldsm_x4_t(kx, reinterpret_cast<const unsigned char*>(&st.k[0][0]) + kro[kp]);
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int kk = 2 * kp + e;
@@ -637,7 +650,7 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
 #pragma unroll
     for (int db = 0; db < 4; ++db) {
       uint32_t vx[4];
-      ldsm_x4_t(vx, reinterpret_cast<const unsigned char*>(&st.v[db >> 1][0][0]) + ((db & 1) ? voff1 : voff0));
+      ldsm_x4_t(vx, reinterpret_cast<const unsigned char*>(&st.v[0][0]) + vro[db]);
       const int gg = NG == 2 ? (db >> 1) : 0;
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
@@ -721,31 +734,32 @@ int encode_maps(const DecodeParams& p, CUtensorMap* tk, CUtensorMap* tv) {
   auto enc = encode_fn();
   if (enc == nullptr) return set_error(QKV_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
   {
-    // k_quant as [NB * KVH * D rows][B/8 words]
+    // k_quant as [NB * KVH * D rows][B/8 words]; one (page, head) block is one
+    // box of 64-byte rows with the 64-byte swizzle (see koff)
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kBlk / 8),
                                 static_cast<cuuint64_t>(p.num_blocks) * p.kvh * kD};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kBlk / 8) * 4};
-    const cuuint32_t box[2] = {4, kD};
+    const cuuint32_t box[2] = {kBlk / 8, kD};
     const cuuint32_t es[2] = {1, 1};
     const CUresult r = enc(tk, CU_TENSOR_MAP_DATA_TYPE_INT32, 2, const_cast<int32_t*>(p.kq), dims,
-                           strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
       return set_error(QKV_ERR_CUDA, "cuTensorMapEncodeTiled(k_quant) failed: " + std::to_string(r));
   }
   {
     // v_quant [NB * B tokens][KVH][D/8 words] viewed as
-    // [token % 4][token / 4][KVH][D/8 words]: the box {8 words, 1 head, B/4
-    // quads, 4} lands as [token % 4][token / 4][8 words], 32-byte rows with
-    // the 32-byte swizzle (see vrow_off)
+    // [token % 4][token / 4][KVH][D/8 words]: the box {16 words, 1 head, B/4
+    // quads, 4} lands as [token % 4][token / 4][16 words], 64-byte rows with
+    // the 64-byte swizzle (see voff)
     const cuuint64_t row = static_cast<cuuint64_t>(kD / 8) * 4 * p.kvh;  // bytes per token
     const cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD / 8), static_cast<cuuint64_t>(p.kvh),
                                 static_cast<cuuint64_t>(p.num_blocks) * (kBlk / 4), 4};
     const cuuint64_t strides[3] = {static_cast<cuuint64_t>(kD / 8) * 4, 4 * row, row};
-    const cuuint32_t box[4] = {8, 1, kBlk / 4, 4};
+    const cuuint32_t box[4] = {kD / 8, 1, kBlk / 4, 4};
     const cuuint32_t es[4] = {1, 1, 1, 1};
     const CUresult r = enc(tv, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, const_cast<int32_t*>(p.vq), dims,
-                           strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+                           strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
       return set_error(QKV_ERR_CUDA, "cuTensorMapEncodeTiled(v_quant) failed: " + std::to_string(r));
