@@ -797,7 +797,10 @@ def run_e2e(w, device, steps, warmup, world=1, rank=0):
     per step, pinned q/k/v of this rank's heads go in, the mixin's forward
     runs (window planning, packs, decode), N > 1 gathers every rank's heads
     with ``qkv_b200.distributed.gather_heads``, and the full output comes back
-    to the host."""
+    to the host. As a serving engine does, the copies run on their own
+    streams into double-buffered device slots: step i + 1's inputs go up while
+    step i computes, and step i's output comes down while step i + 1 runs;
+    every step's copies are inside the timed region."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -808,7 +811,6 @@ def run_e2e(w, device, steps, warmup, world=1, rank=0):
     B, Hq, H, D = w.B, w.Hql, w.Hl, w.D
     shard = HeadShard(rank, world, num_kv_heads=H * world, num_heads=Hq * world)
     g_buf = torch.empty(world * B, Hq, D, dtype=torch.bfloat16, device=device) if world > 1 else None
-    full = torch.empty(B, Hq * world, D, dtype=torch.bfloat16, device=device)
     bt_host = w.bt.numpy()
     total = steps + warmup
     gen = torch.Generator().manual_seed(7)
@@ -825,23 +827,52 @@ def run_e2e(w, device, steps, warmup, world=1, rank=0):
     slots_h = torch.from_numpy(bt_host[np.arange(B)[None, :], pos // w.blk].astype(np.int64) * w.blk
                                + pos % w.blk).pin_memory()
     q_lens = list(range(1, B + 1))
+    compute = torch.cuda.current_stream(device)
+    up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    q_d = torch.empty(2, B, Hq, D, dtype=torch.bfloat16, device=device)
+    k_d = torch.empty(2, B, H, D, dtype=torch.bfloat16, device=device)
+    v_d = torch.empty(2, B, H, D, dtype=torch.bfloat16, device=device)
+    out_d = torch.empty(2, B, Hq, D, dtype=torch.bfloat16, device=device)
+    res_d = torch.empty(2, B, Hq * world, D, dtype=torch.bfloat16, device=device) if world > 1 else None
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_used = [torch.cuda.Event() for _ in range(2)]  # slot's inputs consumed by the forward
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    ev_read = [torch.cuda.Event() for _ in range(2)]  # slot's output copied to the host
+    for e in ev_used + ev_read:
+        e.record(compute)
+
+    def upload(i):
+        s = i & 1
+        up.wait_event(ev_used[s])
+        with torch.cuda.stream(up):
+            q_d[s].copy_(q_h[i], non_blocking=True)
+            k_d[s].copy_(k_h[i], non_blocking=True)
+            v_d[s].copy_(v_h[i], non_blocking=True)
+        ev_in[s].record(up)
 
     def step(i):
+        s = i & 1
         for b in range(B):
             lens[b] += 1
-        q = q_h[i].to(device, non_blocking=True)
-        k = k_h[i].to(device, non_blocking=True)
-        v = v_h[i].to(device, non_blocking=True)
         md = SimpleNamespace(
             attn_state=SimpleNamespace(name="DecodeOnly"), actual_seq_lengths_q=q_lens,
             seq_lens_list=list(lens), slot_mapping=slots_h[i], block_tables=bt_pinned, req_ids=names,
             num_actual_tokens=B, causal=True, finished_req_ids=None,
         )
-        out = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=device)
-        impl.forward(None, q, k, v, (w.kbuf, w.vbuf), md, out)
-        res = gather_heads(out, shard, gathered=g_buf, out=full)
-        out_h.copy_(res, non_blocking=True)
+        compute.wait_event(ev_in[s])
+        compute.wait_event(ev_read[s])
+        impl.forward(None, q_d[s], k_d[s], v_d[s], (w.kbuf, w.vbuf), md, out_d[s])
+        ev_used[s].record(compute)
+        if i + 1 < total:
+            upload(i + 1)
+        res = gather_heads(out_d[s], shard, gathered=g_buf, out=None if res_d is None else res_d[s])
+        ev_out[s].record(compute)
+        down.wait_event(ev_out[s])
+        with torch.cuda.stream(down):
+            out_h.copy_(res, non_blocking=True)
+        ev_read[s].record(down)
 
+    upload(0)
     for i in range(warmup):
         step(i)
     torch.cuda.synchronize(device)

@@ -81,16 +81,40 @@ int ensure_device(StepRuntime& rt, size_t bytes, cudaStream_t stream) {
   return QKV_OK;
 }
 
+// True when ring[k] == base + k for k in [0, n): the slots of consecutive
+// positions inside one page.
+bool is_run(const int64_t* ring, int64_t n, int64_t base) {
+  int64_t bad = 0;
+  for (int64_t k = 0; k < n; ++k) bad |= ring[k] ^ (base + k);
+  return bad == 0;
+}
+
+// Whether both windows of `row` hold exactly the slots of positions
+// [L - n, L) in FIFO order. Walks page runs (one table lookup and one division
+// per page touched) and compares each contiguous piece of the ring against an
+// arithmetic progression.
 bool window_holds_last_positions(const win::Window& w, int64_t row, int64_t L, const int64_t* table, int cols,
                                  int blk) {
   for (const win::Side& sd : w.side) {
     const int64_t n = sd.length[row];
     if (n > L) return false;
-    for (int64_t j = 0; j < n; ++j) {
-      const int64_t pos = L - n + j;
-      const int64_t col = pos / blk;
+    if (n == 0) continue;
+    const int64_t* ring = sd.slots + row * w.cap;
+    int64_t lane = sd.start[row] % w.cap;
+    int64_t pos = L - n, col = pos / blk, off = pos % blk;
+    for (int64_t j = 0; j < n;) {
       if (col >= cols || table[col] < 0) return false;
-      if (table[col] * blk + pos % blk != sd.slots[row * w.cap + (sd.start[row] + j) % w.cap]) return false;
+      // positions of this page, cut where the ring wraps
+      const int64_t run = std::min(std::min(n - j, static_cast<int64_t>(blk) - off), w.cap - lane);
+      if (!is_run(ring + lane, run, table[col] * blk + off)) return false;
+      j += run;
+      off += run;
+      lane += run;
+      if (lane == w.cap) lane = 0;
+      if (off == blk) {
+        off = 0;
+        ++col;
+      }
     }
   }
   return true;
