@@ -434,7 +434,7 @@ QKV_API int qkv_kivi_window_scatter(void* ring_key, void* ring_value,
  *   window            a qkv_window_create handle (its state is updated)
  *   rows, slots       int64 [batch] host: residual row and new-token slot
  *   seq_lens          int32 [batch] host, including the new token
- *   block_table_host  int64 [batch, table_cols] host (liveness check)
+ *   block_table_host  int32 [batch, table_cols] host (liveness check)
  *   block_table       int32 device [batch, >= max blocks], row stride bt_stride
  *   query, out        bf16 [batch, num_heads, head_size], row strides in elements
  *   new_key/new_value bf16 [batch, num_kv_heads, head_size] device, contiguous
@@ -448,7 +448,7 @@ QKV_API void qkv_kivi_step_destroy(void* step);
 QKV_API int qkv_kivi_decode_step(
     void* step, void* window, int batch, const int64_t* rows,
     const int64_t* slots, const int32_t* seq_lens,
-    const int64_t* block_table_host, int table_cols,
+    const int32_t* block_table_host, int table_cols,
     const int32_t* block_table, int64_t bt_stride, const void* query,
     int64_t q_stride, const void* new_key, const void* new_value,
     int32_t* k_quant, float* k_scale, float* k_mn, int32_t* v_quant,

@@ -93,7 +93,7 @@ bool is_run(const int64_t* ring, int64_t n, int64_t base) {
 // [L - n, L) in FIFO order. Walks page runs (one table lookup and one division
 // per page touched) and compares each contiguous piece of the ring against an
 // arithmetic progression.
-bool window_holds_last_positions(const win::Window& w, int64_t row, int64_t L, const int64_t* table, int cols,
+bool window_holds_last_positions(const win::Window& w, int64_t row, int64_t L, const int32_t* table, int cols,
                                  int blk) {
   for (const win::Side& sd : w.side) {
     const int64_t n = sd.length[row];
@@ -106,7 +106,7 @@ bool window_holds_last_positions(const win::Window& w, int64_t row, int64_t L, c
       if (col >= cols || table[col] < 0) return false;
       // positions of this page, cut where the ring wraps
       const int64_t run = std::min(std::min(n - j, static_cast<int64_t>(blk) - off), w.cap - lane);
-      if (!is_run(ring + lane, run, table[col] * blk + off)) return false;
+      if (!is_run(ring + lane, run, static_cast<int64_t>(table[col]) * blk + off)) return false;
       j += run;
       off += run;
       lane += run;
@@ -150,7 +150,7 @@ QKV_API void qkv_kivi_step_destroy(void* h) {
 
 QKV_API int qkv_kivi_decode_step(
     void* step, void* window, int batch, const int64_t* rows, const int64_t* slots, const int32_t* seq_lens,
-    const int64_t* block_table_host, int table_cols, const int32_t* block_table, int64_t bt_stride,
+    const int32_t* block_table_host, int table_cols, const int32_t* block_table, int64_t bt_stride,
     const void* query, int64_t q_stride, const void* new_key, const void* new_value, int32_t* k_quant,
     float* k_scale, float* k_mn, int32_t* v_quant, float* v_scale, float* v_mn, void* res_key, void* res_value,
     int num_heads, int num_kv_heads, int head_size, int group_size, int block_size, int64_t num_blocks,
@@ -189,12 +189,13 @@ QKV_API int qkv_kivi_decode_step(
   for (int b = 0; b < batch; ++b) {
     const int64_t L = std::max<int32_t>(seq_lens[b], 0);
     max_len = std::max<int32_t>(max_len, static_cast<int32_t>(L));
-    const int64_t* trow = block_table_host + static_cast<int64_t>(b) * table_cols;
+    const int32_t* trow = block_table_host + static_cast<int64_t>(b) * table_cols;
     if (window_holds_last_positions(*w, rows[b], L, trow, table_cols, block_size)) continue;
     rt->live.clear();
     for (int64_t p = 0; p < L; ++p) {
       const int64_t col = p / block_size;
-      if (col < table_cols && trow[col] >= 0) rt->live.push_back(trow[col] * block_size + p % block_size);
+      if (col < table_cols && trow[col] >= 0)
+        rt->live.push_back(static_cast<int64_t>(trow[col]) * block_size + p % block_size);
     }
     for (int k = 1; k >= 0; --k)
       qkv_window_prune(w, static_cast<int>(rows[b]), static_cast<int>(rt->live.size()), rt->live.data(), k);

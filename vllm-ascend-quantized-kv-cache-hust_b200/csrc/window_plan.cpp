@@ -22,7 +22,6 @@
 // token -1 - s.
 #include <algorithm>
 #include <cstdint>
-#include <map>
 #include <new>
 #include <unordered_map>
 #include <unordered_set>
@@ -39,11 +38,6 @@ using qkv::win::SidePlan;
 using qkv::win::Window;
 
 inline int64_t new_src(int64_t t) { return -1 - t; }
-
-int64_t src_of(const SidePlan& p, int64_t flat) {
-  auto it = p.lane_src.find(flat);
-  return it == p.lane_src.end() ? flat : it->second;
-}
 
 // is_aligned_key_window (methods/kivi_int4/semantics.py:254-283): whole
 // groups, each contiguous, starting at a group-aligned block offset and
@@ -87,6 +81,7 @@ QKV_API void* qkv_window_create(int rows, int capacity, int group_size, int64_t*
   w->group = group_size;
   w->side[0] = Side{key_slots, key_start, key_length};
   w->side[1] = Side{value_slots, value_start, value_length};
+  for (SidePlan& p : w->plan) p.resize(static_cast<int64_t>(rows) * capacity);
   return w;
 }
 
@@ -109,44 +104,47 @@ QKV_API int qkv_window_store(void* h, int row, int n, const int64_t* slots, cons
   const int cap = w->cap;
   int64_t* rs = sd.slots + static_cast<int64_t>(row) * cap;
   const int64_t base = static_cast<int64_t>(row) * cap;
-  std::vector<int> lanes;
-  std::vector<int64_t> ev_slots;
+  std::vector<int64_t>& ev = w->scratch;
   for (int i = 0; i < n; ++i) {
     const int64_t slot = slots[i];
     const int64_t t = tokens[i];
+    // a slot the window holds is overwritten in place (first hit in FIFO
+    // order: lanes start .. cap - 1, then 0 .. the wrapped end)
     int hit = -1;
-    fifo_lanes(*w, sd, row, lanes);
-    for (int l : lanes)
-      if (rs[l] == slot) {
-        hit = l;
-        break;
-      }
+    {
+      const int64_t st = sd.start[row], len = sd.length[row];
+      const int64_t end1 = std::min<int64_t>(st + len, cap);
+      for (int64_t l = st; l < end1 && hit < 0; ++l)
+        if (rs[l] == slot) hit = static_cast<int>(l);
+      for (int64_t l = 0; l < st + len - cap && hit < 0; ++l)
+        if (rs[l] == slot) hit = static_cast<int>(l);
+    }
     if (hit >= 0) {
-      p.lane_src[base + hit] = new_src(t);
-      p.ring_writes[base + hit] = new_src(t);
+      p.set(base + hit, new_src(t));
       continue;
     }
     while (sd.length[row] >= cap) {
       const int count = is_key ? cap : 1;
-      fifo_lanes(*w, sd, row, lanes);
-      ev_slots.clear();
-      for (int j = 0; j < count; ++j) ev_slots.push_back(rs[lanes[j]]);
+      const int64_t st = sd.start[row];
+      ev.clear();
+      for (int j = 0; j < count; ++j) ev.push_back(rs[(st + j) % cap]);
       if (is_key && gate_block_size > 0 &&
-          !aligned_key_window(ev_slots.data(), static_cast<int64_t>(ev_slots.size()), w->group, gate_block_size))
+          !aligned_key_window(ev.data(), static_cast<int64_t>(ev.size()), w->group, gate_block_size))
         return QKV_ERR_INVALID;
       for (int j = 0; j < count; ++j) {
-        p.flush_src.push_back(src_of(p, base + lanes[j]));
-        p.flush_slots.push_back(ev_slots[j]);
-        rs[lanes[j]] = -1;
+        const int64_t lane = (st + j) % cap;
+        p.flush_src.push_back(p.src_of(base + lane));
+        p.flush_slots.push_back(ev[j]);
+        rs[lane] = -1;
       }
+      p.keep_valid = false;
       sd.length[row] -= count;
-      sd.start[row] = sd.length[row] == 0 ? 0 : (sd.start[row] + count) % cap;
+      sd.start[row] = sd.length[row] == 0 ? 0 : (st + count) % cap;
     }
     const int64_t tail = (sd.start[row] + sd.length[row]) % cap;
     rs[tail] = slot;
     sd.length[row] += 1;
-    p.lane_src[base + tail] = new_src(t);
-    p.ring_writes[base + tail] = new_src(t);
+    p.set(base + tail, new_src(t));
   }
   return QKV_OK;
 }
@@ -171,6 +169,7 @@ QKV_API int qkv_window_flush_direct(void* h, int n, const int64_t* slots, const 
     p.flush_src.push_back(new_src(tokens[i]));
     p.flush_slots.push_back(slots[i]);
   }
+  p.keep_valid = false;
   return QKV_OK;
 }
 
@@ -191,7 +190,7 @@ QKV_API int qkv_window_prune(void* h, int row, int n_live, const int64_t* live_s
   for (int l : lanes)
     if (live.count(rs[l])) {
       kept_slots.push_back(rs[l]);
-      srcs.push_back(src_of(p, base + l));
+      srcs.push_back(p.src_of(base + l));
     }
   if (kept_slots.size() == lanes.size()) return QKV_OK;
   std::fill(rs, rs + cap, int64_t{-1});
@@ -200,14 +199,9 @@ QKV_API int qkv_window_prune(void* h, int row, int n_live, const int64_t* live_s
   sd.length[row] = static_cast<int64_t>(kept_slots.size());
   // the compaction reads the kept lanes' sources (captured above) before
   // anything of this plan lands; it replaces every pending write of the row
-  for (int l = 0; l < cap; ++l) {
-    p.ring_writes.erase(base + l);
-    p.lane_src.erase(base + l);
-  }
-  for (size_t i = 0; i < srcs.size(); ++i) {
-    p.ring_writes[base + static_cast<int64_t>(i)] = srcs[i];
-    p.lane_src[base + static_cast<int64_t>(i)] = srcs[i];
-  }
+  for (int l = 0; l < cap; ++l) p.erase(base + l);
+  for (size_t i = 0; i < srcs.size(); ++i) p.set(base + static_cast<int64_t>(i), srcs[i]);
+  p.keep_valid = false;
   return QKV_OK;
 }
 
@@ -226,9 +220,11 @@ QKV_API int qkv_window_reset_row(void* h, int row) {
 // Deduplicated flush list sizes and the ring writes of the open plan. A
 // batched pack has no write order where the reference's sequential flushes
 // do, so only the last flush of a slot (keys: of a whole group, found by its
-// first slot) is kept.
-static void dedupe(const Window& w, int is_key, std::vector<int64_t>& keep) {
-  const SidePlan& p = w.plan[is_key ? 0 : 1];
+// first slot) is kept. Cached until the plan changes.
+static const std::vector<int64_t>& dedupe(Window& w, int is_key) {
+  SidePlan& p = w.plan[is_key ? 0 : 1];
+  if (p.keep_valid) return p.keep;
+  std::vector<int64_t>& keep = p.keep;
   keep.clear();
   const int64_t n = static_cast<int64_t>(p.flush_slots.size());
   if (is_key) {
@@ -241,20 +237,39 @@ static void dedupe(const Window& w, int is_key, std::vector<int64_t>& keep) {
     for (int64_t gi : groups)
       for (int j = 0; j < g; ++j) keep.push_back(gi * g + j);
   } else {
-    std::unordered_map<int64_t, int64_t> last;
-    for (int64_t i = 0; i < n; ++i) last[p.flush_slots[i]] = i;
-    for (auto& kv : last) keep.push_back(kv.second);
-    std::sort(keep.begin(), keep.end());
+    // the common case (every evicted slot distinct) keeps everything
+    std::vector<int64_t>& sorted = w.scratch;
+    sorted.assign(p.flush_slots.begin(), p.flush_slots.end());
+    std::sort(sorted.begin(), sorted.end());
+    if (std::adjacent_find(sorted.begin(), sorted.end()) == sorted.end()) {
+      for (int64_t i = 0; i < n; ++i) keep.push_back(i);
+    } else {
+      std::unordered_map<int64_t, int64_t> last;
+      for (int64_t i = 0; i < n; ++i) last[p.flush_slots[i]] = i;
+      for (auto& kv : last) keep.push_back(kv.second);
+      std::sort(keep.begin(), keep.end());
+    }
   }
+  p.keep_valid = true;
+  return keep;
+}
+
+// lanes with a pending write, ascending
+static void live_writes(SidePlan& p, std::vector<int64_t>& out) {
+  out.clear();
+  for (int64_t l : p.touched)
+    if (p.write_gen[l] == p.gen) out.push_back(l);
+  std::sort(out.begin(), out.end());
 }
 
 QKV_API int qkv_window_plan_counts(void* h, int is_key, int64_t* n_flush, int64_t* n_writes) {
   Window* w = static_cast<Window*>(h);
   if (w == nullptr || !n_flush || !n_writes) return QKV_ERR_INVALID;
-  std::vector<int64_t> keep;
-  dedupe(*w, is_key, keep);
-  *n_flush = static_cast<int64_t>(keep.size());
-  *n_writes = static_cast<int64_t>(w->plan[is_key ? 0 : 1].ring_writes.size());
+  *n_flush = static_cast<int64_t>(dedupe(*w, is_key).size());
+  SidePlan& p = w->plan[is_key ? 0 : 1];
+  int64_t nw = 0;
+  for (int64_t l : p.touched) nw += p.write_gen[l] == p.gen;
+  *n_writes = nw;
   return QKV_OK;
 }
 
@@ -262,20 +277,19 @@ QKV_API int qkv_window_plan_export(void* h, int is_key, int64_t* flush_src, int6
                                    int64_t* write_lanes, int64_t* write_src) {
   Window* w = static_cast<Window*>(h);
   if (w == nullptr) return QKV_ERR_INVALID;
-  const SidePlan& p = w->plan[is_key ? 0 : 1];
-  std::vector<int64_t> keep;
-  dedupe(*w, is_key, keep);
+  const std::vector<int64_t>& keep = dedupe(*w, is_key);
+  SidePlan& p = w->plan[is_key ? 0 : 1];
+  std::vector<int64_t> lanes;
+  live_writes(p, lanes);
   if (!keep.empty() && (!flush_src || !flush_slots)) return QKV_ERR_INVALID;
-  if (!p.ring_writes.empty() && (!write_lanes || !write_src)) return QKV_ERR_INVALID;
+  if (!lanes.empty() && (!write_lanes || !write_src)) return QKV_ERR_INVALID;
   for (size_t i = 0; i < keep.size(); ++i) {
     flush_src[i] = p.flush_src[keep[i]];
     flush_slots[i] = p.flush_slots[keep[i]];
   }
-  size_t i = 0;
-  for (const auto& kv : p.ring_writes) {
-    write_lanes[i] = kv.first;
-    write_src[i] = kv.second;
-    ++i;
+  for (size_t i = 0; i < lanes.size(); ++i) {
+    write_lanes[i] = lanes[i];
+    write_src[i] = p.write_val[lanes[i]];
   }
   return QKV_OK;
 }

@@ -233,6 +233,7 @@ class AscendKiviInt4AttentionBackendMixin:
         row = self.kivi_residual_req_to_row.pop(req_key, None)
         if row is None:
             return
+        self._kivi_rows_cache = None
         self.kivi_residual_row_to_req[row] = None
         self._kivi_planner.key.reset(row)
         self._kivi_planner.value.reset(row)
@@ -667,26 +668,38 @@ class AscendKiviInt4AttentionBackendMixin:
         if slots.size != B or slots.min() < 0:
             return False
         self._ensure_kivi_residual_buffers()
-        keys = self._get_kivi_req_keys(req_ids, B)
-        rows = np.fromiter((self._get_kivi_residual_row(k, create=True) for k in keys), dtype=np.int64, count=B)
+        rows = self._kivi_rows_of(self._get_kivi_req_keys(req_ids, B))
         bt = attn_metadata.block_tables
         if isinstance(bt, torch.Tensor):
             bt_host = (bt[:B].cpu() if bt.is_cuda else bt[:B]).numpy()
         else:
             bt_host = np.asarray(bt)[:B]
+        if bt_host.dtype != np.int32 or not bt_host.flags.c_contiguous:
+            bt_host = np.ascontiguousarray(bt_host, dtype=np.int32)
         dev = self.kivi_residual_key_cache.device
         k = key[:B] if key.dtype == torch.bfloat16 and key.device == dev else key[:B].to(dev, torch.bfloat16)
         v = value[:B] if value.dtype == torch.bfloat16 and value.device == dev else value[:B].to(dev, torch.bfloat16)
         step = getattr(self, "_kivi_step", None)
         if step is None:
             step = self._kivi_step = KiviDecodeStep()
-        step.run(
-            self._kivi_planner._handle, rows, slots, np.asarray(seq_lens, dtype=np.int32), bt_host,
-            self._kivi_table(bt, B), query[:B], k.contiguous(), v.contiguous(), self._kivi_views(),
-            self.kivi_residual_key_cache, self.kivi_residual_value_cache, self.kivi_group_size, self.scale,
-            output[:B],
-        )
+        if getattr(self, "_kivi_step_bound", None) is not self._kivi_bound:
+            step.bind(self._kivi_planner._handle, self._kivi_views(), self.kivi_residual_key_cache,
+                      self.kivi_residual_value_cache, self.kivi_group_size, self.scale)
+            self._kivi_step_bound = self._kivi_bound
+        step.run(rows, slots, np.asarray(seq_lens, dtype=np.int32), bt_host, self._kivi_table(bt, B), query[:B],
+                 k.contiguous(), v.contiguous(), output[:B])
         return True
+
+    def _kivi_rows_of(self, keys: list[str]) -> np.ndarray:
+        """Residual rows of the batch's requests (created on first sight),
+        reused while the batch's request list and the row map are unchanged."""
+        cached = getattr(self, "_kivi_rows_cache", None)
+        if cached is not None and cached[0] == keys:
+            return cached[1]
+        rows = np.fromiter((self._get_kivi_residual_row(k, create=True) for k in keys), dtype=np.int64,
+                           count=len(keys))
+        self._kivi_rows_cache = (keys, rows)
+        return rows
 
     def _kivi_res_state(self, req_keys: list[str], ends: list[int]) -> np.ndarray:
         st = np.zeros((len(req_keys), 6), dtype=np.int32)
@@ -709,12 +722,20 @@ class AscendKiviInt4AttentionBackendMixin:
         return t.to(self.k_quant_cache.device, non_blocking=True)
 
     def _kivi_table(self, block_table: Any, rows: int) -> torch.Tensor:
+        """The first ``rows`` block-table rows as int32 on the device. A host
+        table lands in a buffer this layer reuses: the result is valid until
+        the next call (kernels enqueued before it on the stream are safe)."""
         dev = self.k_quant_cache.device
         if isinstance(block_table, torch.Tensor):
             bt = block_table[:rows]
-            if bt.device != dev:
-                bt = bt.to(dev, non_blocking=True)
-            return bt.to(torch.int32).contiguous()
+            if bt.device == dev:
+                return bt.to(torch.int32).contiguous()
+            # a host table: one copy into a device buffer kept for the shape
+            buf = getattr(self, "_kivi_bt_dev", None)
+            if buf is None or buf.shape != bt.shape:
+                buf = self._kivi_bt_dev = torch.empty(bt.shape, dtype=torch.int32, device=dev)
+            buf.copy_(bt, non_blocking=True)
+            return buf
         return self._kivi_device_i32(np.asarray(block_table)[:rows])
 
     def _forward_kivi_paged_decode_attention(self, query, block_table, seq_lens, req_ids, output):
