@@ -65,7 +65,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--e2e-steps", type=int, default=30, help="0 skips the end-to-end leg")
+    ap.add_argument("--e2e-steps", type=int, default=200,
+                    help="timed steps of the end-to-end leg (10 untimed first; at most 246), 0 skips it")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-int8", action="store_true", help="skip the config-3 INT8 leg")
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 chunked-prefill leg")
@@ -799,8 +800,10 @@ def run_e2e(w, device, steps, warmup, world=1, rank=0):
     with ``qkv_b200.distributed.gather_heads``, and the full output comes back
     to the host. As a serving engine does, the copies run on their own
     streams into double-buffered device slots: step i + 1's inputs go up while
-    step i computes, and step i's output comes down while step i + 1 runs;
-    every step's copies are inside the timed region."""
+    step i computes, and step i's output comes down while step i + 1 runs
+    (issued after step i + 1 is enqueued, so it never holds up that step's
+    own host-to-device copy); every step's copies are inside the timed
+    region."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -838,6 +841,7 @@ def run_e2e(w, device, steps, warmup, world=1, rank=0):
     ev_used = [torch.cuda.Event() for _ in range(2)]  # slot's inputs consumed by the forward
     ev_out = [torch.cuda.Event() for _ in range(2)]
     ev_read = [torch.cuda.Event() for _ in range(2)]  # slot's output copied to the host
+    res = [None, None]
     for e in ev_used + ev_read:
         e.record(compute)
 
@@ -865,16 +869,24 @@ def run_e2e(w, device, steps, warmup, world=1, rank=0):
         ev_used[s].record(compute)
         if i + 1 < total:
             upload(i + 1)
-        res = gather_heads(out_d[s], shard, gathered=g_buf, out=None if res_d is None else res_d[s])
+        res[s] = gather_heads(out_d[s], shard, gathered=g_buf, out=None if res_d is None else res_d[s])
         ev_out[s].record(compute)
+        # the previous step's output goes down now: queued behind this step's
+        # host-to-device staging copy, not ahead of it
+        if i > 0:
+            download(i - 1)
+
+    def download(i):
+        s = i & 1
         down.wait_event(ev_out[s])
         with torch.cuda.stream(down):
-            out_h.copy_(res, non_blocking=True)
+            out_h.copy_(res[s], non_blocking=True)
         ev_read[s].record(down)
 
     upload(0)
     for i in range(warmup):
         step(i)
+    download(warmup - 1)
     torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
@@ -882,6 +894,7 @@ def run_e2e(w, device, steps, warmup, world=1, rank=0):
     t0 = time.perf_counter()
     for i in range(warmup, total):
         step(i)
+    download(total - 1)
     torch.cuda.synchronize(device)
     dt = (time.perf_counter() - t0) / max(steps, 1)
     h2d = B * (Hq + 2 * H) * D * 2 + B * 8 + B * 5 * 4 + B * 4 + w.bt.numel() * 4
@@ -1020,7 +1033,7 @@ def main():
         config4 = run_config4_leg(device, args)
     e2e_dt, h2d, d2h = (None, 0, 0)
     if args.e2e_steps > 0:
-        e2e_dt, h2d, d2h = run_e2e(w, device, args.e2e_steps, 3, world, rank)
+        e2e_dt, h2d, d2h = run_e2e(w, device, min(args.e2e_steps, 246), 10, world, rank)
         t = torch.tensor([e2e_dt], dtype=torch.float64, device=device)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)

@@ -435,7 +435,9 @@ QKV_API int qkv_kivi_window_scatter(void* ring_key, void* ring_value,
  *   rows, slots       int64 [batch] host: residual row and new-token slot
  *   seq_lens          int32 [batch] host, including the new token
  *   block_table_host  int32 [batch, table_cols] host (liveness check)
- *   block_table       int32 device [batch, >= max blocks], row stride bt_stride
+ *   block_table       int32 device [batch, >= max blocks], row stride bt_stride;
+ *                     NULL: the host table is staged with the indices (one
+ *                     copy for the whole step) and bt_stride is ignored
  *   query, out        bf16 [batch, num_heads, head_size], row strides in elements
  *   new_key/new_value bf16 [batch, num_kv_heads, head_size] device, contiguous
  *   k_quant..v_mn     the six KIVI views; res_key/res_value the bf16 rings

@@ -266,12 +266,15 @@ def test_int8_dequant_gather_bit_exact():
     assert np.array_equal(dv.float().cpu().numpy().view(np.uint32), wv.astype(np.float32).view(np.uint32))
 
 
-def test_native_decode_step_matches_general_path():
+@pytest.mark.parametrize("table_on", ["device", "host"])
+def test_native_decode_step_matches_general_path(table_on):
     """qkv_kivi_decode_step (planning, sync and launches in one native call)
     against the general Python-planned path on the same decode sequence:
     bulk prompt writes, 140 decode steps crossing key-window flushes, value
     evictions, a roll-back of 3 tokens and a finished request. Outputs, int4
-    pages and windows must be identical bit for bit."""
+    pages and windows must be identical bit for bit. The block table comes
+    on the device, or on the host (pinned; the step then stages it with its
+    indices)."""
     dev = torch.device("cuda", 0)
     head, kvh, group, block, residual, nb, num_heads = 128, 8, 64, 128, 128, 40, 32
     geo = {"geometry": np.array([head, kvh, group, block, residual, nb, num_heads])}
@@ -313,7 +316,8 @@ def test_native_decode_step_matches_general_path():
                 attn_state=SimpleNamespace(name="DecodeOnly"), actual_seq_lengths_q=list(range(1, B + 1)),
                 seq_lens_list=[lens[b] for b in live],
                 slot_mapping=torch.tensor([slot(b, lens[b] - 1) for b in live], device=dev),
-                block_tables=bt[live].to(dev), req_ids=[reqs[b] for b in live], num_actual_tokens=B, causal=True,
+                block_tables=bt[live].to(dev) if table_on == "device" else bt[live].pin_memory(),
+                req_ids=[reqs[b] for b in live], num_actual_tokens=B, causal=True,
                 finished_req_ids={"b"} if step == 100 else None,
             )
             out = torch.zeros(B, num_heads, head, dtype=torch.bfloat16, device=dev)

@@ -162,7 +162,7 @@ QKV_API int qkv_kivi_decode_step(
   QKV_CHECK_ARG(batch > 0 && batch <= w->rows && table_cols > 0 && block_size > 0 && num_kv_heads > 0 &&
                     head_size > 0 && head_size % 8 == 0,
                 "qkv_kivi_decode_step: bad sizes");
-  QKV_CHECK_ARG(rows && slots && seq_lens && block_table_host && block_table && query && new_key && new_value &&
+  QKV_CHECK_ARG(rows && slots && seq_lens && block_table_host && query && new_key && new_value &&
                     res_key && res_value && out,
                 "qkv_kivi_decode_step: null pointer");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -205,10 +205,13 @@ QKV_API int qkv_kivi_decode_step(
   int64_t nf[2], nw[2];
   for (int k = 0; k < 2; ++k) qkv_window_plan_counts(w, 1 - k, &nf[k], &nw[k]);
   // staging layout (int64): [k_src: nf0+nw0][v_src: nf1+nw1][k_fslots][v_fslots][k_lanes][v_lanes]
-  // then int32: res_state [B, 6], seq_lens [B]; then (device only) gathered rows
+  // then int32: res_state [B, 6], seq_lens [B], and (without a device block
+  // table) the host table [B, table_cols]; then (device only) gathered rows
   const int64_t n64 = nf[0] + nw[0] + nf[1] + nw[1] + nf[0] + nf[1] + nw[0] + nw[1];
   const size_t bytes64 = align16(static_cast<size_t>(n64) * 8);
-  const size_t bytes32 = align16(static_cast<size_t>(batch) * 7 * 4);
+  const bool stage_table = block_table == nullptr;
+  const size_t table_words = stage_table ? static_cast<size_t>(batch) * table_cols : 0;
+  const size_t bytes32 = align16((static_cast<size_t>(batch) * 7 + table_words) * 4);
   const size_t rows_k = static_cast<size_t>(nf[0] + nw[0]), rows_v = static_cast<size_t>(nf[1] + nw[1]);
   const size_t staged = bytes64 + bytes32;
   const size_t total = staged + (rows_k + rows_v) * static_cast<size_t>(row_bytes);
@@ -241,6 +244,7 @@ QKV_API int qkv_kivi_decode_step(
     s6[5] = seq_lens[b];
     h32[6 * batch + b] = seq_lens[b];
   }
+  if (stage_table) std::memcpy(h32 + 7 * batch, block_table_host, table_words * 4);
   cudaError_t e = cudaMemcpyAsync(rt->dev, pin.host, staged, cudaMemcpyHostToDevice, st);
   if (e != cudaSuccess) return cuda_error(e, "cudaMemcpyAsync(step staging)");
   e = cudaEventRecord(pin.done, st);
@@ -281,7 +285,8 @@ QKV_API int qkv_kivi_decode_step(
     if (rc != QKV_OK) return rc;
   }
   return qkv_kivi_paged_decode(query, q_stride, k_quant, k_scale, k_mn, v_quant, v_scale, v_mn, res_key, res_value,
-                               w->rows, cap, block_table, bt_stride, d32 + 6 * batch, d32, batch, num_heads,
+                               w->rows, cap, stage_table ? d32 + 7 * batch : block_table,
+                               stage_table ? table_cols : bt_stride, d32 + 6 * batch, d32, batch, num_heads,
                                num_kv_heads, head_size, group_size, block_size, num_blocks, std::max(max_len, 1),
                                scale, workspace, workspace_bytes, out, out_stride, stream);
 }

@@ -670,8 +670,13 @@ class AscendKiviInt4AttentionBackendMixin:
         self._ensure_kivi_residual_buffers()
         rows = self._kivi_rows_of(self._get_kivi_req_keys(req_ids, B))
         bt = attn_metadata.block_tables
+        bt_dev = None  # a host table is staged by the step with its indices
         if isinstance(bt, torch.Tensor):
-            bt_host = (bt[:B].cpu() if bt.is_cuda else bt[:B]).numpy()
+            if bt.is_cuda:
+                bt_dev = self._kivi_table(bt, B)
+                bt_host = bt[:B].cpu().numpy()
+            else:
+                bt_host = bt[:B].numpy()
         else:
             bt_host = np.asarray(bt)[:B]
         if bt_host.dtype != np.int32 or not bt_host.flags.c_contiguous:
@@ -686,8 +691,8 @@ class AscendKiviInt4AttentionBackendMixin:
             step.bind(self._kivi_planner._handle, self._kivi_views(), self.kivi_residual_key_cache,
                       self.kivi_residual_value_cache, self.kivi_group_size, self.scale)
             self._kivi_step_bound = self._kivi_bound
-        step.run(rows, slots, np.asarray(seq_lens, dtype=np.int32), bt_host, self._kivi_table(bt, B), query[:B],
-                 k.contiguous(), v.contiguous(), output[:B])
+        step.run(rows, slots, np.asarray(seq_lens, dtype=np.int32), bt_host, bt_dev, query[:B], k.contiguous(),
+                 v.contiguous(), output[:B])
         return True
 
     def _kivi_rows_of(self, keys: list[str]) -> np.ndarray:

@@ -53,7 +53,7 @@ class KiviDecodeStep:
         slots: np.ndarray,
         seq_lens: np.ndarray,
         block_table_host: np.ndarray,
-        block_table: torch.Tensor,
+        block_table: torch.Tensor | None,
         query: torch.Tensor,
         key: torch.Tensor,
         value: torch.Tensor,
@@ -61,13 +61,15 @@ class KiviDecodeStep:
     ) -> torch.Tensor:
         """``rows`` / ``slots`` int64 and ``seq_lens`` int32 host arrays of
         the batch; ``block_table_host`` int32 ``[B, cols]`` host,
-        ``block_table`` int32 on the device; ``query`` / ``out`` bf16
+        ``block_table`` the same table int32 on the device, or None to let
+        the step stage the host table with its indices (one copy for the
+        whole step); ``query`` / ``out`` bf16
         ``[B, Hq, D]``; ``key`` / ``value`` the new tokens, bf16
         ``[B, KVH, D]`` contiguous on the device."""
         if self._static is None:
             raise RuntimeError("kivi_decode_step: bind() the layer's caches first")
         H, D, blk, nb, group_size, scale = self._geom
-        require_cuda("kivi_decode_step", query, key, value, block_table, out)
+        require_cuda("kivi_decode_step", query, key, value, out)
         B, Hq = query.shape[0], query.shape[1]
         for name, t in (("query", query), ("out", out)):
             if t.dtype != torch.bfloat16 or t.stride(2) != 1 or t.stride(1) != D:
@@ -75,8 +77,10 @@ class KiviDecodeStep:
         for name, t in (("key", key), ("value", value)):
             if t.dtype != torch.bfloat16 or not t.is_contiguous() or t.shape != (B, H, D):
                 raise RuntimeError(f"kivi_decode_step: {name} must be contiguous bf16 [{B}, {H}, {D}]")
-        if block_table.dtype != torch.int32 or block_table.stride(1) != 1:
-            raise RuntimeError("kivi_decode_step: block_table must be int32 with contiguous rows")
+        if block_table is not None:
+            require_cuda("kivi_decode_step", block_table)
+            if block_table.dtype != torch.int32 or block_table.stride(1) != 1:
+                raise RuntimeError("kivi_decode_step: block_table must be int32 with contiguous rows")
         if block_table_host.dtype != np.int32 or not block_table_host.flags.c_contiguous:
             block_table_host = np.ascontiguousarray(block_table_host, dtype=np.int32)
         max_len = max(int(seq_lens.max()) if seq_lens.size else 1, 1)
@@ -88,7 +92,8 @@ class KiviDecodeStep:
         ws = WORKSPACE.get(self._device, self._ws_need)
         rc = self._lib.qkv_kivi_decode_step(
             self._handle, self._window, B, rows.ctypes.data, slots.ctypes.data, seq_lens.ctypes.data,
-            block_table_host.ctypes.data, block_table_host.shape[1], block_table.data_ptr(), block_table.stride(0),
+            block_table_host.ctypes.data, block_table_host.shape[1],
+            0 if block_table is None else block_table.data_ptr(), 0 if block_table is None else block_table.stride(0),
             query.data_ptr(), query.stride(0), key.data_ptr(), value.data_ptr(), *self._static, Hq, H, D,
             group_size, blk, nb, scale, ptr(ws), 0 if ws is None else ws.numel(), out.data_ptr(), out.stride(0),
             stream_handle(self._device),
