@@ -17,8 +17,8 @@ for N > 1, by the all-gather. The caches (1.22 GB / N per GPU) exceed the
 Reported on one JSON line (rank 0):
   value     tokens/s/layer over all GPUs, inputs resident in HBM, device-timed
             with CUDA events, max over ranks; the step is captured once as a
-            CUDA graph (decode + combine [+ all-gather]) and replayed, as a
-            serving loop does;
+            CUDA graph (decode + combine [+ the NVLink peer all-gather of the
+            heads, qkv_peer_allgather]) and replayed, as a serving loop does;
   roofline  algorithmic bytes per decode call / its CUDA-event time vs the
             measured HBM copy bandwidth (MEASURED_PEAKS.json);
   pack      KIVI pack GB/s (config 2 definition, 5248 B/token);
@@ -180,7 +180,7 @@ def workload_config(cfg, n):
         "batch": cfg["batch"], "context": cfg["context"], "num_heads": cfg["num_heads"],
         "num_kv_heads": cfg["num_kv_heads"], "head_size": cfg["head_size"], "group_size": cfg["group_size"],
         "residual": cfg["residual"], "block_size": cfg["block_size"],
-        "parallelism": f"kv-head shard x{n}" + (" + NCCL all-gather" if n > 1 else ""),
+        "parallelism": f"kv-head shard x{n}" + (" + NVLink peer all-gather" if n > 1 else ""),
         "l2": "inputs larger than L2 (KIVI cache 1.22 GB / N per GPU), no flush",
     }
 
@@ -808,12 +808,12 @@ def run_e2e(w, device, steps, warmup, world=1, rank=0):
     import torch
     import torch.distributed as dist
 
-    from qkv_b200.distributed import HeadShard, gather_heads
+    from qkv_b200.distributed import HeadShard, PeerGather, gather_heads
 
     impl = e2e_impl(w, device)
     B, Hq, H, D = w.B, w.Hql, w.Hl, w.D
     shard = HeadShard(rank, world, num_kv_heads=H * world, num_heads=Hq * world)
-    g_buf = torch.empty(world * B, Hq, D, dtype=torch.bfloat16, device=device) if world > 1 else None
+    peer = PeerGather(shard, B, D, device) if world > 1 else None
     bt_host = w.bt.numpy()
     total = steps + warmup
     gen = torch.Generator().manual_seed(7)
@@ -869,7 +869,9 @@ def run_e2e(w, device, steps, warmup, world=1, rank=0):
         ev_used[s].record(compute)
         if i + 1 < total:
             upload(i + 1)
-        res[s] = gather_heads(out_d[s], shard, gathered=g_buf, out=None if res_d is None else res_d[s])
+        # the gathered heads leave the peer buffer at once (its next call
+        # reuses it): into this step's slot, which the download reads
+        res[s] = gather_heads(out_d[s], shard, out=None if res_d is None else res_d[s], peer=peer)
         ev_out[s].record(compute)
         # the previous step's output goes down now: queued behind this step's
         # host-to-device staging copy, not ahead of it
@@ -941,17 +943,21 @@ def main():
         return
     w = build_workload(cfg, rank, world, device)
     out = torch.empty(w.B, w.Hql, w.D, dtype=torch.bfloat16, device=device)
-    gathered = torch.empty(world, w.B, w.Hql, w.D, dtype=torch.bfloat16, device=device) if world > 1 else None
-    full = torch.empty(w.B, cfg["num_heads"], w.D, dtype=torch.bfloat16, device=device)
+    peer = None
+    if world > 1:
+        from qkv_b200.distributed import HeadShard, PeerGather
+
+        peer = PeerGather(HeadShard(rank, world, num_kv_heads=cfg["num_kv_heads"], num_heads=cfg["num_heads"]),
+                          w.B, w.D, device)
+        full = torch.empty(w.B, cfg["num_heads"], w.D, dtype=torch.bfloat16, device=device)
 
     def decode():
         kivi_paged_decode(w.q, w.views, w.rk, w.rv, w.bt_dev, w.seq_lens, w.state, w.g, w.D ** -0.5, out, w.L)
 
     def step():
         decode()
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, out)
-            full.view(w.B, world, w.Hql, w.D).copy_(gathered.permute(1, 0, 2, 3))
+        if peer is not None:
+            peer.gather(out, out=full)  # every rank's heads into every rank's [B, Hq, D]
 
     if args.only == "kivi":
         decode_ms = time_loop(decode, args.steps, args.warmup, device)

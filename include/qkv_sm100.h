@@ -62,7 +62,8 @@ QKV_API int qkv_last_error(char* buf, int len);
  * (1 = slot out of range, 2 = block id out of range, 3 = residual row out of
  * range, 4 = block-table entry negative for a live token, 5 = a bounded wait
  * on an in-kernel copy gave up, 6 = window plan source or lane out of
- * range). Returns QKV_OK or QKV_ERR_CUDA. */
+ * range, 7 = a bounded wait for the other ranks of a peer all-gather gave
+ * up). Returns QKV_OK or QKV_ERR_CUDA. */
 QKV_API int qkv_device_error(int* code, qkv_stream_t stream);
 
 /* ------------------------------------------------------------------------
@@ -459,6 +460,46 @@ QKV_API int qkv_kivi_decode_step(
     int block_size, int64_t num_blocks, float scale, void* workspace,
     size_t workspace_bytes, void* out, int64_t out_stride,
     qkv_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * NVLink peer all-gather of the KV-head-sharded outputs
+ *
+ * With the KV heads sharded over N GPUs (rank i owns KV heads
+ * [KVH i/N, KVH (i+1)/N) and the query heads reading them; the per-head cache
+ * layout is the reference's with num_kv_heads = KVH/N, as its host-TP test
+ * builds it, tests/test_kivi_int4.py:1484-1494), the outputs [B, Hq/N, D]
+ * are reassembled into [B, Hq, D] on every rank by one kernel per call: each
+ * 4-byte word of this rank's slice goes to every peer's receive buffer
+ * (peer memory opened through CUDA IPC) in one 8-byte store together with
+ * the call's epoch, and the receivers poll the flags. No barrier; the epoch
+ * is kept on the device, so the call can be captured in a CUDA graph. Waits
+ * give up after about a second (device error 7). Every rank makes the same
+ * calls in the same order, and the call's CTAs (at most 128) must be able to
+ * run at once (no other kernel filling the GPU).
+ *
+ * qkv_peer_alloc     one rank's receive buffer for slices of up to
+ *                    slice_bytes_max bytes (a multiple of 16) from `world`
+ *                    ranks, zeroed; qkv_peer_buffer_bytes gives its size
+ * qkv_ipc_handle     the 64-byte CUDA IPC handle of such a buffer, to send to
+ *                    the other ranks; qkv_ipc_open maps a peer's, _close
+ *                    unmaps it
+ * qkv_peer_allgather local [batch, row_bytes] (this rank's heads of each
+ *                    request), buffers[r] = rank r's buffer as mapped here
+ *                    (this rank's own at [rank]), out [batch, world *
+ *                    row_bytes] on this rank: rank r's row b lands at byte
+ *                    (b * world + r) * row_bytes.
+ * ---------------------------------------------------------------------- */
+#define QKV_IPC_HANDLE_BYTES 64
+QKV_API size_t qkv_peer_buffer_bytes(int64_t slice_bytes_max, int world);
+QKV_API int qkv_peer_alloc(int64_t slice_bytes_max, int world, void** ptr);
+QKV_API int qkv_peer_free(void* ptr);
+QKV_API int qkv_ipc_handle(const void* ptr, void* handle_out);
+QKV_API int qkv_ipc_open(const void* handle, void** ptr);
+QKV_API int qkv_ipc_close(void* ptr);
+QKV_API int qkv_peer_allgather(const void* local, int64_t batch,
+                               int64_t row_bytes, void* const* buffers,
+                               int64_t slice_bytes_max, void* out, int rank,
+                               int world, qkv_stream_t stream);
 
 #ifdef __cplusplus
 }

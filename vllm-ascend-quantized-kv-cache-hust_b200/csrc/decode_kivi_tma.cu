@@ -808,8 +808,9 @@ int kivi_tma_ctas_per_sm(int group) {
 }
 
 // Splits chosen for whole waves: among split counts that keep each split
-// within kMaxPages pages, the one whose grid best fills its last wave, with a
-// small charge per split for the partial-state traffic of the combine.
+// within kMaxPages pages, the one whose grid (window CTAs included) best
+// fills its last wave, with a small charge per split for the partial-state
+// traffic of the combine.
 SplitPlan plan_kivi_tma(int batch, int kvh, int group, int max_seq_len, int sms) {
   SplitPlan plan;
   const int pages = max_seq_len > 0 ? (max_seq_len + kBlk - 1) / kBlk : 1;
@@ -825,7 +826,8 @@ SplitPlan plan_kivi_tma(int batch, int kvh, int group, int max_seq_len, int sms)
     const int pps = (pages + s - 1) / s;
     if (pps > kMaxPages) continue;
     const int se = (pages + pps - 1) / pps;
-    const long long grid = static_cast<long long>(units) * se;
+    // the window CTAs are short but take their slots when the grid starts
+    const long long grid = static_cast<long long>(units) * (se + kTailCtas);
     const long long waves = (grid + resident - 1) / resident;
     const double eff = static_cast<double>(grid) / static_cast<double>(waves * resident);
     const double score = eff - 0.004 * se;

@@ -46,6 +46,7 @@ enum DeviceError : int {
   kErrNegativeBlock = 4,
   kErrPipelineTimeout = 5,  // a bounded wait on an in-kernel copy gave up
   kErrWindowSource = 6,     // a window plan source or lane out of range
+  kErrPeerTimeout = 7,      // a bounded wait for the other ranks' flags gave up
 };
 
 // Device address of this device's error word (a __device__ int defined in

@@ -62,13 +62,97 @@ class HeadShard:
         return x.narrow(dim, a, b - a)
 
 
+class PeerGather:
+    """All-gather of the sharded ``[B, Hq/N, D]`` outputs over NVLink peer
+    memory (``qkv_peer_allgather``): one kernel per call sends this rank's
+    heads into every peer's receive buffer, each word stored together with
+    the call's epoch, and assembles ``[B, Hq, D]`` from what the peers sent
+    (no barrier; graph-capturable; waits bounded). Built collectively: every
+    rank constructs it with the same arguments (its buffer's CUDA IPC handle
+    goes to the others through ``all_gather_object``) and makes the same
+    ``gather`` calls in order."""
+
+    def __init__(self, shard: HeadShard, max_batch: int, head_size: int, device: torch.device | str,
+                 group=None) -> None:
+        import ctypes
+
+        import torch.distributed as dist
+
+        from .ops import _lib
+
+        if shard.world > 8:
+            raise ValueError("PeerGather supports up to 8 ranks")
+        self._lib = lib = _lib.load()
+        self.shard, self.device = shard, torch.device(device)
+        self.max_batch, self.head_size = max_batch, head_size
+        self.row_bytes = shard.local_heads * head_size * 2
+        self.slice_bytes = (max_batch * self.row_bytes + 15) // 16 * 16
+        own = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.check(lib.qkv_peer_alloc(self.slice_bytes, shard.world, ctypes.byref(own)), "qkv_peer_alloc")
+            handle = ctypes.create_string_buffer(64)
+            _lib.check(lib.qkv_ipc_handle(own, handle), "qkv_ipc_handle")
+            handles: list = [None] * shard.world
+            dist.all_gather_object(handles, handle.raw, group=group)
+            peers = []
+            for r, h in enumerate(handles):
+                if r == shard.rank:
+                    peers.append(own.value)
+                    continue
+                p = ctypes.c_void_p()
+                _lib.check(lib.qkv_ipc_open(ctypes.create_string_buffer(h, 64), ctypes.byref(p)), "qkv_ipc_open")
+                peers.append(p.value)
+        self._own, self._peers = own.value, peers
+        self._buffers = (ctypes.c_void_p * shard.world)(*peers)
+        self._buffers_ptr = ctypes.addressof(self._buffers)
+
+    def gather(self, local_out: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """``local_out`` bf16 ``[B, Hq/N, D]`` contiguous -> ``out`` (or a new
+        tensor) bf16 ``[B, Hq, D]``."""
+        from .ops import _lib
+        from .ops._torch import require_cuda, stream_handle
+
+        B = local_out.shape[0]
+        if (local_out.dtype != torch.bfloat16 or not local_out.is_contiguous() or B > self.max_batch
+                or tuple(local_out.shape[1:]) != (self.shard.local_heads, self.head_size)):
+            raise RuntimeError(f"PeerGather: expected contiguous bf16 [<= {self.max_batch}, "
+                               f"{self.shard.local_heads}, {self.head_size}]")
+        if out is None:
+            out = torch.empty(B, self.shard.num_heads, self.head_size, dtype=torch.bfloat16, device=self.device)
+        elif (out.dtype != torch.bfloat16 or not out.is_contiguous()
+              or tuple(out.shape) != (B, self.shard.num_heads, self.head_size)):
+            raise RuntimeError("PeerGather: out must be contiguous bf16 [B, Hq, D]")
+        require_cuda("PeerGather", local_out, out)
+        rc = self._lib.qkv_peer_allgather(local_out.data_ptr(), B, self.row_bytes, self._buffers_ptr,
+                                          self.slice_bytes, out.data_ptr(), self.shard.rank, self.shard.world,
+                                          stream_handle(self.device))
+        _lib.check(rc, "qkv_peer_allgather")
+        return out
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers and frees this rank's (after every rank
+        has finished its calls)."""
+        if self._own is None:
+            return
+        for r, p in enumerate(self._peers):
+            if r != self.shard.rank:
+                self._lib.qkv_ipc_close(p)
+        self._lib.qkv_peer_free(self._own)
+        self._own = None
+
+
 def gather_heads(local_out: torch.Tensor, shard: HeadShard, group=None,
-                 gathered: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+                 gathered: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                 peer: PeerGather | None = None) -> torch.Tensor:
     """All-gathers every rank's ``[B, Hq/N, D]`` attention output into
     ``[B, Hq, D]`` (rank-major head order, i.e. the model's head order).
-    One collective; ``gathered``/``out`` may be preallocated."""
+    With ``peer`` the NVLink peer all-gather runs (one kernel, writing the
+    final layout); otherwise one NCCL collective and a head permute;
+    ``gathered``/``out`` may be preallocated."""
     import torch.distributed as dist
 
+    if shard.world > 1 and peer is not None:
+        return peer.gather(local_out.contiguous(), out=out)
     if shard.world == 1:
         if out is not None:
             out.copy_(local_out)
@@ -85,4 +169,4 @@ def gather_heads(local_out: torch.Tensor, shard: HeadShard, group=None,
     return out
 
 
-__all__ = ["HeadShard", "gather_heads"]
+__all__ = ["HeadShard", "PeerGather", "gather_heads"]

@@ -121,6 +121,13 @@ SIGNATURES: dict[str, tuple] = {
             c_int, c_int, c_int, c_int, c_int, c_i64, c_float, c_vp, c_size, c_vp, c_i64, c_vp,
         ],
     ),
+    "qkv_peer_buffer_bytes": (c_size, [c_i64, c_int]),
+    "qkv_peer_alloc": (c_int, [c_i64, c_int, ctypes.POINTER(c_vp)]),
+    "qkv_peer_free": (c_int, [c_vp]),
+    "qkv_ipc_handle": (c_int, [c_vp, c_vp]),
+    "qkv_ipc_open": (c_int, [c_vp, ctypes.POINTER(c_vp)]),
+    "qkv_ipc_close": (c_int, [c_vp]),
+    "qkv_peer_allgather": (c_int, [c_vp, c_i64, c_i64, c_vp, c_i64, c_vp, c_int, c_int, c_vp]),
     "qkv_fp8_store": (
         c_int, [c_vp, c_vp, c_int, c_vp, c_int, c_i64, c_int, c_int, c_int, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp],
     ),
@@ -207,6 +214,7 @@ DEVICE_ERRORS = {
     4: "block table entry negative for a live token",
     5: "a bounded wait on an in-kernel copy gave up",
     6: "window plan source or lane out of range",
+    7: "a bounded wait for the other ranks of a peer all-gather gave up",
 }
 
 
