@@ -17,8 +17,9 @@ for N > 1, by the all-gather. The caches (1.22 GB / N per GPU) exceed the
 Reported on one JSON line (rank 0):
   value     tokens/s/layer over all GPUs, inputs resident in HBM, device-timed
             with CUDA events, max over ranks; the step is captured once as a
-            CUDA graph (decode + combine [+ the NVLink peer all-gather of the
-            heads, qkv_peer_allgather]) and replayed, as a serving loop does;
+            CUDA graph (decode + combine; for N > 1 the combine runs fused
+            with the NVLink peer all-gather of the heads,
+            qkv_peer_combine_allgather) and replayed, as a serving loop does;
   roofline  algorithmic bytes per decode call / its CUDA-event time vs the
             measured HBM copy bandwidth (MEASURED_PEAKS.json);
   pack      KIVI pack GB/s (config 2 definition, 5248 B/token);
@@ -955,9 +956,14 @@ def main():
         kivi_paged_decode(w.q, w.views, w.rk, w.rv, w.bt_dev, w.seq_lens, w.state, w.g, w.D ** -0.5, out, w.L)
 
     def step():
-        decode()
-        if peer is not None:
-            peer.gather(out, out=full)  # every rank's heads into every rank's [B, Hq, D]
+        if peer is None:
+            decode()
+            return
+        # the decode leaves its split partials; one kernel merges them and
+        # sends every rank's heads into every rank's [B, Hq, D]
+        parts = kivi_paged_decode(w.q, w.views, w.rk, w.rv, w.bt_dev, w.seq_lens, w.state, w.g, w.D ** -0.5, out,
+                                  w.L, partials=True)
+        peer.gather_partials(parts, out, out=full)
 
     if args.only == "kivi":
         decode_ms = time_loop(decode, args.steps, args.warmup, device)

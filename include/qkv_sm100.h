@@ -198,6 +198,22 @@ QKV_API int qkv_kivi_paged_decode(
     int head_size, int group_size, int block_size, int64_t num_blocks,
     int max_seq_len, float scale, void* workspace, size_t workspace_bytes,
     void* out, int64_t out_stride, qkv_stream_t stream);
+/* qkv_kivi_paged_decode for a consumer that merges the split partials itself
+ * (qkv_peer_combine_allgather): when the page-pipelined kernel runs with
+ * several splits, the [B, Hq, splits, D] fp32 sums and the [B, Hq, splits, 2]
+ * (max, sum) pairs that follow them stay at the start of `workspace`, no
+ * combine runs, and *splits_used receives the split count; otherwise `out`
+ * is written as by qkv_kivi_paged_decode and *splits_used = 1. */
+QKV_API int qkv_kivi_paged_decode_partials(
+    const void* query, int64_t q_stride, const int32_t* k_quant,
+    const float* k_scale, const float* k_mn, const int32_t* v_quant,
+    const float* v_scale, const float* v_mn, const void* res_key,
+    const void* res_value, int res_rows, int res_capacity,
+    const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
+    const int32_t* res_state, int batch, int num_heads, int num_kv_heads,
+    int head_size, int group_size, int block_size, int64_t num_blocks,
+    int max_seq_len, float scale, void* workspace, size_t workspace_bytes,
+    void* out, int64_t out_stride, int* splits_used, qkv_stream_t stream);
 
 /* qkv_kivi_paged_decode for callers that cannot allocate device memory. This
  * entry point has no counterpart in the reference; it exists for callers of
@@ -500,6 +516,21 @@ QKV_API int qkv_peer_allgather(const void* local, int64_t batch,
                                int64_t row_bytes, void* const* buffers,
                                int64_t slice_bytes_max, void* out, int rank,
                                int world, qkv_stream_t stream);
+/* qkv_peer_allgather fused with the split combine of a decode: with
+ * splits > 1, one warp per (request, local head) row merges the splits left
+ * by qkv_kivi_paged_decode_partials (partial_acc [batch, local_heads, splits,
+ * head_size] fp32, partial_ml [batch, local_heads, splits, 2]) exactly as the
+ * decode's own combine does, and the bf16 results go out as in
+ * qkv_peer_allgather; with splits <= 1 `local` (the decode's output) is
+ * gathered as is. */
+QKV_API int qkv_peer_combine_allgather(const float* partial_acc,
+                                       const float* partial_ml, int splits,
+                                       int64_t batch, int local_heads,
+                                       int head_size, const void* local,
+                                       void* const* buffers,
+                                       int64_t slice_bytes_max, void* out,
+                                       int rank, int world,
+                                       qkv_stream_t stream);
 
 #ifdef __cplusplus
 }

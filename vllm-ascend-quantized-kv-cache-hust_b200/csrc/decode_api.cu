@@ -13,7 +13,7 @@ SplitPlan plan_generic(const DecodeParams& p, bool kivi, int max_seq_len);
 bool kivi_tma_geometry(const DecodeParams& p);
 bool kivi_tma_supported(const DecodeParams& p);
 SplitPlan plan_kivi_tma(int batch, int kvh, int group, int max_seq_len, int sms);
-int launch_kivi_tma(const DecodeParams& p, cudaStream_t stream);
+int launch_kivi_tma(const DecodeParams& p, cudaStream_t stream, bool combine = true, int* splits_used = nullptr);
 bool int8_tma_geometry(const DecodeParams& p);
 bool int8_tma_supported(const DecodeParams& p);
 SplitPlan plan_int8_tma(int batch, int kvh, int max_seq_len, int sms);
@@ -178,7 +178,13 @@ int qkv_int8_paged_decode(const void* query, int64_t q_stride,
   return launch_decode_generic(p, kInt8Pages, s);  // planned for it by plan_for
 }
 
-int qkv_kivi_paged_decode(
+namespace qkv {
+namespace {
+
+// The KIVI decode; with combine == false and several splits on the
+// page-pipelined kernel, the split partials stay in the workspace and
+// *splits_used reports their count (1: `out` was written).
+int kivi_decode(
     const void* query, int64_t q_stride, const int32_t* k_quant,
     const float* k_scale, const float* k_mn, const int32_t* v_quant,
     const float* v_scale, const float* v_mn, const void* res_key,
@@ -187,8 +193,8 @@ int qkv_kivi_paged_decode(
     const int32_t* res_state, int batch, int num_heads, int num_kv_heads,
     int head_size, int group_size, int block_size, int64_t num_blocks,
     int max_seq_len, float scale, void* workspace, size_t workspace_bytes_,
-    void* out, int64_t out_stride, qkv_stream_t stream) {
-  using namespace qkv;
+    void* out, int64_t out_stride, qkv_stream_t stream, bool combine, int* splits_used) {
+  if (splits_used != nullptr) *splits_used = 1;
   int rc = check_decode_args("qkv_kivi_paged_decode", batch, num_heads,
                              num_kv_heads, head_size, block_size, num_blocks,
                              max_seq_len);
@@ -238,19 +244,60 @@ int qkv_kivi_paged_decode(
   p.num_hist_splits = plan.hist_splits;
   p.split_tokens = plan.split_tokens;
   p.splits_total = plan.total;
-  const size_t need = workspace_bytes(batch, num_heads, head_size, plan.total);
+  const bool tma = kivi_tma_supported(p);
+  // the page-pipelined kernel has window CTAs only when there is a window:
+  // the partials (and their layout in the workspace) shrink to match
+  if (tma && res_state == nullptr) p.splits_total = p.num_hist_splits;
+  const size_t need = workspace_bytes(batch, num_heads, head_size, p.splits_total);
   if (need > 0) {
     if (workspace == nullptr || workspace_bytes_ < need)
       return set_error(QKV_ERR_WORKSPACE,
                        "qkv_kivi_paged_decode: workspace needs " +
                            std::to_string(need) + " bytes");
     p.ws_acc = static_cast<float*>(workspace);
-    p.ws_ml = p.ws_acc + static_cast<size_t>(batch) * num_heads * plan.total *
+    p.ws_ml = p.ws_acc + static_cast<size_t>(batch) * num_heads * p.splits_total *
                              head_size;
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (kivi_tma_supported(p)) return launch_kivi_tma(p, s);
+  if (tma) return launch_kivi_tma(p, s, combine, splits_used);
   return launch_decode_generic(p, kKiviPages, s);  // planned for it by plan_for
+}
+
+}  // namespace
+}  // namespace qkv
+
+int qkv_kivi_paged_decode(
+    const void* query, int64_t q_stride, const int32_t* k_quant,
+    const float* k_scale, const float* k_mn, const int32_t* v_quant,
+    const float* v_scale, const float* v_mn, const void* res_key,
+    const void* res_value, int res_rows, int res_capacity,
+    const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
+    const int32_t* res_state, int batch, int num_heads, int num_kv_heads,
+    int head_size, int group_size, int block_size, int64_t num_blocks,
+    int max_seq_len, float scale, void* workspace, size_t workspace_bytes_,
+    void* out, int64_t out_stride, qkv_stream_t stream) {
+  return qkv::kivi_decode(query, q_stride, k_quant, k_scale, k_mn, v_quant, v_scale, v_mn, res_key, res_value,
+                          res_rows, res_capacity, block_table, bt_stride, seq_lens, res_state, batch, num_heads,
+                          num_kv_heads, head_size, group_size, block_size, num_blocks, max_seq_len, scale,
+                          workspace, workspace_bytes_, out, out_stride, stream, true, nullptr);
+}
+
+int qkv_kivi_paged_decode_partials(
+    const void* query, int64_t q_stride, const int32_t* k_quant,
+    const float* k_scale, const float* k_mn, const int32_t* v_quant,
+    const float* v_scale, const float* v_mn, const void* res_key,
+    const void* res_value, int res_rows, int res_capacity,
+    const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
+    const int32_t* res_state, int batch, int num_heads, int num_kv_heads,
+    int head_size, int group_size, int block_size, int64_t num_blocks,
+    int max_seq_len, float scale, void* workspace, size_t workspace_bytes_,
+    void* out, int64_t out_stride, int* splits_used, qkv_stream_t stream) {
+  using namespace qkv;
+  QKV_CHECK_ARG(splits_used != nullptr, "qkv_kivi_paged_decode_partials: null splits_used");
+  return kivi_decode(query, q_stride, k_quant, k_scale, k_mn, v_quant, v_scale, v_mn, res_key, res_value, res_rows,
+                     res_capacity, block_table, bt_stride, seq_lens, res_state, batch, num_heads, num_kv_heads,
+                     head_size, group_size, block_size, num_blocks, max_seq_len, scale, workspace, workspace_bytes_,
+                     out, out_stride, stream, false, splits_used);
 }
 
 size_t qkv_dense_prefill_workspace(int total_q, int num_heads,

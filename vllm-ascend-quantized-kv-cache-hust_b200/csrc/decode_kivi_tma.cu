@@ -842,10 +842,11 @@ SplitPlan plan_kivi_tma(int batch, int kvh, int group, int max_seq_len, int sms)
   return plan;
 }
 
-int launch_kivi_tma(const DecodeParams& p0, cudaStream_t stream) {
+int launch_kivi_tma(const DecodeParams& p0, cudaStream_t stream, bool combine, int* splits_used) {
   DecodeParams p = p0;
   // window CTAs only when there is a window; the partial count shrinks to match
   if (p.res_state == nullptr) p.splits_total = p.num_hist_splits;
+  if (splits_used != nullptr) *splits_used = p.splits_total;
   CUtensorMap tk, tv;
   int rc = encode_maps(p, &tk, &tv);
   if (rc != QKV_OK) return rc;
@@ -858,7 +859,7 @@ int launch_kivi_tma(const DecodeParams& p0, cudaStream_t stream) {
     kivi_decode_tma_kernel<2><<<grid, kThreads, kivi_smem_bytes<2>(), stream>>>(p, tk, tv);
   }
   QKV_CHECK_LAUNCH("kivi_decode_tma_kernel");
-  if (p.splits_total > 1) {
+  if (p.splits_total > 1 && combine) {
     launch_combine(p, stream);
     QKV_CHECK_LAUNCH("combine_kernel");
   }

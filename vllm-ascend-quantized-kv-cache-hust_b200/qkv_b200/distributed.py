@@ -129,6 +129,34 @@ class PeerGather:
         _lib.check(rc, "qkv_peer_allgather")
         return out
 
+    def gather_partials(self, partials, local_out: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """The split combine of a decode fused with the gather
+        (``qkv_peer_combine_allgather``): ``partials`` is the
+        ``DecodePartials`` that ``kivi_paged_decode(..., partials=True)``
+        returned for ``local_out`` bf16 ``[B, Hq/N, D]``; -> ``out`` (or a
+        new tensor) bf16 ``[B, Hq, D]``."""
+        from .ops import _lib
+        from .ops._torch import require_cuda, stream_handle
+
+        if partials.splits <= 1:
+            return self.gather(local_out, out=out)
+        B = partials.batch
+        if (partials.num_heads != self.shard.local_heads or partials.head_size != self.head_size
+                or B > self.max_batch or local_out.shape[0] != B):
+            raise RuntimeError("PeerGather: partials of another geometry")
+        if out is None:
+            out = torch.empty(B, self.shard.num_heads, self.head_size, dtype=torch.bfloat16, device=self.device)
+        elif (out.dtype != torch.bfloat16 or not out.is_contiguous()
+              or tuple(out.shape) != (B, self.shard.num_heads, self.head_size)):
+            raise RuntimeError("PeerGather: out must be contiguous bf16 [B, Hq, D]")
+        require_cuda("PeerGather", partials.workspace, out)
+        rc = self._lib.qkv_peer_combine_allgather(
+            partials.acc_ptr(), partials.ml_ptr(), partials.splits, B, self.shard.local_heads, self.head_size,
+            local_out.data_ptr(), self._buffers_ptr, self.slice_bytes, out.data_ptr(), self.shard.rank,
+            self.shard.world, stream_handle(self.device))
+        _lib.check(rc, "qkv_peer_combine_allgather")
+        return out
+
     def close(self) -> None:
         """Unmaps the peers' buffers and frees this rank's (after every rank
         has finished its calls)."""

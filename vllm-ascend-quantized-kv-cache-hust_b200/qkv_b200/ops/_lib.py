@@ -69,6 +69,15 @@ SIGNATURES: dict[str, tuple] = {
             c_vp, c_size, c_vp, c_i64, c_vp,
         ],
     ),
+    "qkv_kivi_paged_decode_partials": (
+        c_int,
+        [
+            c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int,
+            c_vp, c_i64, c_vp, c_vp,
+            c_int, c_int, c_int, c_int, c_int, c_int, c_i64, c_int, c_float,
+            c_vp, c_size, c_vp, c_i64, ctypes.POINTER(c_int), c_vp,
+        ],
+    ),
     "qkv_kivi_paged_decode_noalloc": (
         c_int,
         [
@@ -128,6 +137,8 @@ SIGNATURES: dict[str, tuple] = {
     "qkv_ipc_open": (c_int, [c_vp, ctypes.POINTER(c_vp)]),
     "qkv_ipc_close": (c_int, [c_vp]),
     "qkv_peer_allgather": (c_int, [c_vp, c_i64, c_i64, c_vp, c_i64, c_vp, c_int, c_int, c_vp]),
+    "qkv_peer_combine_allgather": (
+        c_int, [c_vp, c_vp, c_int, c_i64, c_int, c_int, c_vp, c_vp, c_i64, c_vp, c_int, c_int, c_vp]),
     "qkv_fp8_store": (
         c_int, [c_vp, c_vp, c_int, c_vp, c_int, c_i64, c_int, c_int, c_int, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp],
     ),

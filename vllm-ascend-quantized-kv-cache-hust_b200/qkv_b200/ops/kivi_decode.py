@@ -8,6 +8,9 @@ residual window into the same online softmax."""
 
 from __future__ import annotations
 
+import ctypes
+from typing import NamedTuple
+
 import torch
 
 from . import _lib
@@ -28,13 +31,17 @@ def kivi_paged_decode(
     scale: float,
     out: torch.Tensor,
     max_seq_len: int,
-) -> torch.Tensor:
+    partials: bool = False,
+):
     """Decode attention for ``query`` bf16 ``[B, Hq, D]`` into ``out``.
 
     ``caches`` are the six views ``(k_quant, k_scale, k_mn, v_quant, v_scale,
     v_mn)``; ``residual_key/value`` bf16 ``[rows, cap, KVH, D]``;
     ``res_state`` int32 ``[B, 6]`` (row, k_start, k_len, v_start, v_len, end);
-    ``block_table`` int32 ``[B, >=max_blocks]``; ``seq_lens`` int32 ``[B]``."""
+    ``block_table`` int32 ``[B, >=max_blocks]``; ``seq_lens`` int32 ``[B]``.
+    With ``partials=True`` the split partials stay in the workspace for a
+    combining consumer and a ``DecodePartials`` is returned
+    (``qkv_kivi_paged_decode_partials``)."""
     kq, ks, km, vq, vs, vm = caches
     require_cuda("kivi_paged_decode", query, kq, vq, block_table, seq_lens, out)
     B, Hq, D = query.shape
@@ -61,16 +68,38 @@ def kivi_paged_decode(
     lib = _lib.load()
     need = lib.qkv_kivi_paged_decode_workspace(B, Hq, H, D, group_size, blk, max_seq_len)
     ws = WORKSPACE.get(query.device, need)
-    rc = lib.qkv_kivi_paged_decode(
+    args = (
         ptr(query), query.stride(0), ptr(kq), ptr(ks), ptr(km), ptr(vq), ptr(vs), ptr(vm),
         ptr(residual_key), ptr(residual_value), rows, cap,
         ptr(bt), bt.stride(0), ptr(sl), ptr(res_state),
         B, Hq, H, D, group_size, blk, nb, max_seq_len, float(scale),
         ptr(ws), 0 if ws is None else ws.numel(), ptr(out), out.stride(0),
-        stream_handle(query.device),
     )
-    _lib.check(rc, "kivi_paged_decode")
-    return out
+    if not partials:
+        _lib.check(lib.qkv_kivi_paged_decode(*args, stream_handle(query.device)), "kivi_paged_decode")
+        return out
+    splits = ctypes.c_int(1)
+    rc = lib.qkv_kivi_paged_decode_partials(*args, ctypes.byref(splits), stream_handle(query.device))
+    _lib.check(rc, "kivi_paged_decode_partials")
+    return DecodePartials(splits.value, ws, B, Hq, D)
 
 
-__all__ = ["RES_STATE_FIELDS", "kivi_paged_decode"]
+class DecodePartials(NamedTuple):
+    """Split partials a decode left in ``workspace`` for a combining consumer
+    (``PeerGather.gather_partials``): ``[B, Hq, splits, D]`` fp32 sums, then
+    ``[B, Hq, splits, 2]`` (max, sum); splits == 1 means ``out`` was written."""
+
+    splits: int
+    workspace: torch.Tensor | None
+    batch: int
+    num_heads: int
+    head_size: int
+
+    def acc_ptr(self) -> int:
+        return self.workspace.data_ptr()
+
+    def ml_ptr(self) -> int:
+        return self.workspace.data_ptr() + self.batch * self.num_heads * self.splits * self.head_size * 4
+
+
+__all__ = ["RES_STATE_FIELDS", "DecodePartials", "kivi_paged_decode"]
