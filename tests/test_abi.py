@@ -70,3 +70,36 @@ def test_ops_refuse_cpu_tensors():
     views = (torch.zeros(4, 16, 2, 4, dtype=torch.int32), torch.zeros(4, 16, 2, 4), torch.zeros(4, 16, 2, 4))
     with pytest.raises(RuntimeError, match="needs CUDA"):
         kivi_pack_value_cache(v, torch.arange(2), *views, 8)
+
+
+def test_peer_allgather_sizes_and_argument_checks():
+    """The NVLink peer all-gather entry points validate before touching the
+    device: bad world / rank, row sizes, slices larger than the buffers and
+    null pointers come back as QKV_ERR_INVALID with a message."""
+    import ctypes
+
+    lib = _lib.load()
+    # receive words: 2 parities x world x (slice / 4) words x 8 bytes, plus 64 control bytes
+    assert lib.qkv_peer_buffer_bytes(65536, 8) == 2 * 8 * (65536 // 4) * 8 + 64
+    assert lib.qkv_peer_buffer_bytes(0, 8) == 0
+    bufs = (ctypes.c_void_p * 2)(16, 32)
+    addr = ctypes.addressof(bufs)
+    cases = [
+        ((16, 4, 64, addr, 4096, 16, 0, 9, None), "world must be 1..8"),
+        ((16, 4, 64, addr, 4096, 16, 2, 2, None), "rank inside it"),
+        ((16, 4, 62, addr, 4096, 16, 0, 2, None), "multiple of 4 bytes"),
+        ((16, 100, 64, addr, 4096, 16, 0, 2, None), "does not fit"),
+        ((None, 4, 64, addr, 4096, 16, 0, 2, None), "null pointer"),
+        ((18, 4, 64, addr, 4096, 16, 0, 2, None), "4-byte aligned"),
+    ]
+    for args, match in cases:
+        assert lib.qkv_peer_allgather(*args) == _lib.QKV_ERR_INVALID
+        assert match in _lib.last_error(), (args, _lib.last_error())
+    # the combine + gather checks its own arguments the same way
+    rc = lib.qkv_peer_combine_allgather(16, 32, 4, 4, 0, 128, 16, addr, 4096, 16, 0, 2, None)
+    assert rc == _lib.QKV_ERR_INVALID and "head sizes" in _lib.last_error()
+    rc = lib.qkv_peer_combine_allgather(None, 32, 4, 4, 2, 128, 16, addr, 1 << 20, 16, 0, 2, None)
+    assert rc == _lib.QKV_ERR_INVALID and "null pointer" in _lib.last_error()
+    out = ctypes.c_void_p()
+    assert lib.qkv_peer_alloc(10, 2, ctypes.byref(out)) == _lib.QKV_ERR_INVALID  # not a multiple of 16
+    assert lib.qkv_ipc_handle(None, None) == _lib.QKV_ERR_INVALID
