@@ -9,7 +9,8 @@
 //         (ops/kivi_gather.py:110-136);
 //         residual positions read the bf16 window
 //         (methods/kivi_int4/attention_backend.py:889-935).
-// The production geometries run the tensor-core kernels in decode_mma.cu.
+// The production geometries run the page-pipelined tensor-core kernels of
+// decode_kivi_tma.cu, decode_int8_tma.cu and decode_fp8_tma.cu.
 #include <math_constants.h>
 
 #include <atomic>
