@@ -2,4 +2,4 @@
 
 from . import fp8_per_token_head, int8_dynamic, kivi_int4  # noqa: F401  (registration side effect)
 
-__all__ = ["int8_dynamic", "kivi_int4"]
+__all__ = ["fp8_per_token_head", "int8_dynamic", "kivi_int4"]
