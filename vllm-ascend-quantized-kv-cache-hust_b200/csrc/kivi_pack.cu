@@ -69,12 +69,24 @@ __device__ __forceinline__ void load8<__half>(const __half* p, float (&v)[8]) {
 // quant group is an aligned run of g/8 of them, so the group min/max is an
 // xor-shuffle reduction. Every lane takes part in the shuffles; only lanes
 // with a valid slot store.
+// Where a packed token's row comes from: token t of `value` (dense), or, with
+// `src`, ring lane src[t] >= 0 of `ring` / new token -1 - src[t] of `fresh`
+// (a window plan's flush sources, read in place).
+template <typename T>
+struct RowSource {
+  const int64_t* src;
+  const T* ring;
+  const T* fresh;
+  int64_t ring_lanes, n_new;
+};
+
 template <typename T>
 __global__ void __launch_bounds__(256)
 pack_value_kernel(const T* __restrict__ value, const void* __restrict__ slots,
                   int slot_dtype, int64_t num_tokens, int kvh, int head_size,
                   int group_size, int64_t num_slots, int32_t* __restrict__ v_quant,
-                  float* __restrict__ v_scale, float* __restrict__ v_mn, int* err) {
+                  float* __restrict__ v_scale, float* __restrict__ v_mn, int* err,
+                  RowSource<T> rs) {
   const int words = head_size >> 3;
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t total = num_tokens * kvh * words;
@@ -94,8 +106,22 @@ pack_value_kernel(const T* __restrict__ value, const void* __restrict__ slots,
   }
 
   float v[8];
-  if (in_range) {
-    load8<T>(value + row * head_size + w * 8, v);
+  const T* rowp = value + row * head_size;
+  if (rs.src != nullptr && in_range) {
+    const int64_t sidx = rs.src[token];
+    const int64_t tok_row = static_cast<int64_t>(kvh) * head_size;
+    if (sidx >= 0 && sidx < rs.ring_lanes) {
+      rowp = rs.ring + sidx * tok_row + static_cast<int64_t>(head) * head_size;
+    } else if (sidx < 0 && -1 - sidx < rs.n_new) {
+      rowp = rs.fresh + (-1 - sidx) * tok_row + static_cast<int64_t>(head) * head_size;
+    } else {
+      if (w == 0) record_error(err, kErrWindowSource);
+      valid = false;
+      rowp = nullptr;
+    }
+  }
+  if (in_range && rowp != nullptr) {
+    load8<T>(rowp + w * 8, v);
   } else {
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = 0.0f;
@@ -378,7 +404,7 @@ int launch_pack_value(const void* value, const void* slots, int slot_dtype,
     const int64_t grid = (threads + block - 1) / block;
     pack_value_kernel<T><<<grid, block, 0, stream>>>(
         v, slots, slot_dtype, num_tokens, kvh, head_size, group_size, num_slots,
-        vq, vs, vm, err);
+        vq, vs, vm, err, RowSource<T>{nullptr, nullptr, nullptr, 0, 0});
     QKV_CHECK_LAUNCH("pack_value_kernel");
   } else {
     const int64_t threads = num_tokens * kvh * (head_size / group_size);
@@ -412,6 +438,27 @@ int check_common(const char* fn, int dtype, int slot_dtype, int64_t num_tokens,
 }
 
 }  // namespace
+
+// Value pack of a window plan's flushed rows read where they are (ring
+// lanes or new tokens, `src` as in qkv_kivi_window_gather), bf16 rings; the
+// vector kernel's geometry only (head_size / 8 a power of two up to 32).
+int pack_value_from_sources(const __nv_bfloat16* ring, int64_t ring_lanes, const __nv_bfloat16* fresh,
+                            int64_t n_new, const int64_t* src, const int64_t* slots, int64_t num_tokens, int kvh,
+                            int head_size, int group_size, int block_size, int64_t num_blocks, int32_t* vq,
+                            float* vs, float* vm, cudaStream_t stream) {
+  if (num_tokens == 0) return QKV_OK;
+  const int words = head_size / 8;
+  QKV_CHECK_ARG((words & (words - 1)) == 0 && words <= 32 && head_size % group_size == 0 && src && slots,
+                "pack_value_from_sources: unsupported geometry");
+  const int64_t threads = num_tokens * kvh * words;
+  const int block = 256;
+  pack_value_kernel<__nv_bfloat16><<<(threads + block - 1) / block, block, 0, stream>>>(
+      nullptr, slots, QKV_I64, num_tokens, kvh, head_size, group_size, num_blocks * block_size, vq, vs, vm,
+      device_error_ptr(), RowSource<__nv_bfloat16>{src, ring, fresh, ring_lanes, n_new});
+  QKV_CHECK_LAUNCH("pack_value_kernel");
+  return QKV_OK;
+}
+
 }  // namespace qkv
 
 extern "C" {

@@ -25,6 +25,17 @@
 #include "window_plan.h"
 
 namespace qkv {
+
+// internal launchers (kivi_pack.cu, window_apply.cu)
+int pack_value_from_sources(const __nv_bfloat16* ring, int64_t ring_lanes, const __nv_bfloat16* fresh,
+                            int64_t n_new, const int64_t* src, const int64_t* slots, int64_t num_tokens, int kvh,
+                            int head_size, int group_size, int block_size, int64_t num_blocks, int32_t* vq,
+                            float* vs, float* vm, cudaStream_t stream);
+int scatter_new_tokens(void* ring_key, void* ring_value, int64_t ring_lanes, const int64_t* k_lanes,
+                       const int64_t* k_src, int64_t nk, const int64_t* v_lanes, const int64_t* v_src, int64_t nv,
+                       const void* new_key, const void* new_value, int64_t n_new, int64_t row_bytes,
+                       cudaStream_t stream);
+
 namespace {
 
 // Pinned staging ring: a buffer is rewritten only after the copy that last
@@ -263,6 +274,30 @@ QKV_API int qkv_kivi_decode_step(
   char* gv = gk + rows_k * row_bytes;
 
   // ---- 4. gather, packs, scatter, decode
+  // A steady decode step (no key window flushes, every ring write a new
+  // token) needs no snapshot: the value pack reads its flushed lanes in place
+  // before the scatter overwrites them (stream order), and the scatter reads
+  // the new tokens directly. Otherwise the plan's rows are gathered first.
+  bool direct = nf[0] == 0 && (head_size / 8 & (head_size / 8 - 1)) == 0 && head_size / 8 <= 32;
+  for (int64_t i = 0; direct && i < nw[0]; ++i) direct = k_src[nf[0] + i] < 0;
+  for (int64_t i = 0; direct && i < nw[1]; ++i) direct = v_src[nf[1] + i] < 0;
+  if (direct) {
+    if (nf[1] > 0) {
+      rc = pack_value_from_sources(static_cast<const __nv_bfloat16*>(res_value), ring_lanes,
+                                   static_cast<const __nv_bfloat16*>(new_value), batch, dv_src, dv_fsl, nf[1],
+                                   num_kv_heads, head_size, group_size, block_size, num_blocks, v_quant, v_scale,
+                                   v_mn, st);
+      if (rc != QKV_OK) return rc;
+    }
+    rc = scatter_new_tokens(res_key, res_value, ring_lanes, dk_lan, dk_src + nf[0], nw[0], dv_lan, dv_src + nf[1],
+                            nw[1], new_key, new_value, batch, row_bytes, st);
+    if (rc != QKV_OK) return rc;
+    return qkv_kivi_paged_decode(query, q_stride, k_quant, k_scale, k_mn, v_quant, v_scale, v_mn, res_key,
+                                 res_value, w->rows, cap, stage_table ? d32 + 7 * batch : block_table,
+                                 stage_table ? table_cols : bt_stride, d32 + 6 * batch, d32, batch, num_heads,
+                                 num_kv_heads, head_size, group_size, block_size, num_blocks, std::max(max_len, 1),
+                                 scale, workspace, workspace_bytes, out, out_stride, stream);
+  }
   if (rows_k + rows_v > 0) {
     rc = qkv_kivi_window_gather(res_key, res_value, ring_lanes, new_key, new_value, batch, dk_src,
                                 static_cast<int64_t>(rows_k), dv_src, static_cast<int64_t>(rows_v), row_bytes, gk, gv,

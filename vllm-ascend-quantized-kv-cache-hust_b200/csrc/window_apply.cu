@@ -35,9 +35,12 @@ __global__ void window_gather_kernel(const uint4* ring_k, const uint4* ring_v, i
   (key ? out_k : out_v)[i * row_words + w] = val;
 }
 
+// Rows written into the ring lanes: item i of the dense k_data / v_data, or,
+// with k_src / v_src, the new token -1 - src[i] of new_k / new_v.
 __global__ void window_scatter_kernel(uint4* ring_k, uint4* ring_v, int64_t ring_lanes, const int64_t* k_lanes,
                                       int64_t nk, const uint4* k_data, const int64_t* v_lanes, int64_t nv,
-                                      const uint4* v_data, int64_t row_words, int* err) {
+                                      const uint4* v_data, int64_t row_words, int* err, const int64_t* k_src,
+                                      const int64_t* v_src, int64_t n_new) {
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t total = (nk + nv) * row_words;
   if (idx >= total) return;
@@ -49,7 +52,16 @@ __global__ void window_scatter_kernel(uint4* ring_k, uint4* ring_v, int64_t ring
     if (w == 0) record_error(err, kErrWindowSource);
     return;
   }
-  (key ? ring_k : ring_v)[lane * row_words + w] = (key ? k_data : v_data)[i * row_words + w];
+  const int64_t* src = key ? k_src : v_src;
+  int64_t row = i;
+  if (src != nullptr) {
+    row = -1 - src[i];
+    if (row < 0 || row >= n_new) {
+      if (w == 0) record_error(err, kErrWindowSource);
+      return;
+    }
+  }
+  (key ? ring_k : ring_v)[lane * row_words + w] = (key ? k_data : v_data)[row * row_words + w];
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -57,6 +69,26 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 unsigned grid_for(int64_t threads, int block) { return static_cast<unsigned>((threads + block - 1) / block); }
 
 }  // namespace
+
+// Ring writes whose rows are all new tokens, read in place (k_src / v_src:
+// -1 - token), one launch for both sides.
+int scatter_new_tokens(void* ring_key, void* ring_value, int64_t ring_lanes, const int64_t* k_lanes,
+                       const int64_t* k_src, int64_t nk, const int64_t* v_lanes, const int64_t* v_src, int64_t nv,
+                       const void* new_key, const void* new_value, int64_t n_new, int64_t row_bytes,
+                       cudaStream_t stream) {
+  if (nk + nv == 0) return QKV_OK;
+  QKV_CHECK_ARG(row_bytes > 0 && row_bytes % 16 == 0 && new_key && new_value && aligned16(new_key) &&
+                    aligned16(new_value) && aligned16(ring_key) && aligned16(ring_value),
+                "scatter_new_tokens: bad rows");
+  const int64_t row_words = row_bytes / 16;
+  const int64_t threads = (nk + nv) * row_words;
+  window_scatter_kernel<<<grid_for(threads, 256), 256, 0, stream>>>(
+      static_cast<uint4*>(ring_key), static_cast<uint4*>(ring_value), ring_lanes, k_lanes, nk,
+      static_cast<const uint4*>(new_key), v_lanes, nv, static_cast<const uint4*>(new_value), row_words,
+      device_error_ptr(), k_src, v_src, n_new);
+  QKV_CHECK_LAUNCH("window_scatter_kernel");
+  return QKV_OK;
+}
 
 }  // namespace qkv
 
@@ -103,7 +135,7 @@ int qkv_kivi_window_scatter(void* ring_key, void* ring_value, int64_t ring_lanes
   window_scatter_kernel<<<grid_for(threads, 256), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<uint4*>(ring_key), static_cast<uint4*>(ring_value), ring_lanes, k_lanes, nk,
       static_cast<const uint4*>(k_data), v_lanes, nv, static_cast<const uint4*>(v_data), row_words,
-      device_error_ptr());
+      device_error_ptr(), nullptr, nullptr, 0);
   QKV_CHECK_LAUNCH("window_scatter_kernel");
   return QKV_OK;
 }
