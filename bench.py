@@ -3,8 +3,9 @@
 Default workload: KIVI INT4 long-context decode,
 32 requests at context 32768, 64 query / 8 KV heads, head 128, group 128,
 residual 128, sharded by KV head across N GPUs (GPU i owns KV heads
-[8i/N, 8(i+1)/N) and their query heads) with one NCCL all-gather of the
-attention outputs per step. The cache of every request is built the way the
+[8i/N, 8(i+1)/N) and their query heads) with one NVLink peer all-gather of
+the attention outputs per step (qkv_peer_combine_allgather, the split combine
+fused into it). The cache of every request is built the way the
 reference builds it — bulk prefill of L-1 tokens (floor(n/r)*r straight to
 int4, the rest to the bf16 window) plus one decode write — with K/V ~ N(0,1)
 in bf16 and x10 key outliers on 2% of (head, channel) pairs.

@@ -445,8 +445,10 @@ QKV_API int qkv_kivi_window_scatter(void* ring_key, void* ring_value,
  * (:562-606) through the window planner, _sync_kivi_residual_windows
  * (:813-836), then _forward_kivi_paged_decode_attention (:1193-1230). Every
  * index the device needs is staged in one pinned buffer and copied once; the
- * gather, packs, ring scatter and decode launch on `stream` with no host
- * sync. qkv_kivi_step_create returns the runtime (staging buffers) of one
+ * value pack, ring scatter and decode launch on `stream` with no host sync
+ * (a steady step reads the flushed lanes and new tokens in place; a step
+ * with a key-window flush, or a ring write from a ring lane, first gathers
+ * the plan's rows and also packs keys). qkv_kivi_step_create returns the runtime (staging buffers) of one
  * caller; destroy releases it.
  *   window            a qkv_window_create handle (its state is updated)
  *   rows, slots       int64 [batch] host: residual row and new-token slot
