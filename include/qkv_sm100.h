@@ -488,12 +488,17 @@ QKV_API int qkv_kivi_decode_step(
  * builds it, tests/test_kivi_int4.py:1484-1494), the outputs [B, Hq/N, D]
  * are reassembled into [B, Hq, D] on every rank by one kernel per call: each
  * 4-byte word of this rank's slice goes to every peer's receive buffer
- * (peer memory opened through CUDA IPC) in one 8-byte store together with
- * the call's epoch, and the receivers poll the flags. No barrier; the epoch
- * is kept on the device, so the call can be captured in a CUDA graph. Waits
- * give up after about a second (device error 7). Every rank makes the same
- * calls in the same order, and the call's CTAs (at most 128) must be able to
- * run at once (no other kernel filling the GPU).
+ * (peer memory opened through CUDA IPC) as one 64-bit scalar store that
+ * carries the call's epoch in its high half, and the receivers poll those
+ * words. No barrier; the epoch is kept on the device, so the call can be
+ * captured in a CUDA graph. Waits give up after about a second (device
+ * error 7). Every rank makes the same calls in the same order, and the
+ * call's CTAs (at most 128) must be able to run at once (no other kernel
+ * filling the GPU). Calls on one rank that use the same buffer set must be
+ * ordered on one stream (or by events): each call reads its epoch from the
+ * buffer's control word, which the previous call's last CTA advances, so two
+ * calls that overlap on the GPU (two streams, two graphs replaying at once)
+ * would take the same epoch and corrupt each other's receive words.
  *
  * qkv_peer_alloc     one rank's receive buffer for slices of up to
  *                    slice_bytes_max bytes (a multiple of 16) from `world`

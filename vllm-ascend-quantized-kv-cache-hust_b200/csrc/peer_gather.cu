@@ -5,10 +5,13 @@
 // [B, Hq, D] layout.
 //
 // Protocol (one round, no barrier, no fence): every 4-byte word of a rank's
-// slice travels to each peer together with the call's epoch in ONE 8-byte
-// store into the peer's receive buffer; a receiver polls each 8-byte word
-// until its flag equals the epoch, then the data word is the current one
-// (an aligned 8-byte store and load are single accesses). Receive buffers are
+// slice travels to each peer together with the call's epoch as ONE 64-bit
+// scalar (epoch << 32 | data), written with one st.relaxed.sys.u64 into the
+// peer's receive buffer; a receiver polls the word with ld.relaxed.sys.u64
+// until its high half equals the epoch, and its low half is then the data of
+// the same store. An aligned 64-bit scalar access is a single access in the
+// PTX memory model, so the epoch is never seen beside a stale data half (a
+// vector access, v2.u32, would be two accesses of unspecified order). Receive buffers are
 // double-buffered by epoch parity: a rank reaches call e + 2 only after every
 // peer has sent its call e + 1 words, i.e. after every peer finished
 // receiving call e, so call e + 2 never overwrites words still unread.
@@ -35,8 +38,8 @@ constexpr long long kPeerWaitCycles = 2000000000LL;  // ~1 s at 2 GHz
 
 struct PeerGatherArgs {
   const uint32_t* local;       // [B, row_words] this rank's slice
-  uint2* recv[kMaxPeers];      // each rank's receive words (as mapped here)
-  const uint2* own;            // recv[rank], passed on its own (no dynamic index)
+  unsigned long long* recv[kMaxPeers];  // each rank's receive words (as mapped here)
+  const unsigned long long* own;        // recv[rank], passed on its own (no dynamic index)
   uint32_t* ctl;               // this rank's control words
   uint32_t* out;               // [B, world * row_words] on this rank
   int64_t batch, row_words;    // row_words = Hq/N * D * 2 / 4
@@ -45,14 +48,18 @@ struct PeerGatherArgs {
   int* err;
 };
 
-__device__ __forceinline__ void store_word(uint2* p, uint32_t data, uint32_t flag) {
-  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};\n" ::"l"(p), "r"(data), "r"(flag) : "memory");
+// One receive word: data in the low 32 bits, the call's epoch in the high 32.
+__device__ __forceinline__ void store_word(unsigned long long* p, uint32_t data, uint32_t flag) {
+  const unsigned long long w = (static_cast<unsigned long long>(flag) << 32) | data;
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;\n" ::"l"(p), "l"(w) : "memory");
 }
-__device__ __forceinline__ uint2 load_word(const uint2* p) {
-  uint2 v;
-  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long load_word(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ uint32_t word_flag(unsigned long long v) { return static_cast<uint32_t>(v >> 32); }
+__device__ __forceinline__ uint32_t word_data(unsigned long long v) { return static_cast<uint32_t>(v); }
 
 // The call's epoch (read by thread 0 of every CTA before any CTA of the call
 // can advance it; a call starts after the previous one ended).
@@ -83,15 +90,15 @@ __device__ void receive_and_finish(const PeerGatherArgs& a, uint32_t e) {
   const int64_t full_row = static_cast<int64_t>(a.world) * a.row_words;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const uint2* mine = a.own + static_cast<int64_t>(par) * a.world * a.slice_words;
+  const unsigned long long* mine = a.own + static_cast<int64_t>(par) * a.world * a.slice_words;
   const long long start = clock64();
   bool ok = true;
   for (int64_t j = t0; j < (a.world - 1) * n && ok; j += stride) {
     const int64_t k = j / n, i = j - k * n;
     const int src = static_cast<int>(k) + (static_cast<int>(k) >= a.rank ? 1 : 0);
-    const uint2* p = mine + static_cast<int64_t>(src) * a.slice_words + i;
-    uint2 v = load_word(p);
-    while (v.y != e) {
+    const unsigned long long* p = mine + static_cast<int64_t>(src) * a.slice_words + i;
+    unsigned long long v = load_word(p);
+    while (word_flag(v) != e) {
       if (clock64() - start > kPeerWaitCycles) {
         ok = false;
         break;
@@ -101,7 +108,7 @@ __device__ void receive_and_finish(const PeerGatherArgs& a, uint32_t e) {
     }
     if (!ok) break;
     const int64_t b = i / a.row_words, w = i - b * a.row_words;
-    a.out[b * full_row + src * a.row_words + w] = v.x;
+    a.out[b * full_row + src * a.row_words + w] = word_data(v);
   }
   if (!ok) record_error(a.err, kErrPeerTimeout);
   // the last CTA of this call advances the epoch for the next one
@@ -281,7 +288,7 @@ int qkv_peer_allgather(const void* local, int64_t batch, int64_t row_bytes, void
   const size_t recv = recv_bytes(slice_bytes_max, world);
   for (int r = 0; r < world; ++r) {
     QKV_CHECK_ARG(buffers[r] != nullptr, "qkv_peer_allgather: null peer buffer");
-    a.recv[r] = static_cast<uint2*>(buffers[r]);
+    a.recv[r] = static_cast<unsigned long long*>(buffers[r]);
   }
   a.ctl = reinterpret_cast<uint32_t*>(static_cast<char*>(buffers[rank]) + recv);
   a.own = a.recv[rank];
@@ -320,7 +327,7 @@ int qkv_peer_combine_allgather(const float* partial_acc, const float* partial_ml
   const size_t recv = recv_bytes(slice_bytes_max, world);
   for (int r = 0; r < world; ++r) {
     QKV_CHECK_ARG(buffers[r] != nullptr, "qkv_peer_combine_allgather: null peer buffer");
-    a.recv[r] = static_cast<uint2*>(buffers[r]);
+    a.recv[r] = static_cast<unsigned long long*>(buffers[r]);
   }
   a.ctl = reinterpret_cast<uint32_t*>(static_cast<char*>(buffers[rank]) + recv);
   a.own = a.recv[rank];

@@ -83,7 +83,7 @@ class PeerGather:
         if shard.world > 8:
             raise ValueError("PeerGather supports up to 8 ranks")
         self._lib = lib = _lib.load()
-        self.shard, self.device = shard, torch.device(device)
+        self.shard, self.device, self.group = shard, torch.device(device), group
         self.max_batch, self.head_size = max_batch, head_size
         self.row_bytes = shard.local_heads * head_size * 2
         self.slice_bytes = (max_batch * self.row_bytes + 15) // 16 * 16
@@ -158,10 +158,18 @@ class PeerGather:
         return out
 
     def close(self) -> None:
-        """Unmaps the peers' buffers and frees this rank's (after every rank
-        has finished its calls)."""
+        """Unmaps the peers' buffers and frees this rank's. Collective: every
+        rank of the group calls it. This rank's stream is synchronised and the
+        ranks pass a barrier first, so no peer can still be running a call
+        that stores into the buffer freed here."""
         if self._own is None:
             return
+        import torch.distributed as dist
+
+        torch.cuda.synchronize(self.device)
+        if dist.is_initialized() and self.shard.world > 1:
+            dist.barrier(group=self.group)
+            torch.cuda.synchronize(self.device)
         for r, p in enumerate(self._peers):
             if r != self.shard.rank:
                 self._lib.qkv_ipc_close(p)
