@@ -69,14 +69,18 @@ def parse():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--e2e-steps", type=int, default=200,
                     help="timed steps of the end-to-end leg (10 untimed first; at most 246), 0 skips it")
-    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true",
+                    help="skip the CPU legs (the oracle's port of the reference's CPU path: timed baseline and the "
+                         "parity check of sampled requests)")
     ap.add_argument("--no-int8", action="store_true", help="skip the config-3 INT8 leg")
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 chunked-prefill leg")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the request count (small cases for ncu captures)")
     ap.add_argument("--only", choices=("kivi", "int8", "config4", "fp8", "small"), default=None,
                     help="run just one decode kernel loop (for ncu captures)")
-    return ap.parse_args()
+    args = ap.parse_args()
+    args.check = not args.no_cpu_baseline
+    return args
 
 
 # ---------------------------------------------------------------------------
@@ -126,6 +130,142 @@ def cpu_reference_sample(cfg, seed=0):
         return O.dense_attention(q, dk, dv, [1], [L], D ** -0.5, causal=True)
 
     return run
+
+
+def _oracle():
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import qkv_oracle as O
+
+    return O
+
+
+def kivi_sample(views, rk, rv, bt, state, lens, blk, reqs):
+    """Host copies of what the reference's KIVI read path needs for requests
+    ``reqs``: their pages of the six views (in block-table order, so the
+    sample's block table is 0..n-1) and their key / value windows in FIFO
+    order, as numpy arrays."""
+    import torch
+
+    bt = bt.cpu()
+    st = state.cpu() if torch.is_tensor(state) else torch.tensor(state)
+    cap = rk.shape[1]
+    out = []
+    for b in reqs:
+        L = int(lens[b])
+        n = (L + blk - 1) // blk
+        pages = bt[b, :n].long()
+        v = [x[pages.to(x.device)].cpu().numpy() for x in views]
+        row, ks, kl, vs, vl, _ = (int(z) for z in st[b])
+
+        def win(buf, start, length):
+            if length <= 0:
+                return None
+            idx = ((start + torch.arange(length)) % cap).to(buf.device)
+            return buf[row, idx].float().cpu().numpy()
+
+        out.append((v, L, win(rk, ks, kl), win(rv, vs, vl)))
+    return out
+
+
+def cpu_check_kivi(c, out, reqs, time_runs=5, scale=None):
+    """The reference's CPU read path (oracle/ numpy port) on requests
+    ``reqs`` of a KIVI workload ``c`` (views, rk, rv, bt, state, lens, q, g,
+    blk, D): its outputs against the GPU's ``out`` rows, with the dequantised
+    K/V cast to bf16 as the reference casts them to the query dtype, and kept
+    in fp32. With ``time_runs`` > 0 the bf16-cast path of the first sampled
+    request is also timed (1 warm-up, then the median of ``time_runs``): the
+    CPU baseline of the leg, in decode tokens/s/layer."""
+    import numpy as np
+
+    O = _oracle()
+    reqs = list(reqs)
+    scale = c.D ** -0.5 if scale is None else scale
+    samples = kivi_sample(c.views, c.rk, c.rv, c.bt, c.state, c.lens, c.blk, reqs)
+    q = c.q.float().cpu().numpy()
+    got = out.float().cpu().numpy()
+    res = {"requests": reqs}
+    for name, cast in (("vs_bf16_cast", True), ("vs_fp32_dequant", False)):
+        want = np.concatenate([
+            O.kivi_decode_reference(v, np.arange((L + c.blk - 1) // c.blk, dtype=np.int32)[None], [L], [kw], [vw],
+                                    q[b:b + 1], c.g, scale, target_bf16=cast)
+            for b, (v, L, kw, vw) in zip(reqs, samples)])
+        res[name] = O.attention_error(got[reqs], want)
+    if time_runs > 0:
+        v, L, kw, vw = samples[0]
+        b = reqs[0]
+        bt0 = np.arange((L + c.blk - 1) // c.blk, dtype=np.int32)[None]
+        run = lambda: O.kivi_decode_reference(v, bt0, [L], [kw], [vw], q[b:b + 1], c.g, scale, target_bf16=True)
+        res["cpu"] = _time_cpu(run, time_runs, f"request {b} (context {L})")
+    return res
+
+
+def cpu_check_int8(c, out, reqs, time_runs=5):
+    """As ``cpu_check_kivi`` for an INT8 workload (kc, vc, k_aq, v_aq, bt,
+    lens, q, blk, D): the reference's dense dequantisation (bf16 ``code *
+    aq``, or kept in fp32) and fp32 attention."""
+    import numpy as np
+
+    O = _oracle()
+    reqs = list(reqs)
+    bt = c.bt.cpu()
+    k_aq, v_aq = c.k_aq.float().cpu().numpy(), c.v_aq.float().cpu().numpy()
+    q = c.q.float().cpu().numpy()
+    got = out.float().cpu().numpy()
+    samples = []
+    for b in reqs:
+        L = int(c.lens[b])
+        pages = bt[b, :(L + c.blk - 1) // c.blk].long().to(c.kc.device)
+        samples.append((c.kc[pages].cpu().numpy(), c.vc[pages].cpu().numpy(), L))
+    res = {"requests": reqs}
+    scale = c.D ** -0.5
+
+    def ref(kc, vc, L, b, cast):
+        bt0 = np.arange(kc.shape[0], dtype=np.int32)[None]
+        return O.int8_decode_reference(kc, vc, k_aq, v_aq, bt0, [L], q[b:b + 1], scale, target_bf16=cast)
+
+    for name, cast in (("vs_bf16_cast", True), ("vs_fp32_dequant", False)):
+        want = np.concatenate([ref(kc, vc, L, b, cast) for b, (kc, vc, L) in zip(reqs, samples)])
+        res[name] = O.attention_error(got[reqs], want)
+    if time_runs > 0:
+        kc, vc, L = samples[0]
+        res["cpu"] = _time_cpu(lambda: ref(kc, vc, L, reqs[0], True), time_runs,
+                               f"request {reqs[0]} (context {L})")
+    return res
+
+
+def _time_cpu(run, runs, what):
+    """1 warm-up, then the median of ``runs`` timed calls: decode tokens/s/layer
+    of one request (one query token per call)."""
+    run()
+    times = []
+    for _ in range(runs):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": 1.0 / t, "unit": UNIT, "seconds_per_request": t, "runs": runs, "sample": what,
+            **cpu_info()}
+
+
+def cpu_info() -> dict:
+    """Host CPU model, logical cores and the BLAS / torch thread counts the
+    numpy port runs with."""
+    model = ""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    try:
+        import torch
+
+        torch_threads = torch.get_num_threads()
+    except Exception:
+        torch_threads = None
+    return {"cpu_model": model, "cpu_count": os.cpu_count(), "cores": cpu_threads(),
+            "torch_threads": torch_threads}
 
 
 def cpu_threads() -> int:
@@ -395,6 +535,15 @@ def run_config4_leg(device, args):
         prefill()
         decode()
 
+    parity = None
+    if args.check:
+        step()
+        torch.cuda.synchronize(device)
+        dec = list(range(len(c.q_lens_pre), len(c.lens)))
+        cd = SimpleNamespace(views=c.views, rk=c.rk, rv=c.rv, bt=c.bt_dec, state=c.st_dec,
+                             lens=[c.lens[b] for b in dec], q=c.q_dec, g=c.g, blk=c.blk, D=c.D)
+        parity = {"decode_rows": cpu_check_kivi(cd, out_dec, [0, 17], time_runs=0),
+                  "chunk_rows": cpu_check_chunks(c, out_pre, [0, 1, 777, c.q_lens_pre[0] - 1])}
     steps = max(3, min(args.steps, 50))
     ms_gather = time_loop(gather, steps, 3, device)
     ms_attn = time_loop(attend, steps, 3, device)
@@ -415,7 +564,38 @@ def run_config4_leg(device, args):
             "gather_frac_of_hbm": gather_gbs / hbm,
             "attn_ms": ms_attn, "prefill_flops": c.prefill_flops, "prefill_tflops": tflops,
             "prefill_frac_of_bf16_peak": tflops / tf_peak,
-            "decode_ms": ms_dec, "decode_bytes": c.decode_bytes, "decode_gbs": gbs, "decode_frac_of_hbm": gbs / hbm}
+            "decode_ms": ms_dec, "decode_bytes": c.decode_bytes, "decode_gbs": gbs, "decode_frac_of_hbm": gbs / hbm,
+            "parity": parity}
+
+
+def cpu_check_chunks(c, out_pre, rows):
+    """Prompt rows of config 4's chunk requests against the reference's
+    generic branch (methods/kivi_int4/attention_backend.py:1157-1191): dense
+    K/V from the int4 pages and the windows (cast to bf16, or kept in fp32),
+    then fp32 attention of query row i over keys [0, L - chunk + i]."""
+    import numpy as np
+
+    O = _oracle()
+    P = len(c.q_lens_pre)
+    C = c.q_lens_pre[0]
+    samples = kivi_sample(c.views, c.rk, c.rv, c.bt_pre, c.st_pre, c.kv_pre, c.blk, range(P))
+    q = c.q_pre.float().cpu().numpy()
+    got = out_pre.float().cpu().numpy()
+    res = {"rows": rows, "requests": P}
+    scale = c.D ** -0.5
+    for name, cast in (("vs_bf16_cast", True), ("vs_fp32_dequant", False)):
+        want, have = [], []
+        for p, (v, L, kw, vw) in enumerate(samples):
+            bt0 = np.arange((L + c.blk - 1) // c.blk, dtype=np.int32)[None]
+            dk, dv = O.kivi_dequant_gather(*v, bt0, [L], c.g, target_bf16=cast)
+            dk, dv = O.overwrite_residual_tail(dk, dv, [L], [kw], [vw])
+            for i in rows:
+                n = L - C + i + 1
+                r = p * C + i
+                want.append(O.dense_attention(q[r:r + 1], dk[:n], dv[:n], [1], [n], scale, causal=True))
+                have.append(got[r:r + 1])
+        res[name] = O.attention_error(np.concatenate(have), np.concatenate(want))
+    return res
 
 
 def run_small_configs(device, args):
@@ -429,13 +609,58 @@ def run_small_configs(device, args):
     caches fit in L2, so L2 is flushed before every timed step."""
     import torch
 
-    from qkv_b200.ops import int8_calc_scales, int8_paged_decode, int8_quant_store, kivi_paged_decode
+    from qkv_b200.ops import int8_paged_decode, kivi_paged_decode
 
     peak = measured_peaks().get("hbm_gbs") or 6650.0
     out = {}
     # ---- config 1
-    gen = torch.Generator(device=device).manual_seed(1001)
-    cpu_gen = torch.Generator().manual_seed(1001)
+    c1 = build_config1(device)
+    D, H, Hq, blk, lens = c1.D, c1.H, c1.Hq, c1.blk, c1.lens
+    o = torch.empty_like(c1.q)
+
+    def dec1():
+        int8_paged_decode(c1.q, c1.kc, c1.vc, c1.k_aq, c1.v_aq, c1.bt_dev, c1.seq_lens, D ** -0.5, o, max(lens))
+
+    dec1()
+    parity1 = cpu_check_int8(c1, o, range(len(lens)), time_runs=0) if args.check else None
+    ms = time_loop_flushed(dec1, args.steps, args.warmup, device)
+    pages = [(L + blk - 1) // blk for L in lens]
+    by = sum(L * H * D * 2 for L in lens) + 2 * H * D * 2 + 2 * len(lens) * Hq * D * 2 + 4 * sum(pages)
+    out["config1"] = {"workload": "BASELINE config 1: INT8, 4 requests at 512/1024/1536/2048, Hq 32 / KVH 8",
+                      "ms_per_step": ms, "tokens_per_s_per_layer": len(lens) / (ms * 1e-3), "bytes_per_launch": by,
+                      "hbm_gbs": by / (ms * 1e-3) / 1e9, "frac_of_measured_hbm": by / (ms * 1e-3) / 1e9 / peak,
+                      "l2": "256 MB buffer written before every timed step", "parity": parity1}
+    # ---- config 2
+    c2 = build_config2(device)
+    o = torch.empty_like(c2.q)
+
+    def dec2():
+        kivi_paged_decode(c2.q, c2.views, c2.rk, c2.rv, c2.bt_dev, c2.seq_lens, c2.state_dev, c2.g, c2.D ** -0.5, o,
+                          max(c2.lens))
+
+    dec2()
+    parity2 = cpu_check_kivi(c2, o, range(len(c2.lens)), time_runs=0) if args.check else None
+    ms = time_loop_flushed(dec2, args.steps, args.warmup, device)
+    by = sum(request_decode_bytes(L, c2.H, c2.Hq, c2.D, c2.g, c2.r, c2.blk) for L in c2.lens)
+    out["config2"] = {"workload": "BASELINE config 2: KIVI INT4 decode, 8 requests at U{1024..8192}, Hq 40 / KVH 8",
+                      "lens": c2.lens, "ms_per_step": ms, "tokens_per_s_per_layer": len(c2.lens) / (ms * 1e-3),
+                      "bytes_per_launch": by, "hbm_gbs": by / (ms * 1e-3) / 1e9,
+                      "frac_of_measured_hbm": by / (ms * 1e-3) / 1e9 / peak,
+                      "l2": "256 MB buffer written before every timed step", "parity": parity2}
+    return out
+
+
+def build_config1(device, seed=1001):
+    """Config 1: INT8, 4 requests at 512 / 1024 / 1536 / 2048, Hq 32 / KVH 8,
+    head 128, block 128; K/V ~ N(0,1) bf16 with 4 fixed channels per head
+    x20; scales from the four prompts as one prefill batch, then every token
+    quantised into the pages through a permuted block table."""
+    import torch
+
+    from qkv_b200.ops import int8_calc_scales, int8_quant_store
+
+    gen = torch.Generator(device=device).manual_seed(seed)
+    cpu_gen = torch.Generator().manual_seed(seed)
     lens, Hq, H, D, blk = [512, 1024, 1536, 2048], 32, 8, 128, 128
     scale = torch.ones(H, D)
     for h in range(H):
@@ -458,33 +683,26 @@ def run_small_configs(device, args):
     vc = torch.zeros_like(kc)
     int8_quant_store(k, v, torch.tensor(slots, device=device), k_inv, v_inv, kc, vc)
     q = torch.randn(len(lens), Hq, D, generator=gen, device=device).to(torch.bfloat16)
-    o = torch.empty_like(q)
-    bt_d, sl = bt.to(device), torch.tensor(lens, dtype=torch.int32, device=device)
-    ms = time_loop_flushed(lambda: int8_paged_decode(q, kc, vc, k_aq, v_aq, bt_d, sl, D ** -0.5, o, max(lens)),
-                   args.steps, args.warmup, device)
-    by = sum(L * H * D * 2 for L in lens) + 2 * H * D * 2 + 2 * len(lens) * Hq * D * 2 + 4 * sum(pages)
-    out["config1"] = {"workload": "BASELINE config 1: INT8, 4 requests at 512/1024/1536/2048, Hq 32 / KVH 8",
-                      "ms_per_step": ms, "tokens_per_s_per_layer": len(lens) / (ms * 1e-3), "bytes_per_launch": by,
-                      "hbm_gbs": by / (ms * 1e-3) / 1e9, "frac_of_measured_hbm": by / (ms * 1e-3) / 1e9 / peak,
-                      "l2": "256 MB buffer written before every timed step"}
-    # ---- config 2
-    gen = torch.Generator(device=device).manual_seed(1002)
-    cpu_gen = torch.Generator().manual_seed(1002)
-    Hq, H, D, g, r = 40, 8, 128, 128, 128
+    return SimpleNamespace(kc=kc, vc=vc, k_aq=k_aq, v_aq=v_aq, bt=bt, bt_dev=bt.to(device), q=q, lens=lens,
+                           seq_lens=torch.tensor(lens, dtype=torch.int32, device=device), H=H, Hq=Hq, D=D, blk=blk,
+                           k=k, v=v, slots=slots)
+
+
+def build_config2(device, seed=1002):
+    """Config 2: KIVI INT4, 8 requests at L ~ U{1024..8192}, Hq 40 / KVH 8,
+    head 128, g 128, r 128, keys x10 on 2% of (head, channel) pairs."""
+    import torch
+
+    gen = torch.Generator(device=device).manual_seed(seed)
+    cpu_gen = torch.Generator().manual_seed(seed)
+    Hq, H, D, g, r, blk = 40, 8, 128, 128, 128, 128
     lens = torch.randint(1024, 8193, (8,), generator=cpu_gen).tolist()
     kv = build_kivi_requests(lens, H, D, g, r, blk, device, cpu_gen, gen)
     q = torch.randn(len(lens), Hq, D, generator=gen, device=device).to(torch.bfloat16)
-    o = torch.empty_like(q)
-    bt_d, sl, st = kv.bt.to(device), torch.tensor(lens, dtype=torch.int32, device=device), kv.state.to(device)
-    ms = time_loop_flushed(lambda: kivi_paged_decode(q, kv.views, kv.rk, kv.rv, bt_d, sl, st, g, D ** -0.5, o, max(lens)),
-                   args.steps, args.warmup, device)
-    by = sum(request_decode_bytes(L, H, Hq, D, g, r, blk) for L in lens)
-    out["config2"] = {"workload": "BASELINE config 2: KIVI INT4 decode, 8 requests at U{1024..8192}, Hq 40 / KVH 8",
-                      "lens": lens, "ms_per_step": ms, "tokens_per_s_per_layer": len(lens) / (ms * 1e-3),
-                      "bytes_per_launch": by, "hbm_gbs": by / (ms * 1e-3) / 1e9,
-                      "frac_of_measured_hbm": by / (ms * 1e-3) / 1e9 / peak,
-                      "l2": "256 MB buffer written before every timed step"}
-    return out
+    return SimpleNamespace(views=kv.views, rk=kv.rk, rv=kv.rv, bt=kv.bt, bt_dev=kv.bt.to(device), state=kv.state,
+                           state_dev=kv.state.to(device), q=q, lens=lens,
+                           seq_lens=torch.tensor(lens, dtype=torch.int32, device=device), H=H, Hq=Hq, D=D, g=g, r=r,
+                           blk=blk)
 
 
 def build_int8_workload(cfg, rank, world, device, seed=4321):
@@ -521,7 +739,7 @@ def build_int8_workload(cfg, rank, world, device, seed=4321):
         int8_quant_store(k, v, slots, k_inv, v_inv, kc, vc)
     torch.cuda.synchronize(device)
     q = torch.randn(B, Hql, D, generator=gen, device=device).to(torch.bfloat16)
-    return SimpleNamespace(kc=kc, vc=vc, k_aq=k_aq, v_aq=v_aq, bt_dev=bt.to(device), q=q,
+    return SimpleNamespace(kc=kc, vc=vc, k_aq=k_aq, v_aq=v_aq, bt=bt, bt_dev=bt.to(device), q=q, lens=[L] * B,
                            seq_lens=torch.full((B,), L, dtype=torch.int32, device=device),
                            B=B, L=L, Hl=Hl, Hql=Hql, D=D, blk=blk)
 
@@ -720,7 +938,7 @@ def measured_peaks() -> dict:
     return {}
 
 
-def bench_pack(device):
+def bench_pack(device, check=False):
     """Pack GB/s (config 2's definition: 5248 B/token = 4096 bf16 in + 1152
     out at KVH 8, D 128, g 128): keys and values of 8192 tokens."""
     import torch
@@ -755,8 +973,44 @@ def bench_pack(device):
         times.append(s.elapsed_time(e) / 1e3)
     t = statistics.median(times)
     by = T * (H * D * 2 * 2 + H * (D // 2 + 8 * D // g) * 2)
-    return {"gbs": by / t / 1e9, "bytes_per_call": by, "us_per_call": t * 1e6, "tokens": T,
-            "bytes_per_token": by // T, "launches_per_call": 2}
+    res = {"gbs": by / t / 1e9, "bytes_per_call": by, "us_per_call": t * 1e6, "tokens": T,
+           "bytes_per_token": by // T, "launches_per_call": 2}
+    if check:
+        res.update(cpu_check_pack(k, v, slots, views, g, by))
+    return res
+
+
+def cpu_check_pack(k, v, slots, views, g, by, runs=5):
+    """The reference's pack arithmetic (oracle/ numpy port of the
+    layout-exact CPU packers) on the same inputs: bit-exact comparison of all
+    six views, and its GB/s on the host (1 warm-up, median of ``runs``)."""
+    import numpy as np
+
+    O = _oracle()
+    kn, vn = k.float().cpu().numpy(), v.float().cpu().numpy()
+    sn = slots.cpu().numpy()
+    ov = [np.zeros(x.shape, x.cpu().numpy().dtype) for x in views]
+
+    def run():
+        O.kivi_pack_key(kn, sn, ov[0], ov[1], ov[2], g)
+        O.kivi_pack_value(vn, sn, ov[3], ov[4], ov[5], g)
+
+    run()
+    names = ("k_quant", "k_scale", "k_mn", "v_quant", "v_scale", "v_mn")
+    exact = {n: bool(np.array_equal(x.cpu().numpy().view(np.uint32), o.view(np.uint32)))
+             for n, x, o in zip(names, views, ov)}
+    times = []
+    for _ in range(runs):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    info = cpu_info()
+    return {"parity": {"bit_exact": all(exact.values()), "views": exact, "tokens": int(kn.shape[0])},
+            "cpu_baseline": {"value": by / t / 1e9, "unit": "GB/s", "cores": info["cores"], "kind": "port",
+                             "sample": f"the same {kn.shape[0]} tokens (keys and values): 1 warm-up, median of "
+                                       f"{runs} runs", "cpu_model": info["cpu_model"],
+                             "torch_threads": info["torch_threads"]}}
 
 
 def e2e_impl(w, device):
@@ -990,6 +1244,15 @@ def main():
     for _ in range(3):
         step_graph.replay()
     torch.cuda.synchronize(device)
+    # parity of sampled requests against the reference's CPU path (which is
+    # also the timed CPU baseline), before the timed region
+    parity = None
+    if world == 1 and args.check:
+        decode()
+        torch.cuda.synchronize(device)
+        wc = SimpleNamespace(views=w.views, rk=w.rk, rv=w.rv, bt=w.bt, state=w.state, lens=[w.L] * w.B, q=w.q,
+                             g=w.g, blk=w.blk, D=w.D)
+        parity = cpu_check_kivi(wc, out, [0, w.B // 2 + 3], time_runs=5)
     sampler = ClockSampler(local)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with sampler:
@@ -1031,7 +1294,7 @@ def main():
     # grid), then the combine kernel when the plan has several splits
     launches_per_step = 2 if workspace_splits > 0 else 1
 
-    pack = bench_pack(device) if rank == 0 else None
+    pack = bench_pack(device, check=world == 1 and args.check) if rank == 0 else None
     int8 = None
     if not args.no_int8:
         int8 = run_int8_leg(cfg3, rank, world, device, args)
@@ -1061,16 +1324,13 @@ def main():
         achieved = by / (decode_ms * 1e-3) / 1e9
         value = w.B / (ms * 1e-3)
         cpu = None
-        if world == 1 and not args.no_cpu_baseline:
-            run = cpu_reference_sample(cfg)
-            n = 1  # one ~10 s pass of the numpy port
-            t0 = time.perf_counter()
-            for _ in range(n):
-                run()
-            cdt = (time.perf_counter() - t0) / n
-            cpu = {"value": 1.0 / cdt, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
-                   "sample": "one request of the workload (context 32768, 64 q / 8 kv heads), one timed pass; "
-                             "the CPU path is linear in requests"}
+        if parity is not None and "cpu" in parity:
+            c = parity.pop("cpu")
+            cpu = {"value": c["value"], "unit": UNIT, "cores": c["cores"], "kind": "port",
+                   "sample": f"{c['sample']} of the workload (64 q / 8 kv heads): 1 warm-up, median of "
+                             f"{c['runs']} runs; the CPU path is linear in requests",
+                   "seconds_per_request": c["seconds_per_request"], "cpu_model": c["cpu_model"],
+                   "cpu_count": c["cpu_count"], "torch_threads": c["torch_threads"]}
         line = {
             "metric": METRIC,
             "value": value,
@@ -1093,6 +1353,7 @@ def main():
                          "traffic_source": "profiles/kivi_decode_tma_config5.md (ncu, 1 GPU, scaled 1/N)",
                          "peak_source": peak_src,
                          "bytes_per_launch": by, "kernel_ms": decode_ms},
+            "parity": parity,
             "pack": pack,
             "int8_config3": int8,
             "config4": config4,
@@ -1126,6 +1387,11 @@ def run_int8_leg(cfg3, rank, world, device, args):
     def decode8():
         int8_paged_decode(w8.q, w8.kc, w8.vc, w8.k_aq, w8.v_aq, w8.bt_dev, w8.seq_lens, w8.D ** -0.5, out8, w8.L)
 
+    parity = None
+    if world == 1 and rank == 0 and args.check:
+        decode8()
+        torch.cuda.synchronize(device)
+        parity = cpu_check_int8(w8, out8, [0, 37], time_runs=5)
     ms8 = time_loop(decode8, args.steps, args.warmup, device)
     t = torch.tensor([ms8], dtype=torch.float64, device=device)
     if world > 1:
@@ -1139,7 +1405,17 @@ def run_int8_leg(cfg3, rank, world, device, args):
     return {"workload": "BASELINE config 3: INT8 decode, 64 x 8192, Hq 32 / KVH 8, head 128",
             "tokens_per_s_per_layer": cfg3["batch"] / (ms8 * 1e-3), "ms_per_step": ms8,
             "bytes_per_launch": by, "hbm_gbs": gbs, "frac_of_measured_hbm": gbs / peak,
-            "frac_of_8tbs": gbs / 8000.0}
+            "frac_of_8tbs": gbs / 8000.0, "cpu_baseline": _leg_cpu(parity, "port"), "parity": parity}
+
+
+def _leg_cpu(parity, kind):
+    """The CPU-baseline entry of a leg: the timing its parity check made."""
+    if not parity or "cpu" not in parity:
+        return None
+    c = parity.pop("cpu")
+    return {"value": c["value"], "unit": c["unit"], "cores": c["cores"], "kind": kind,
+            "sample": f"{c['sample']}: 1 warm-up, median of {c['runs']} runs", "cpu_model": c["cpu_model"],
+            "torch_threads": c["torch_threads"]}
 
 
 def run_fp8_leg(cfg3, rank, world, device, args):

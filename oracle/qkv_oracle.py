@@ -405,6 +405,63 @@ def dense_attention(q, k, v, q_lens, kv_lens, scale, causal=True):
     return out
 
 
+def kivi_decode_reference(views, block_table, seq_lens, k_windows, v_windows, q, group_size, scale,
+                          target_bf16: bool = True):
+    """One decode query per request through the reference's KIVI read path:
+    ``kivi_dequant_gather_cache`` (ops/kivi_gather.py:36-156) with the cast to
+    the query dtype (bf16; ``target_bf16=False`` keeps the fp32 values), the
+    residual-tail overwrite (methods/kivi_int4/attention_backend.py:889-935),
+    then attention in fp32 (``dense_attention``)."""
+    dk, dv = kivi_dequant_gather(*views, block_table, seq_lens, group_size, target_bf16=target_bf16)
+    dk, dv = overwrite_residual_tail(dk, dv, seq_lens, k_windows, v_windows)
+    return dense_attention(q, dk, dv, [1] * len(seq_lens), seq_lens, scale, causal=True)
+
+
+def int8_decode_reference(key_cache, value_cache, k_aq, v_aq, block_table, seq_lens, q, scale,
+                          target_bf16: bool = True):
+    """One decode query per request through the reference's INT8 dense
+    dequantisation (methods/int8_dynamic/attention_backend.py:370-404, bf16
+    ``code * aq`` unless ``target_bf16=False``), then fp32 attention."""
+    dk, dv = int8_dequant_gather(key_cache, value_cache, k_aq, v_aq, block_table, seq_lens,
+                                 target_bf16=target_bf16)
+    return dense_attention(q, dk, dv, [1] * len(seq_lens), seq_lens, scale, causal=True)
+
+
+# Attention parity bound: max-abs 1e-2 wherever a bf16 output can resolve it.
+# The outputs (the reference's and these kernels') are bf16; for |want| >= 2
+# adjacent bf16 values are more than 1e-2 apart (2^-6 in [2, 4), 2^-5 in
+# [4, 8), ...), so there the bound is one bf16 step of the reference value.
+ATTN_ATOL = 1e-2
+
+
+def bf16_spacing(x) -> np.ndarray:
+    """Distance between adjacent bf16 values around |x|: 2^(e - 7) for |x| in
+    [2^e, 2^(e + 1))."""
+    a = np.abs(np.asarray(x, dtype=np.float64))
+    e = np.floor(np.log2(np.maximum(a, 2.0 ** -126)))
+    return np.exp2(e - 7)
+
+
+def attention_error(got, want, atol: float = ATTN_ATOL) -> dict:
+    """Errors of bf16 attention outputs ``got`` against reference values
+    ``want``: the max-abs error overall and where bf16 resolves ``atol``
+    (|want| < 2), how many outputs lie beyond that resolution, and whether
+    every output is within max(atol, one bf16 step of want)."""
+    got = np.asarray(got, dtype=np.float64)
+    want = np.asarray(want, dtype=np.float64)
+    d = np.abs(got - want)
+    bound = np.maximum(atol, bf16_spacing(want))
+    small = np.abs(want) < 2.0
+    return {
+        "max_abs": float(d.max()) if d.size else 0.0,
+        "max_abs_where_bf16_resolves_1e-2": float(d[small].max()) if small.any() else 0.0,
+        "outputs": int(d.size),
+        "outputs_abs_ge_2": int((~small).sum()),
+        "worst_excess_over_bound": float((d - bound).max()) if d.size else 0.0,
+        "within_bound": bool(np.isfinite(got).all() and (d <= bound).all()),
+    }
+
+
 # ---------------------------------------------------------------------------
 # Residual-window state machine (methods/kivi_int4/attention_backend.py:181-462,
 # :562-674, :813-836; semantics.py:224-283) — pure Python, small cases

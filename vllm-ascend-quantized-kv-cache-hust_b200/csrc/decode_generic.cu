@@ -27,12 +27,16 @@ constexpr int kGenChunk = 128;  // positions per softmax step (one per thread)
 constexpr int kGenMaxG = 16;
 #define kNegInf (-CUDART_INF_F)
 
-// Dequantised values in fp32 (the reference's arithmetic before its final
-// cast to the query dtype, which the tensor-core kernels do not apply either).
+// INT8: the reference's dense dequantisation, code.to(bf16) * aq in bf16
+// (methods/int8_dynamic/attention_backend.py:398-401): the exact product
+// rounded once to bf16, as the page-pipelined INT8 kernel computes it.
 __device__ __forceinline__ float int8_dequant(int8_t code, float aq) {
-  return __fmul_rn(static_cast<float>(code), aq);
+  return __bfloat162float(__float2bfloat16_rn(__fmul_rn(static_cast<float>(code), aq)));
 }
 
+// KIVI: code * scale + min in fp32 (ops/kivi_gather.py), before the
+// reference's cast to the query dtype (the page-pipelined KIVI kernel also
+// uses these values unrounded).
 __device__ __forceinline__ float kivi_dequant(uint32_t code, float scale,
                                               float mn) {
   return __fadd_rn(__fmul_rn(static_cast<float>(code), scale), mn);

@@ -10,14 +10,19 @@
 // Warp w computes tokens [32w, 32w + 32) of every page:
 //     S^T[token][head] = K[token][channel] . Q'^T[channel][head]
 //     O^T[dim][head]  += V^T[dim][token]   . P^T[token][head]
-// with mma.sync m16n8k16 (fp16 x fp16 -> fp32), the query heads of the KV head
-// as N. The antiquant scales are per channel and per head, so
-// Q' = q * k_aq * softmax_scale * log2(e) is built once per CTA in registers
-// and v_aq multiplies the fp32 output once at the end: the dequantised values
-// enter exactly (code * aq in real arithmetic).
+// with mma.sync m16n8k16 (bf16 x bf16 -> fp32), the query heads of the KV head
+// as N. The operands are the reference's dequantised values: its dense
+// dequantisation (methods/int8_dynamic/attention_backend.py:398-401) computes
+// code.to(bf16) * (1 / inv) in bf16, i.e. bf16(code * aq) with one rounding,
+// and that is what enters both MMAs here (i8_bf16_neg: four instructions per
+// pair of codes, the per-channel aq pairs held in registers). The query is
+// the MMA's other operand as is (bf16, exact); softmax_scale * log2(e)
+// multiplies the fp32 scores. P enters the PV MMA as two bf16 operands
+// (hi + lo, ~16 significant bits).
 //
-// int8 -> fp16: one LOP3 ((x & 0x00FF00FF) ^ 0x64806480) turns the signed bytes
-// 0 and 2 of a word into the fp16 pair 1152 + c; one HSUB2 removes 1152 exactly.
+// Both dequantised operands are produced negated (it saves an instruction per
+// pair); the query fragments are negated to match and the output is negated
+// once at the end.
 //
 // Rows of an m-tile: row g (and g + 8) of m-tile i of warp w is page token
 // 32 w + 16 i + perm(g) (+ 8), perm = 0 4 3 7 5 1 6 2. With the TMA's 128-byte
@@ -63,17 +68,6 @@ constexpr size_t kInt8SmemBytes = sizeof(Int8Shared) + 1024;  // + base alignmen
 
 __device__ __forceinline__ int perm8(int g) { return (kPerm8 >> (4 * g)) & 7; }
 
-// int8 bytes 0 and 2 of x -> fp16 pair 1152 + c (one LOP3)
-__device__ __forceinline__ uint32_t i8_pair(uint32_t x) {
-  uint32_t y;
-  asm("lop3.b32 %0, %1, 0x00FF00FF, 0x64806480, 0x6A;\n" : "=r"(y) : "r"(x));
-  return y;
-}
-__device__ __forceinline__ uint32_t hsub2_1152(uint32_t x) {
-  uint32_t y;
-  asm("sub.f16x2 %0, %1, %2;\n" : "=r"(y) : "r"(x), "r"(0x64806480u));
-  return y;
-}
 __device__ __forceinline__ uint32_t lds32(const unsigned char* p) {
   return *reinterpret_cast<const uint32_t*>(p);
 }
@@ -107,25 +101,36 @@ int8_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
   }
 
-  // ---- Q' = q * k_aq * scale * log2(e) for head g, once per CTA. k-step kk
-  // uses word m = 4t + kk (kk < 4) or 16 + 4t + kk - 4 of a key row: channels
-  // 4m (k 2t), 4m + 2 (k 2t+1), 4m + 1 (k 2t+8), 4m + 3 (k 2t+9)
-  uint32_t bq[8][2];
+  // ---- -q for head g and the k_aq pairs of this thread's channels, once per
+  // CTA. k-step kk uses word m = 4t + kk (kk < 4) or 16 + 4t + kk - 4 of a key
+  // row: channels 4m (k 2t), 4m + 2 (k 2t+1), 4m + 1 (k 2t+8), 4m + 3 (k 2t+9)
+  uint32_t bq[8][2], kaq[8][2];
   {
-    const __nv_bfloat16* qrow =
-        p.q + static_cast<int64_t>(b) * p.q_stride + (static_cast<int64_t>(h) * G + g) * kD;
-    const __nv_bfloat16* aq = p.k_aq + static_cast<int64_t>(h) * kD;
+    const uint16_t* qrow = reinterpret_cast<const uint16_t*>(p.q) + static_cast<int64_t>(b) * p.q_stride +
+                           (static_cast<int64_t>(h) * G + g) * kD;
+    const uint16_t* aq = reinterpret_cast<const uint16_t*>(p.k_aq) + static_cast<int64_t>(h) * kD;
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) {
       const int m = kk < 4 ? 4 * t + kk : 16 + 4 * t + kk - 4;
-      float qq[4];
+      uint32_t qq[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int ch = 4 * m + i;
-        qq[i] = g < G ? __bfloat162float(qrow[ch]) * __bfloat162float(aq[ch]) * p.scale_log2 : 0.0f;
-      }
-      bq[kk][0] = pack_half2(qq[0], qq[2]);
-      bq[kk][1] = pack_half2(qq[1], qq[3]);
+      for (int i = 0; i < 4; ++i) qq[i] = g < G ? static_cast<uint32_t>(qrow[4 * m + i]) ^ 0x8000u : 0u;
+      bq[kk][0] = qq[0] | (qq[2] << 16);
+      bq[kk][1] = qq[1] | (qq[3] << 16);
+      kaq[kk][0] = static_cast<uint32_t>(aq[4 * m]) | (static_cast<uint32_t>(aq[4 * m + 2]) << 16);
+      kaq[kk][1] = static_cast<uint32_t>(aq[4 * m + 1]) | (static_cast<uint32_t>(aq[4 * m + 3]) << 16);
+    }
+  }
+  // v_aq of this thread's dims: m-tile (wq, jb) rows g -> dim 4 (g + 8 wq) + 2 jb,
+  // rows g + 8 -> that + 1 (both halves of a pair: the same dim)
+  uint32_t vaq[8][2];
+  {
+    const uint16_t* aq = reinterpret_cast<const uint16_t*>(p.v_aq) + static_cast<int64_t>(h) * kD;
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      const int d_lo = 4 * (g + 8 * (mt >> 1)) + 2 * (mt & 1);
+      vaq[mt][0] = static_cast<uint32_t>(aq[d_lo]) * 0x00010001u;
+      vaq[mt][1] = static_cast<uint32_t>(aq[d_lo + 1]) * 0x00010001u;
     }
   }
   __syncthreads();
@@ -199,9 +204,12 @@ int8_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t x0 = reinterpret_cast<const uint32_t*>(&k0[kk >> 2])[kk & 3];
           const uint32_t x1 = reinterpret_cast<const uint32_t*>(&k1[kk >> 2])[kk & 3];
-          mma16816(sc[j], hsub2_1152(i8_pair(x0)), hsub2_1152(i8_pair(x1)), hsub2_1152(i8_pair(x0 >> 8)),
-                   hsub2_1152(i8_pair(x1 >> 8)), bq[kk][0], bq[kk][1]);
+          mma16816_bf16(sc[j], i8_bf16_neg(x0, kaq[kk][0]), i8_bf16_neg(x1, kaq[kk][0]),
+                        i8_bf16_neg(x0 >> 8, kaq[kk][1]), i8_bf16_neg(x1 >> 8, kaq[kk][1]), bq[kk][0],
+                        bq[kk][1]);
         }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) sc[j][c] *= p.scale_log2;
       }
       if (valid < kTokW) {
 #pragma unroll
@@ -240,7 +248,7 @@ int8_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
           o[mt][3] *= a1;
         }
       }
-      uint32_t pb[2][2];
+      uint32_t pb[2][2], pl[2][2];  // P^T fragments: bf16 hi and lo parts
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         float pr[4];
@@ -248,8 +256,13 @@ int8_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
         for (int c = 0; c < 4; ++c) pr[c] = fast_exp2(sc[j][c] - m_run[c & 1]);
         l_run[0] += pr[0] + pr[2];
         l_run[1] += pr[1] + pr[3];
-        pb[j][0] = movmatrix_t(pack_half2(pr[0], pr[1]));
-        pb[j][1] = movmatrix_t(pack_half2(pr[2], pr[3]));
+        uint32_t h0, l0, h1, l1;
+        split_bf162(pr[0], pr[1], h0, l0);
+        split_bf162(pr[2], pr[3], h1, l1);
+        pb[j][0] = movmatrix_t(h0);
+        pb[j][1] = movmatrix_t(h1);
+        pl[j][0] = movmatrix_t(l0);
+        pl[j][1] = movmatrix_t(l1);
       }
 
       // ---- O'^T += V^T . P^T; k-step j: k (2t, 2t+1) = rows (A, B) of m-tile
@@ -269,8 +282,11 @@ int8_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
                                                        ((4 + 2 * jb) << 8) | ((5 + 2 * jb) << 12));
             const uint32_t xa = __byte_perm(va0, va1, sel);
             const uint32_t xc = __byte_perm(vc0, vc1, sel);
-            mma16816(o[2 * wq + jb], hsub2_1152(i8_pair(xa)), hsub2_1152(i8_pair(xa >> 8)),
-                     hsub2_1152(i8_pair(xc)), hsub2_1152(i8_pair(xc >> 8)), pb[j][0], pb[j][1]);
+            const int mt = 2 * wq + jb;
+            const uint32_t a0 = i8_bf16_neg(xa, vaq[mt][0]), a1 = i8_bf16_neg(xa >> 8, vaq[mt][1]);
+            const uint32_t a2 = i8_bf16_neg(xc, vaq[mt][0]), a3 = i8_bf16_neg(xc >> 8, vaq[mt][1]);
+            mma16816_bf16(o[mt], a0, a1, a2, a3, pb[j][0], pb[j][1]);
+            mma16816_bf16(o[mt], a0, a1, a2, a3, pl[j][0], pl[j][1]);
           }
         }
       }
@@ -289,17 +305,16 @@ int8_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
   float* mo = reinterpret_cast<float*>(&sh.st[0].k[0][0]);  // [warp][head][dim]
   float* mm = mo + kWarps * kHeads * kD;
   float* ml = mm + kWarps * kHeads;
-  const __nv_bfloat16* vaq = p.v_aq + static_cast<int64_t>(h) * kD;
 #pragma unroll
   for (int mt = 0; mt < 8; ++mt) {
     const int wq = mt >> 1, jb = mt & 1;
     const int d_lo = 4 * (g + 8 * wq) + 2 * jb;  // rows g; rows g + 8 -> d_lo + 1
-    const float s_lo = __bfloat162float(vaq[d_lo]), s_hi = __bfloat162float(vaq[d_lo + 1]);
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int head = 2 * t + e;
-      mo[(warp * kHeads + head) * kD + d_lo] = o[mt][e] * s_lo;
-      mo[(warp * kHeads + head) * kD + d_lo + 1] = o[mt][2 + e] * s_hi;
+      // the value operands were negated
+      mo[(warp * kHeads + head) * kD + d_lo] = -o[mt][e];
+      mo[(warp * kHeads + head) * kD + d_lo + 1] = -o[mt][2 + e];
     }
   }
   if (g == 0) {

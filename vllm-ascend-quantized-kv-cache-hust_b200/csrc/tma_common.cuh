@@ -6,6 +6,7 @@
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -101,6 +102,42 @@ __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma16816_bf16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                              uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf162(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+// p = hi + lo with hi = bf16(p) and lo = bf16(p - hi): ~16 significant bits
+// of a probability pair in two bf16 MMA operands.
+__device__ __forceinline__ void split_bf162(float p0, float p1, uint32_t& hi, uint32_t& lo) {
+  hi = pack_bf162(p0, p1);
+  const float h0 = __uint_as_float(hi << 16), h1 = __uint_as_float(hi & 0xFFFF0000u);
+  lo = pack_bf162(p0 - h0, p1 - h1);
+}
+// The INT8 dequantisation of the reference, bf16(code * aq) (one rounding of
+// the exact product, as torch's bf16 multiply of the bf16 code by the bf16
+// antiquant scale), NEGATED, for the signed bytes 0 and 2 of w (bytes 1 and 3
+// are ignored) against the bf16 pair aq2:
+//   x = -(128 + (c & 127))   (0xC300 | low 7 bits: exact bf16)
+//   y = 128 (1 + sign) aq    (aq's bits + 7 in the exponent, + 1 more when the
+//                             code is negative: an integer add on the bits)
+//   fma.rn(x, aq, y) = -(c aq) rounded once to bf16.
+// Four instructions per pair (LOP3, LOP3, IADD3, HFMA2.BF16). Valid for
+// aq < 2^120 (the exponent add stays in range); aq is positive.
+__device__ __forceinline__ uint32_t i8_bf16_neg(uint32_t w, uint32_t aq2) {
+  const uint32_t x = (w & 0x007F007Fu) | 0xC300C300u;
+  const uint32_t y = aq2 + 0x03800380u + (w & 0x00800080u);
+  uint32_t d;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;\n" : "=r"(d) : "r"(x), "r"(aq2), "r"(y));
+  return d;
 }
 // Four 8x8 matrices of 16-bit elements, transposed: lane L names row L & 7 of
 // matrix L >> 3 (16 bytes); lane (g, t) receives in r[m] the elements of rows
