@@ -76,7 +76,7 @@ def parse():
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 chunked-prefill leg")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the request count (small cases for ncu captures)")
-    ap.add_argument("--only", choices=("kivi", "int8", "config4", "fp8", "small"), default=None,
+    ap.add_argument("--only", choices=("kivi", "int8", "config4", "fp8", "small", "pack"), default=None,
                     help="run just one decode kernel loop (for ncu captures)")
     args = ap.parse_args()
     args.check = not args.no_cpu_baseline
@@ -1188,6 +1188,9 @@ def main():
         return
     if args.only == "config4":
         print(json.dumps({"only": "config4", **run_config4_leg(device, args)}), flush=True)
+        return
+    if args.only == "pack":
+        print(json.dumps({"only": "pack", **bench_pack(device, check=args.check)}), flush=True)
         return
     if args.only == "small":
         print(json.dumps({"only": "small", **run_small_configs(device, args)}), flush=True)
