@@ -2,12 +2,14 @@
 // per KV head).
 //
 // One CTA of 4 warps owns (request, kv head, split) and streams the split's
-// pages through a 2-stage shared-memory ring. Thread 0 issues each page with
-// two TMA tensor copies (the page's K and V rows of this head, 128 tokens x
-// 128 B each, written with the 128-byte swizzle) that complete on the stage's
-// "full" mbarrier; every warp arrives on the stage's "empty" mbarrier when it
-// is done with it, and thread 0 waits for that before refilling the stage.
-// Warp w computes tokens [32w, 32w + 32) of every page:
+// pages through a 2-stage shared-memory ring (a ring of 4 half-page stages
+// measured 11 % slower: more ring bookkeeping, one m-tile per warp per
+// stage). Thread 0 issues each page with two TMA tensor copies (the page's K
+// and V rows of this head, 128 tokens x 128 B each, written with the 128-byte
+// swizzle) that complete on the stage's "full" mbarrier; every warp arrives
+// on the stage's "empty" mbarrier when it is done with it, and thread 0
+// waits for that before refilling the stage. Warp w computes tokens
+// [32w, 32w + 32) of every page:
 //     S^T[token][head] = K[token][channel] . Q'^T[channel][head]
 //     O^T[dim][head]  += V^T[dim][token]   . P^T[token][head]
 // with mma.sync m16n8k16 (bf16 x bf16 -> fp32), the query heads of the KV head
@@ -47,19 +49,23 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kD = 128;
 constexpr int kBlk = 128;
 constexpr int kHeads = 8;
-constexpr int kTokW = kBlk / kWarps;
+constexpr int kStageTok = 128;                // tokens per ring stage (one page)
+constexpr int kHalves = kBlk / kStageTok;     // stages per page
+constexpr int kTokW = kStageTok / kWarps;     // tokens per warp per stage
+constexpr int kJ = kTokW / 16;                // score m-tiles per warp per stage
 constexpr int kMaxPages = 64;
 constexpr int kStages = 2;
 constexpr float kLazy = 4.0f;            // log2 headroom of the running max
 constexpr uint32_t kPerm8 = 0x26157340u;  // perm(g) = nibble g
 
-struct __align__(1024) Int8Page {
-  unsigned char k[kBlk][kD];  // 128-byte rows, 128-byte swizzle
-  unsigned char v[kBlk][kD];
+struct __align__(1024) Int8Stage {
+  unsigned char k[kStageTok][kD];  // 128-byte rows, 128-byte swizzle
+  unsigned char v[kStageTok][kD];
 };
+static_assert(kJ >= 1 && kTokW % 16 == 0 && kBlk % kStageTok == 0, "stage geometry");
 
 struct __align__(1024) Int8Shared {
-  Int8Page st[kStages];
+  Int8Stage st[kStages];
   unsigned long long full[kStages];
   unsigned long long empty[kStages];
   int pid[kMaxPages];
@@ -88,6 +94,7 @@ int8_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
   const int t0 = split * p.split_tokens;
   const int t1 = min(L, t0 + p.split_tokens);
   const int n_pages = t1 > t0 ? min((t1 - t0 + kBlk - 1) / kBlk, kMaxPages) : 0;
+  const int n_steps = t1 > t0 ? min((t1 - t0 + kStageTok - 1) / kStageTok, kMaxPages * kHalves) : 0;
 
   for (int i = tid; i < n_pages; i += kThreads)
     sh.pid[i] = static_cast<int>(page_of(p, b, t0 + i * kBlk));
@@ -135,18 +142,20 @@ int8_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
   }
   __syncthreads();
 
-  auto issue = [&](int ii) {  // thread 0
+  auto issue = [&](int ii) {  // thread 0: half page ii of the split
     const int s = ii % kStages;
-    const int pg = sh.pid[ii];
+    const int pg = sh.pid[ii / kHalves];
     if (pg >= 0) {
-      mbar_expect_tx(&sh.full[s], static_cast<uint32_t>(sizeof(Int8Page)));
-      tma_load_3d(&sh.st[s].k[0][0], &tmap_k, 0, h, pg * kBlk, &sh.full[s]);
-      tma_load_3d(&sh.st[s].v[0][0], &tmap_v, 0, h, pg * kBlk, &sh.full[s]);
+      const int row = pg * kBlk + (ii % kHalves) * kStageTok;
+      mbar_expect_tx(&sh.full[s], static_cast<uint32_t>(sizeof(Int8Stage)));
+      tma_load_3d(&sh.st[s].k[0][0], &tmap_k, 0, h, row, &sh.full[s]);
+      tma_load_3d(&sh.st[s].v[0][0], &tmap_v, 0, h, row, &sh.full[s]);
     } else {
       mbar_arrive(&sh.full[s]);
     }
   };
-  if (tid == 0 && n_pages > 0) issue(0);
+  if (tid == 0)
+    for (int ii = 0; ii < kStages - 1 && ii < n_steps; ++ii) issue(ii);
 
   // ---- per-thread swizzled offsets (bytes from the start of a page's rows)
   const int P = perm8(g);
@@ -169,28 +178,29 @@ int8_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
   float l_run[2] = {0.0f, 0.0f};
   bool timed_out = false;
 
-  for (int i = 0; i < n_pages; ++i) {
+  for (int i = 0; i < n_steps; ++i) {
     const int s = i % kStages;
-    if (tid == 0 && i + 1 < n_pages) {
-      // the stage of page i + 1 held page i - 1: all warps must be done with it
-      if (i + 1 >= kStages &&
-          !mbar_wait(&sh.empty[(i + 1) % kStages], static_cast<uint32_t>(((i - 1) / kStages) & 1)))
+    const int nx = i + kStages - 1;
+    if (tid == 0 && nx < n_steps) {
+      // the stage of step nx held step nx - kStages = i - 1: all warps must be done with it
+      if (nx >= kStages &&
+          !mbar_wait(&sh.empty[nx % kStages], static_cast<uint32_t>((nx / kStages - 1) & 1)))
         timed_out = true;
-      issue(i + 1);
+      issue(nx);
     }
     const bool ok = mbar_wait(&sh.full[s], static_cast<uint32_t>((i / kStages) & 1));
     timed_out |= !ok;
-    const int pg = sh.pid[i];
-    const int pos0 = t0 + i * kBlk;
-    const int valid = min(kBlk, t1 - pos0) - kTokW * warp;  // live tokens of this warp
+    const int pg = sh.pid[i / kHalves];
+    const int pos0 = t0 + i * kStageTok;
+    const int valid = min(kStageTok, t1 - pos0) - kTokW * warp;  // live tokens of this warp
     if (ok && pg >= 0 && valid > 0) {
       const unsigned char* kpage = &sh.st[s].k[0][0];
       const unsigned char* vpage = &sh.st[s].v[0][0];
 
-      // ---- scores: m-tile j, rows g / g + 8 -> tokens 32w + 16j + P (+ 8)
-      float sc[2][4];
+      // ---- scores (unscaled): m-tile j, rows g / g + 8 -> tokens 16 (kJ w + j) + P (+ 8)
+      float sc[kJ][4];
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
+      for (int j = 0; j < kJ; ++j) {
         sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
         const unsigned char* r0 = kpage + k_row + 16 * j * kD;
         const unsigned char* r1 = r0 + 8 * kD;
@@ -208,12 +218,10 @@ int8_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
                         i8_bf16_neg(x0 >> 8, kaq[kk][1]), i8_bf16_neg(x1 >> 8, kaq[kk][1]), bq[kk][0],
                         bq[kk][1]);
         }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) sc[j][c] *= p.scale_log2;
       }
       if (valid < kTokW) {
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
+        for (int j = 0; j < kJ; ++j) {
           const bool lo_ok = 16 * j + P < valid, hi_ok = 16 * j + 8 + P < valid;
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
@@ -223,14 +231,18 @@ int8_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
         }
       }
 
-      // ---- online softmax over heads 2t, 2t+1, lazy rescale
+      // ---- online softmax over heads 2t, 2t+1 in log2 units (scores times
+      // softmax_scale * log2 e, folded into the exponent's FMA), lazy rescale
       float mx[2];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        mx[e] = fmaxf(fmaxf(sc[0][e], sc[0][2 + e]), fmaxf(sc[1][e], sc[1][2 + e]));
+        mx[e] = fmaxf(sc[0][e], sc[0][2 + e]);
+#pragma unroll
+        for (int j = 1; j < kJ; ++j) mx[e] = fmaxf(mx[e], fmaxf(sc[j][e], sc[j][2 + e]));
         mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 4));
         mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 8));
         mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 16));
+        mx[e] *= p.scale_log2;
       }
       const bool grow0 = mx[0] > m_run[0] + kLazy, grow1 = mx[1] > m_run[1] + kLazy;
       if (__any_sync(0xffffffffu, grow0 || grow1)) {
@@ -248,12 +260,12 @@ int8_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
           o[mt][3] *= a1;
         }
       }
-      uint32_t pb[2][2], pl[2][2];  // P^T fragments: bf16 hi and lo parts
+      uint32_t pb[kJ][2], pl[kJ][2];  // P^T fragments: bf16 hi and lo parts
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
+      for (int j = 0; j < kJ; ++j) {
         float pr[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) pr[c] = fast_exp2(sc[j][c] - m_run[c & 1]);
+        for (int c = 0; c < 4; ++c) pr[c] = fast_exp2(fmaf(sc[j][c], p.scale_log2, -m_run[c & 1]));
         l_run[0] += pr[0] + pr[2];
         l_run[1] += pr[1] + pr[3];
         uint32_t h0, l0, h1, l1;
@@ -269,7 +281,7 @@ int8_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
       // j, (2t+8, 2t+9) their + 8; dim m-tile (wq, jb): rows g -> byte 2 jb of
       // word g + 8 wq, rows g + 8 -> byte 2 jb + 1
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
+      for (int j = 0; j < kJ; ++j) {
         const unsigned char* ra = vpage + v_rowA + 16 * j * kD;
         const unsigned char* rb = vpage + v_rowB + 16 * j * kD;
 #pragma unroll
@@ -346,19 +358,19 @@ int8_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
   }
 }
 
-static_assert(sizeof(Int8Page) * kStages >=
+static_assert(sizeof(Int8Stage) * kStages >=
                   sizeof(float) * (kWarps * kHeads * kD + 2 * kWarps * kHeads),
               "merge buffers must fit in the stage memory");
 
 // INT8 pages [NB, block, KVH, D] as a 3-D map {D bytes, KVH, NB * block} with
-// the 128-byte swizzle; one box = the 128 token rows of one head of one page.
+// the 128-byte swizzle; one box = the token rows of one ring stage of one head.
 int encode_int8_map(const int8_t* base, const DecodeParams& p, CUtensorMap* map) {
   auto enc = encode_fn();
   if (enc == nullptr) return set_error(QKV_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(p.kvh),
                               static_cast<cuuint64_t>(p.num_blocks) * kBlk};
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(kD) * p.kvh};
-  const cuuint32_t box[3] = {kD, 1, kBlk};
+  const cuuint32_t box[3] = {kD, 1, kStageTok};
   const cuuint32_t es[3] = {1, 1, 1};
   const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(base), dims, strides,
                          box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
