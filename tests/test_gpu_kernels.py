@@ -213,6 +213,47 @@ def test_kivi_pack_bit_exact_config2_scale(group):
     assert_no_device_error()
 
 
+@pytest.mark.parametrize("group", [64, 128])
+def test_kivi_pack_bit_exact_at_rounding_ties(group):
+    """bf16 inputs whose (x - mn) / scale lies on or next to a rounding tie
+    k + 0.5 (the inputs the pack kernels decide by the exact division
+    sequence), plus constant and scale-floor groups, keys and values."""
+    from qkv_b200.ops import kivi_pack_key_cache, kivi_pack_value_cache
+
+    rng = np.random.default_rng(100 + group)
+    H, D, blk, pages = 8, 128, 128, 4
+    T = pages * blk
+    steps = np.array([0.25, 1.0 / 3.0, 0.1, 0.7, 2.0 ** -7, 3.0, 1e-7], np.float32)
+    key = np.zeros((T, H, D), np.float32)
+    value = np.zeros((T, H, D), np.float32)
+    for h in range(H):
+        st = steps[h % len(steps)]
+        # group ends 0 and 15 st; the rest at (k + 0.5) st and its bf16 neighbours
+        base = (rng.integers(0, 15, (T, D)) + 0.5) * st + rng.integers(-2, 3, (T, D)) * st * 2.0 ** -9
+        key[:, h] = base
+        value[:, h] = base
+    key = O.bf16_round(key)
+    value = O.bf16_round(value)
+    for t0 in range(0, T, group):  # key groups: exact ends
+        key[t0, :, :] = 0.0
+        key[t0 + 1, :, :] = O.bf16_round(15 * steps[np.arange(H) % len(steps)])[:, None]
+    value[:, :, 0::group] = 0.0
+    value[:, :, 1::group] = O.bf16_round(15 * steps[np.arange(H) % len(steps)])[None, :, None]
+    key[: group, 3, :] = 0.5  # constant group: scale floor
+    nb = pages + 2
+    page_ids = rng.permutation(nb)[:pages]
+    slots = (page_ids[np.arange(T) // blk] * blk + np.arange(T) % blk).astype(np.int64)
+    views = _empty_views(nb, blk, H, D, group)
+    kivi_pack_key_cache(bf16_tensor(key), torch.from_numpy(slots).to(dev()), *views[:3], group)
+    kivi_pack_value_cache(bf16_tensor(value), torch.from_numpy(slots).to(dev()), *views[3:], group)
+    ov = [v.cpu().numpy().copy() for v in _empty_views(nb, blk, H, D, group)]
+    O.kivi_pack_key(key, slots, ov[0], ov[1], ov[2], group)
+    O.kivi_pack_value(value, slots, ov[3], ov[4], ov[5], group)
+    for v, o, n in zip(views, ov, ("k_quant", "k_scale", "k_mn", "v_quant", "v_scale", "v_mn")):
+        assert np.array_equal(v.cpu().numpy().view(np.uint32), o.view(np.uint32)), n
+    assert_no_device_error()
+
+
 def test_kivi_pack_value_skips_padding_and_rejects_misaligned_keys():
     from qkv_b200.ops import kivi_pack_key_cache, kivi_pack_value_cache
 

@@ -9,6 +9,8 @@
 //   word  = OR_L (code_L & 0xF) << 4L                 lane L at bits 4L
 // Every operation is written with explicit round-to-nearest intrinsics so the
 // compiler cannot contract or reassociate it.
+#include <type_traits>
+
 #include "qkv_common.cuh"
 
 namespace qkv {
@@ -322,6 +324,261 @@ pack_key_tiled_kernel(const T* __restrict__ key, const void* __restrict__ slots,
   }
 }
 
+// ------------------------------------------------ fast path (bf16, head 128)
+//
+// The same codes, scales and minima as the kernels above, without an IEEE
+// division per element. For a group with minimum mn and scale s (computed
+// exactly as above) and inv = 1/s (correctly rounded), each element takes
+//   d  = x - mn                  (fp32, as the reference)
+//   r  = RN(d * inv + 1.5 2^23)  (= 1.5 2^23 + round(d * inv): the integer k
+//                                 sits in the low mantissa bits of r)
+//   e  = RN(d * inv - k)         (the distance of d * inv to that integer)
+// and k is the reference's clamp(floor(RN(RN(d / s) + 0.5)), 0, 15) whenever
+// |e| < 0.5 - 2^-12: d * inv is within 16 * 2^-23 of d / s (two roundings
+// of relative size 2^-24, d / s <= 15 (1 + 2^-22)), RN(d / s) and the + 0.5
+// move it by at most 2^-20 each, so the reference's floor argument lies in
+// (k, k + 1) and floor gives k; k lies in [0, 15] because 0 <= d <= mx - mn.
+// A word (8 codes) with any element outside that band (a value within 2^-12
+// of a rounding tie, or a non-finite input: NaN fails every comparison) is
+// recomputed with the division sequence above. The fp32 pairs run as packed
+// f32x2 instructions (two lanes per instruction, Blackwell).
+namespace fastq {
+
+using u64 = unsigned long long;
+constexpr float kMagic = 12582912.0f;              // 1.5 * 2^23
+constexpr float kTie2 = (0.5f - 1.0f / 4096.0f) * (0.5f - 1.0f / 4096.0f);
+
+__device__ __forceinline__ u64 pack2(float a, float b) {
+  u64 r;
+  asm("mov.b64 %0, {%1, %2};\n" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void unpack2(u64 r, uint32_t& a, uint32_t& b) {
+  asm("mov.b64 {%0, %1}, %2;\n" : "=r"(a), "=r"(b) : "l"(r));
+}
+__device__ __forceinline__ u64 sub2(u64 a, u64 b) {
+  u64 r;
+  asm("sub.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ u64 fma2(u64 a, u64 b, u64 c) {
+  u64 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;\n" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint32_t bmin2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("min.bf16x2 %0, %1, %2;\n" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bmax2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.bf16x2 %0, %1, %2;\n" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+// Codes of the two bf16 values of w against per-lane (mn, inv): returned in
+// the low byte of r0 / r1; `ok` keeps its sign bit only while every element
+// so far lies inside the exact band.
+__device__ __forceinline__ void quant2(uint32_t w, u64 mn2, u64 inv2, uint32_t& r0, uint32_t& r1, uint32_t& ok) {
+  const u64 m2 = pack2(kMagic, kMagic);
+  const u64 t2 = pack2(-kTie2, -kTie2);
+  const u64 d = sub2(pack2(bf_lo(w), bf_hi(w)), mn2);
+  const u64 r = fma2(d, inv2, m2);
+  const u64 e = fma2(d, inv2, sub2(m2, r));  // d * inv - k
+  uint32_t c0, c1;
+  unpack2(fma2(e, e, t2), c0, c1);           // e^2 - band^2: negative inside
+  unpack2(r, r0, r1);
+  ok &= c0 & c1;
+}
+
+// 8 codes (low bytes of c[0..7], each < 16) -> one int4 word, lane L at bits 4L.
+__device__ __forceinline__ uint32_t pack8(const uint32_t (&c)[8]) {
+  const uint32_t e = __byte_perm(__byte_perm(c[0], c[2], 0x0040), __byte_perm(c[4], c[6], 0x0040), 0x5410);
+  const uint32_t o = __byte_perm(__byte_perm(c[1], c[3], 0x0040), __byte_perm(c[5], c[7], 0x0040), 0x5410);
+  return e | (o << 4);
+}
+
+}  // namespace fastq
+
+// Keys: one CTA of 256 threads per (token group, head). Thread (warp w, lane)
+// owns the channel pair cp = 32 (w & 1) + lane and the token quarter
+// tc = w >> 1 of the group: it loads the pair for its G / 4 tokens (a warp's
+// loads are 128 contiguous bytes of a token row), reduces min / max in bf16
+// pairs (exact), the four quarters meet in shared memory, and each thread
+// quantises and stores its own G / 32 words per channel.
+template <int G>
+__global__ void __launch_bounds__(256)
+pack_key_fast_kernel(const __nv_bfloat16* __restrict__ key, const void* __restrict__ slots, int slot_dtype,
+                     int kvh, int block_size, int64_t num_blocks, int32_t* __restrict__ k_quant,
+                     float* __restrict__ k_scale, float* __restrict__ k_mn, int* err) {
+  using namespace fastq;
+  constexpr int kD = 128, kTok = G / 4, kWords = kTok / 8;
+  __shared__ uint32_t s_mn[4][64], s_mx[4][64];
+  const int head = blockIdx.y;
+  const int64_t gi = blockIdx.x;
+  const int64_t first_slot = load_index(slots, slot_dtype, gi * G);
+  if (first_slot < 0) return;  // the reference kernel skips such groups
+  const int64_t blk = first_slot / block_size;
+  const int off = static_cast<int>(first_slot - blk * block_size);
+  if (blk >= num_blocks || (off % G) != 0 || off + G > block_size) {
+    if (threadIdx.x == 0) record_error(err, kErrSlot);
+    return;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cp = 32 * (warp & 1) + lane, tc = warp >> 1;
+  const int64_t row_words = static_cast<int64_t>(kvh) * (kD / 2);
+  const uint32_t* src =
+      reinterpret_cast<const uint32_t*>(key) + (gi * G + tc * kTok) * row_words + head * (kD / 2) + cp;
+  uint32_t v[kTok];
+#pragma unroll
+  for (int i = 0; i < kTok; ++i) v[i] = __ldg(src + i * row_words);
+  uint32_t mn = v[0], mx = v[0];
+#pragma unroll
+  for (int i = 1; i < kTok; ++i) {
+    mn = bmin2(mn, v[i]);
+    mx = bmax2(mx, v[i]);
+  }
+  s_mn[tc][cp] = mn;
+  s_mx[tc][cp] = mx;
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    mn = bmin2(mn, s_mn[j][cp]);
+    mx = bmax2(mx, s_mx[j][cp]);
+  }
+  const float mn0 = bf_lo(mn), mn1 = bf_hi(mn);
+  const float sc0 = group_scale(mn0, bf_lo(mx)), sc1 = group_scale(mn1, bf_hi(mx));
+  const u64 mn2 = pack2(mn0, mn1), inv2 = pack2(__frcp_rn(sc0), __frcp_rn(sc1));
+  uint32_t w0[kWords], w1[kWords];
+#pragma unroll
+  for (int j = 0; j < kWords; ++j) {
+    uint32_t c0[8], c1[8], ok = 0xFFFFFFFFu;
+#pragma unroll
+    for (int l = 0; l < 8; ++l) quant2(v[8 * j + l], mn2, inv2, c0[l], c1[l], ok);
+    w0[j] = pack8(c0);
+    w1[j] = pack8(c1);
+    if ((ok >> 31) == 0) {  // an element near a tie: the exact sequence
+      w0[j] = w1[j] = 0;
+#pragma unroll
+      for (int l = 0; l < 8; ++l) {
+        w0[j] |= quantize_code(bf_lo(v[8 * j + l]), mn0, sc0) << (4 * l);
+        w1[j] |= quantize_code(bf_hi(v[8 * j + l]), mn1, sc1) << (4 * l);
+      }
+    }
+  }
+  const int64_t chan0 = (blk * kvh + head) * static_cast<int64_t>(kD) + 2 * cp;
+  const int64_t wpc = block_size >> 3;  // words per channel and page
+  int32_t* dst0 = k_quant + chan0 * wpc + (off >> 3) + tc * kWords;
+  int32_t* dst1 = dst0 + wpc;
+  if constexpr (kWords == 4) {
+    *reinterpret_cast<uint4*>(dst0) = make_uint4(w0[0], w0[1], w0[2], w0[3]);
+    *reinterpret_cast<uint4*>(dst1) = make_uint4(w1[0], w1[1], w1[2], w1[3]);
+  } else {
+    *reinterpret_cast<uint2*>(dst0) = make_uint2(w0[0], w0[1]);
+    *reinterpret_cast<uint2*>(dst1) = make_uint2(w1[0], w1[1]);
+  }
+  if (tc == 0) {
+    const int gpb = block_size / G;
+    const int64_t s0 = chan0 * gpb + off / G;
+    k_scale[s0] = sc0;
+    k_mn[s0] = mn0;
+    k_scale[s0 + gpb] = sc1;
+    k_mn[s0 + gpb] = mn1;
+  }
+}
+
+// Values: 8 threads per (token, head) row of 128 dims, 16 dims (two 16-byte
+// loads) each; a group of G dims is G / 16 threads, reduced with shuffles.
+// Each thread stores its two words (8 bytes; a row's 64 bytes contiguous).
+template <int G>
+__global__ void __launch_bounds__(256)
+pack_value_fast_kernel(const __nv_bfloat16* __restrict__ value, const void* __restrict__ slots, int slot_dtype,
+                       int64_t num_tokens, int kvh, int64_t num_slots, int32_t* __restrict__ v_quant,
+                       float* __restrict__ v_scale, float* __restrict__ v_mn, int* err,
+                       RowSource<__nv_bfloat16> rs) {
+  using namespace fastq;
+  constexpr int kD = 128, kTpg = G / 16;  // threads per group
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t row = tid >> 3;  // token * kvh + head
+  const int part = static_cast<int>(tid & 7);
+  const bool in_range = row < num_tokens * kvh;
+  const int64_t token = in_range ? row / kvh : 0;
+  const int head = in_range ? static_cast<int>(row % kvh) : 0;
+  int64_t slot = -1;
+  if (in_range) slot = load_index(slots, slot_dtype, token);
+  bool valid = in_range && slot >= 0;
+  if (valid && slot >= num_slots) {
+    record_error(err, kErrSlot);
+    valid = false;
+  }
+  const __nv_bfloat16* rowp = in_range ? value + row * kD : nullptr;
+  if (rs.src != nullptr && in_range) {
+    const int64_t sidx = rs.src[token];
+    const int64_t tok_row = static_cast<int64_t>(kvh) * kD;
+    if (sidx >= 0 && sidx < rs.ring_lanes) {
+      rowp = rs.ring + sidx * tok_row + static_cast<int64_t>(head) * kD;
+    } else if (sidx < 0 && -1 - sidx < rs.n_new) {
+      rowp = rs.fresh + (-1 - sidx) * tok_row + static_cast<int64_t>(head) * kD;
+    } else {
+      if (part == 0) record_error(err, kErrWindowSource);
+      valid = false;
+      rowp = nullptr;
+    }
+  }
+  uint32_t v[8];
+  if (rowp != nullptr) {
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(rowp) + 2 * part);
+    const uint4 b = __ldg(reinterpret_cast<const uint4*>(rowp) + 2 * part + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0u;
+  }
+  uint32_t mnp = v[0], mxp = v[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) {
+    mnp = bmin2(mnp, v[i]);
+    mxp = bmax2(mxp, v[i]);
+  }
+  float mn = fminf(bf_lo(mnp), bf_hi(mnp)), mx = fmaxf(bf_lo(mxp), bf_hi(mxp));
+#pragma unroll
+  for (int o = 1; o < kTpg; o <<= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  if (!valid) return;
+  const float sc = group_scale(mn, mx);
+  const float inv = __frcp_rn(sc);
+  const u64 mn2 = pack2(mn, mn), inv2 = pack2(inv, inv);
+  uint32_t w[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    uint32_t c[8], ok = 0xFFFFFFFFu;
+#pragma unroll
+    for (int l = 0; l < 4; ++l) quant2(v[4 * j + l], mn2, inv2, c[2 * l], c[2 * l + 1], ok);
+    w[j] = pack8(c);
+    if ((ok >> 31) == 0) {
+      w[j] = 0;
+#pragma unroll
+      for (int l = 0; l < 4; ++l) {
+        w[j] |= quantize_code(bf_lo(v[4 * j + l]), mn, sc) << (8 * l);
+        w[j] |= quantize_code(bf_hi(v[4 * j + l]), mn, sc) << (8 * l + 4);
+      }
+    }
+  }
+  const int64_t dst_row = slot * kvh + head;
+  *reinterpret_cast<uint2*>(v_quant + dst_row * (kD / 8) + 2 * part) = make_uint2(w[0], w[1]);
+  if (part % kTpg == 0) {
+    const int64_t s = dst_row * (kD / G) + part / kTpg;
+    v_scale[s] = sc;
+    v_mn[s] = mn;
+  }
+}
+
 template <typename T>
 int launch_pack_key(const void* key, const void* slots, int slot_dtype,
                     int64_t num_tokens, int kvh, int head_size, int group_size,
@@ -333,6 +590,22 @@ int launch_pack_key(const void* key, const void* slots, int slot_dtype,
   const int64_t grid = (threads + block - 1) / block;
   const T* k = static_cast<const T*>(key);
   int* err = device_error_ptr();
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    // bf16 at head 128, group 64 / 128: the division-free kernel
+    const uintptr_t qa = reinterpret_cast<uintptr_t>(kq);
+    if (head_size == 128 && (group_size == 64 || group_size == 128) &&
+        (reinterpret_cast<uintptr_t>(key) & 3u) == 0 && (qa & (group_size == 128 ? 15u : 7u)) == 0) {
+      dim3 fgrid(static_cast<unsigned>(groups), kvh);
+      if (group_size == 128)
+        pack_key_fast_kernel<128><<<fgrid, 256, 0, stream>>>(k, slots, slot_dtype, kvh, block_size, num_blocks,
+                                                             kq, ks, km, err);
+      else
+        pack_key_fast_kernel<64><<<fgrid, 256, 0, stream>>>(k, slots, slot_dtype, kvh, block_size, num_blocks,
+                                                            kq, ks, km, err);
+      QKV_CHECK_LAUNCH("pack_key_fast_kernel");
+      return QKV_OK;
+    }
+  }
   // 16-byte stores need a 16-byte aligned k_quant base and rows of whole
   // 16-byte units; group offsets are multiples of g/8 words (a multiple of 4
   // whenever the vector path is taken)
@@ -386,6 +659,25 @@ int launch_pack_key(const void* key, const void* slots, int slot_dtype,
   return QKV_OK;
 }
 
+// The division-free value kernel for bf16 rows at head 128, group 64 / 128
+// (rows 16-byte aligned, v_quant 8-byte aligned); false when it does not apply.
+bool launch_pack_value_fast(const __nv_bfloat16* v, const void* slots, int slot_dtype, int64_t num_tokens, int kvh,
+                            int head_size, int group_size, int64_t num_slots, int32_t* vq, float* vs, float* vm,
+                            RowSource<__nv_bfloat16> rs, cudaStream_t stream) {
+  const auto al = [](const void* p, unsigned m) { return (reinterpret_cast<uintptr_t>(p) & m) == 0; };
+  if (head_size != 128 || (group_size != 64 && group_size != 128) || !al(vq, 7u)) return false;
+  if (rs.src == nullptr ? !al(v, 15u) : (!al(rs.ring, 15u) || !al(rs.fresh, 15u))) return false;
+  const int64_t threads = num_tokens * kvh * 8;
+  const unsigned grid = static_cast<unsigned>((threads + 255) / 256);
+  if (group_size == 128)
+    pack_value_fast_kernel<128><<<grid, 256, 0, stream>>>(v, slots, slot_dtype, num_tokens, kvh, num_slots, vq, vs,
+                                                          vm, device_error_ptr(), rs);
+  else
+    pack_value_fast_kernel<64><<<grid, 256, 0, stream>>>(v, slots, slot_dtype, num_tokens, kvh, num_slots, vq, vs,
+                                                         vm, device_error_ptr(), rs);
+  return true;
+}
+
 template <typename T>
 int launch_pack_value(const void* value, const void* slots, int slot_dtype,
                       int64_t num_tokens, int kvh, int head_size, int group_size,
@@ -395,6 +687,13 @@ int launch_pack_value(const void* value, const void* slots, int slot_dtype,
   const int64_t num_slots = num_blocks * block_size;
   const T* v = static_cast<const T*>(value);
   int* err = device_error_ptr();
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    if (launch_pack_value_fast(v, slots, slot_dtype, num_tokens, kvh, head_size, group_size, num_slots, vq, vs,
+                               vm, RowSource<__nv_bfloat16>{nullptr, nullptr, nullptr, 0, 0}, stream)) {
+      QKV_CHECK_LAUNCH("pack_value_fast_kernel");
+      return QKV_OK;
+    }
+  }
   const bool pow2 = (words & (words - 1)) == 0 && words <= 32;
   // the vector path loads 8 elements (16 or 32 bytes) per thread
   const bool aligned = (reinterpret_cast<uintptr_t>(value) & 15u) == 0;
@@ -450,6 +749,12 @@ int pack_value_from_sources(const __nv_bfloat16* ring, int64_t ring_lanes, const
   const int words = head_size / 8;
   QKV_CHECK_ARG((words & (words - 1)) == 0 && words <= 32 && head_size % group_size == 0 && src && slots,
                 "pack_value_from_sources: unsupported geometry");
+  if (launch_pack_value_fast(nullptr, slots, QKV_I64, num_tokens, kvh, head_size, group_size,
+                             num_blocks * block_size, vq, vs, vm,
+                             RowSource<__nv_bfloat16>{src, ring, fresh, ring_lanes, n_new}, stream)) {
+    QKV_CHECK_LAUNCH("pack_value_fast_kernel");
+    return QKV_OK;
+  }
   const int64_t threads = num_tokens * kvh * words;
   const int block = 256;
   pack_value_kernel<__nv_bfloat16><<<(threads + block - 1) / block, block, 0, stream>>>(
