@@ -164,6 +164,24 @@ QKV_API int qkv_kivi_pack_value(const void* value, int value_dtype,
                         int32_t* v_quant, float* v_scale, float* v_mn,
                         qkv_stream_t stream);
 
+/* Pack keys and values of the SAME tokens in one launch: the results of
+ * qkv_kivi_pack_key followed by qkv_kivi_pack_value on (key, slot_mapping)
+ * and (value, slot_mapping). Replaces the pair of launches the reference
+ * makes when a bulk prompt write flushes floor(n / r) * r tokens of both sides
+ * to the int4 history (methods/kivi_int4/attention_backend.py:608-674 ->
+ * kivi_pack_key_cache + kivi_pack_value_cache, ops/triton/kivi_pack.py:229-348).
+ * Keys need whole groups (num_tokens % group_size == 0, every slot valid and
+ * each group contiguous and aligned inside one block, as for
+ * qkv_kivi_pack_key). bf16 at head_size 128, group 64 / 128 runs one fused
+ * kernel; other geometries run the two packs back to back. */
+QKV_API int qkv_kivi_pack_kv(const void* key, const void* value, int dtype,
+                             const void* slot_mapping, int slot_dtype,
+                             int64_t num_tokens, int num_kv_heads, int head_size,
+                             int group_size, int block_size, int64_t num_blocks,
+                             int32_t* k_quant, float* k_scale, float* k_mn,
+                             int32_t* v_quant, float* v_scale, float* v_mn,
+                             qkv_stream_t stream);
+
 /* Bytes of workspace qkv_kivi_paged_decode needs for this batch shape. */
 QKV_API size_t qkv_kivi_paged_decode_workspace(int batch, int num_heads,
                                        int num_kv_heads, int head_size,

@@ -254,6 +254,30 @@ def test_kivi_pack_bit_exact_at_rounding_ties(group):
     assert_no_device_error()
 
 
+@pytest.mark.parametrize("group,dtype", [(128, torch.bfloat16), (64, torch.bfloat16), (128, torch.float32)])
+def test_kivi_pack_kv_equals_the_two_packs(group, dtype):
+    """qkv_kivi_pack_kv (one launch for both sides; the fused kernel for bf16,
+    the two packs back to back otherwise) writes what qkv_kivi_pack_key and
+    qkv_kivi_pack_value write on the same tokens, bit for bit."""
+    from qkv_b200.ops import kivi_pack_key_cache, kivi_pack_kv_cache, kivi_pack_value_cache
+
+    rng = np.random.default_rng(group + 7)
+    H, D, blk, pages = 8, 128, 128, 9
+    T = pages * blk
+    key = torch.from_numpy(kv_data(rng, T, H, D, 0.02, 10.0)).to(dev()).to(dtype)
+    value = torch.from_numpy(kv_data(rng, T, H, D, 0.0, 1.0)).to(dev()).to(dtype)
+    nb = pages + 5
+    page_ids = rng.permutation(nb)[:pages]
+    slots = torch.from_numpy((page_ids[np.arange(T) // blk] * blk + np.arange(T) % blk).astype(np.int64)).to(dev())
+    a, b = _empty_views(nb, blk, H, D, group, 3.0), _empty_views(nb, blk, H, D, group, 3.0)
+    kivi_pack_kv_cache(key, value, slots, a[:3], a[3:], group)
+    kivi_pack_key_cache(key, slots, *b[:3], group)
+    kivi_pack_value_cache(value, slots, *b[3:], group)
+    for x, y in zip(a, b):
+        assert torch.equal(x.view(torch.int32), y.view(torch.int32))
+    assert_no_device_error()
+
+
 def test_kivi_pack_value_skips_padding_and_rejects_misaligned_keys():
     from qkv_b200.ops import kivi_pack_key_cache, kivi_pack_value_cache
 

@@ -334,19 +334,22 @@ pack_key_tiled_kernel(const T* __restrict__ key, const void* __restrict__ slots,
 //                                 sits in the low mantissa bits of r)
 //   e  = RN(d * inv - k)         (the distance of d * inv to that integer)
 // and k is the reference's clamp(floor(RN(RN(d / s) + 0.5)), 0, 15) whenever
-// |e| < 0.5 - 2^-12: d * inv is within 16 * 2^-23 of d / s (two roundings
-// of relative size 2^-24, d / s <= 15 (1 + 2^-22)), RN(d / s) and the + 0.5
-// move it by at most 2^-20 each, so the reference's floor argument lies in
-// (k, k + 1) and floor gives k; k lies in [0, 15] because 0 <= d <= mx - mn.
-// A word (8 codes) with any element outside that band (a value within 2^-12
-// of a rounding tie, or a non-finite input: NaN fails every comparison) is
-// recomputed with the division sequence above. The fp32 pairs run as packed
-// f32x2 instructions (two lanes per instruction, Blackwell).
+// |e| < 0.5 - 2^-16. The bound: with Q = d / s (real), d * inv = Q (1 + a),
+// |a| <= 2^-24 and Q <= 15 (1 + 2^-22), so |d * inv - Q| < 2^-20;
+// |RN(Q) - Q| <= 2^-21 and the + 0.5 rounds by at most 2^-20 (below 16), so
+// the reference's floor argument lies within 2.5 * 2^-20 < 2^-18.6 of
+// d * inv + 0.5, and e itself is within 2^-25 of d * inv - k: inside the band
+// that argument lies in (k, k + 1) and floor gives k. k lies in [0, 15]
+// because 0 <= d <= mx - mn. A word (8 codes) with any element outside the
+// band (within 2^-16 of a rounding tie, about 3e-5 of random inputs, or a
+// non-finite input: NaN fails every comparison) is recomputed with the
+// division sequence above. The fp32 pairs run as packed f32x2 instructions
+// (two lanes per instruction, Blackwell).
 namespace fastq {
 
 using u64 = unsigned long long;
 constexpr float kMagic = 12582912.0f;              // 1.5 * 2^23
-constexpr float kTie2 = (0.5f - 1.0f / 4096.0f) * (0.5f - 1.0f / 4096.0f);
+constexpr float kTie2 = (0.5f - 1.0f / 65536.0f) * (0.5f - 1.0f / 65536.0f);
 
 __device__ __forceinline__ u64 pack2(float a, float b) {
   u64 r;
@@ -410,15 +413,14 @@ __device__ __forceinline__ uint32_t pack8(const uint32_t (&c)[8]) {
 // pairs (exact), the four quarters meet in shared memory, and each thread
 // quantises and stores its own G / 32 words per channel.
 template <int G>
-__global__ void __launch_bounds__(256)
-pack_key_fast_kernel(const __nv_bfloat16* __restrict__ key, const void* __restrict__ slots, int slot_dtype,
-                     int kvh, int block_size, int64_t num_blocks, int32_t* __restrict__ k_quant,
-                     float* __restrict__ k_scale, float* __restrict__ k_mn, int* err) {
+__device__ __forceinline__ void pack_key_fast_tile(const __nv_bfloat16* __restrict__ key,
+                                                   const void* __restrict__ slots, int slot_dtype, int kvh,
+                                                   int block_size, int64_t num_blocks, int32_t* __restrict__ k_quant,
+                                                   float* __restrict__ k_scale, float* __restrict__ k_mn, int* err,
+                                                   int64_t gi, int head) {
   using namespace fastq;
   constexpr int kD = 128, kTok = G / 4, kWords = kTok / 8;
   __shared__ uint32_t s_mn[4][64], s_mx[4][64];
-  const int head = blockIdx.y;
-  const int64_t gi = blockIdx.x;
   const int64_t first_slot = load_index(slots, slot_dtype, gi * G);
   if (first_slot < 0) return;  // the reference kernel skips such groups
   const int64_t blk = first_slot / block_size;
@@ -490,18 +492,28 @@ pack_key_fast_kernel(const __nv_bfloat16* __restrict__ key, const void* __restri
   }
 }
 
+template <int G>
+__global__ void __launch_bounds__(256)
+pack_key_fast_kernel(const __nv_bfloat16* __restrict__ key, const void* __restrict__ slots, int slot_dtype,
+                     int kvh, int block_size, int64_t num_blocks, int32_t* __restrict__ k_quant,
+                     float* __restrict__ k_scale, float* __restrict__ k_mn, int* err) {
+  pack_key_fast_tile<G>(key, slots, slot_dtype, kvh, block_size, num_blocks, k_quant, k_scale, k_mn, err,
+                        blockIdx.x, blockIdx.y);
+}
+
 // Values: 8 threads per (token, head) row of 128 dims, 16 dims (two 16-byte
 // loads) each; a group of G dims is G / 16 threads, reduced with shuffles.
 // Each thread stores its two words (8 bytes; a row's 64 bytes contiguous).
 template <int G>
-__global__ void __launch_bounds__(256)
-pack_value_fast_kernel(const __nv_bfloat16* __restrict__ value, const void* __restrict__ slots, int slot_dtype,
-                       int64_t num_tokens, int kvh, int64_t num_slots, int32_t* __restrict__ v_quant,
-                       float* __restrict__ v_scale, float* __restrict__ v_mn, int* err,
-                       RowSource<__nv_bfloat16> rs) {
+__device__ __forceinline__ void pack_value_fast_rows(const __nv_bfloat16* __restrict__ value,
+                                                     const void* __restrict__ slots, int slot_dtype,
+                                                     int64_t num_tokens, int kvh, int64_t num_slots,
+                                                     int32_t* __restrict__ v_quant, float* __restrict__ v_scale,
+                                                     float* __restrict__ v_mn, int* err,
+                                                     const RowSource<__nv_bfloat16>& rs, int64_t block) {
   using namespace fastq;
   constexpr int kD = 128, kTpg = G / 16;  // threads per group
-  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t tid = block * blockDim.x + threadIdx.x;
   const int64_t row = tid >> 3;  // token * kvh + head
   const int part = static_cast<int>(tid & 7);
   const bool in_range = row < num_tokens * kvh;
@@ -577,6 +589,35 @@ pack_value_fast_kernel(const __nv_bfloat16* __restrict__ value, const void* __re
     v_scale[s] = sc;
     v_mn[s] = mn;
   }
+}
+
+template <int G>
+__global__ void __launch_bounds__(256)
+pack_value_fast_kernel(const __nv_bfloat16* __restrict__ value, const void* __restrict__ slots, int slot_dtype,
+                       int64_t num_tokens, int kvh, int64_t num_slots, int32_t* __restrict__ v_quant,
+                       float* __restrict__ v_scale, float* __restrict__ v_mn, int* err,
+                       RowSource<__nv_bfloat16> rs) {
+  pack_value_fast_rows<G>(value, slots, slot_dtype, num_tokens, kvh, num_slots, v_quant, v_scale, v_mn, err, rs,
+                          blockIdx.x);
+}
+
+// Keys and values of the same tokens in one launch: CTAs [0, groups * kvh)
+// take the key tiles (group = x / kvh, head = x % kvh), the rest the value rows.
+template <int G>
+__global__ void __launch_bounds__(256)
+pack_kv_fast_kernel(const __nv_bfloat16* __restrict__ key, const __nv_bfloat16* __restrict__ value,
+                    const void* __restrict__ slots, int slot_dtype, int64_t num_tokens, int kvh, int block_size,
+                    int64_t num_blocks, int32_t* __restrict__ k_quant, float* __restrict__ k_scale,
+                    float* __restrict__ k_mn, int32_t* __restrict__ v_quant, float* __restrict__ v_scale,
+                    float* __restrict__ v_mn, int* err) {
+  const int64_t key_ctas = num_tokens / G * kvh;
+  const int64_t x = blockIdx.x;
+  if (x < key_ctas)
+    pack_key_fast_tile<G>(key, slots, slot_dtype, kvh, block_size, num_blocks, k_quant, k_scale, k_mn, err,
+                          x / kvh, static_cast<int>(x % kvh));
+  else
+    pack_value_fast_rows<G>(value, slots, slot_dtype, num_tokens, kvh, num_blocks * block_size, v_quant, v_scale,
+                            v_mn, err, RowSource<__nv_bfloat16>{nullptr, nullptr, nullptr, 0, 0}, x - key_ctas);
 }
 
 template <typename T>
@@ -837,6 +878,50 @@ int qkv_kivi_pack_value(const void* value, int value_dtype,
                                        group_size, block_size, num_blocks,
                                        v_quant, v_scale, v_mn, s);
   }
+}
+
+int qkv_kivi_pack_kv(const void* key, const void* value, int dtype, const void* slot_mapping, int slot_dtype,
+                     int64_t num_tokens, int num_kv_heads, int head_size, int group_size, int block_size,
+                     int64_t num_blocks, int32_t* k_quant, float* k_scale, float* k_mn, int32_t* v_quant,
+                     float* v_scale, float* v_mn, qkv_stream_t stream) {
+  using namespace qkv;
+  int rc = check_common("qkv_kivi_pack_kv", dtype, slot_dtype, num_tokens, num_kv_heads, head_size, group_size,
+                        block_size, num_blocks);
+  if (rc != QKV_OK) return rc;
+  QKV_CHECK_ARG(num_tokens % group_size == 0, "qkv_kivi_pack_kv: num_tokens must be a whole number of groups");
+  QKV_CHECK_ARG(block_size % group_size == 0, "qkv_kivi_pack_kv: block_size must be divisible by group_size");
+  QKV_CHECK_ARG(head_size % group_size == 0, "qkv_kivi_pack_kv: head_size must be divisible by group_size");
+  if (num_tokens == 0) return QKV_OK;
+  QKV_CHECK_ARG(key && value && slot_mapping && k_quant && k_scale && k_mn && v_quant && v_scale && v_mn,
+                "qkv_kivi_pack_kv: null pointer");
+  const auto al = [](const void* p, unsigned m) { return (reinterpret_cast<uintptr_t>(p) & m) == 0; };
+  const bool fused = dtype == QKV_BF16 && head_size == 128 && (group_size == 64 || group_size == 128) &&
+                     al(key, 3u) && al(k_quant, group_size == 128 ? 15u : 7u) && al(value, 15u) && al(v_quant, 7u) &&
+                     num_tokens * num_kv_heads < (int64_t{1} << 40);
+  if (!fused) {
+    rc = qkv_kivi_pack_key(key, dtype, slot_mapping, slot_dtype, num_tokens, num_kv_heads, head_size, group_size,
+                           block_size, num_blocks, k_quant, k_scale, k_mn, stream);
+    if (rc != QKV_OK) return rc;
+    return qkv_kivi_pack_value(value, dtype, slot_mapping, slot_dtype, num_tokens, num_kv_heads, head_size,
+                               group_size, block_size, num_blocks, v_quant, v_scale, v_mn, stream);
+  }
+  const int64_t key_ctas = num_tokens / group_size * num_kv_heads;
+  const int64_t value_ctas = (num_tokens * num_kv_heads * 8 + 255) / 256;
+  const int64_t grid = key_ctas + value_ctas;
+  QKV_CHECK_ARG(grid < (int64_t{1} << 31), "qkv_kivi_pack_kv: too many tokens for one launch");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const auto* k = static_cast<const __nv_bfloat16*>(key);
+  const auto* v = static_cast<const __nv_bfloat16*>(value);
+  if (group_size == 128)
+    pack_kv_fast_kernel<128><<<static_cast<unsigned>(grid), 256, 0, s>>>(
+        k, v, slot_mapping, slot_dtype, num_tokens, num_kv_heads, block_size, num_blocks, k_quant, k_scale, k_mn,
+        v_quant, v_scale, v_mn, device_error_ptr());
+  else
+    pack_kv_fast_kernel<64><<<static_cast<unsigned>(grid), 256, 0, s>>>(
+        k, v, slot_mapping, slot_dtype, num_tokens, num_kv_heads, block_size, num_blocks, k_quant, k_scale, k_mn,
+        v_quant, v_scale, v_mn, device_error_ptr());
+  QKV_CHECK_LAUNCH("pack_kv_fast_kernel");
+  return QKV_OK;
 }
 
 }  // extern "C"

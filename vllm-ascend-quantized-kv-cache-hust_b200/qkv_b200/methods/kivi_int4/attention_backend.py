@@ -321,10 +321,14 @@ class AscendKiviInt4AttentionBackendMixin:
         k_src, v_src = idx[o[0]:o[1]], idx[o[1]:o[2]]
         k_fl, v_fl, k_wl, v_wl = idx[o[2]:o[3]], idx[o[3]:o[4]], idx[o[4]:o[5]], idx[o[5]:o[6]]
         gk, gv = kivi_window_gather(rk, rv, new_tokens[0], new_tokens[1], k_src, v_src)
-        if nfk:
-            self._write_kivi_key_quant_cache(gk[:nfk], k_fl, _host_slots=kfl.tolist())
-        if nfv:
-            self._write_kivi_value_quant_cache(gv[:nfv], v_fl)
+        if nfk and nfk == nfv and kfl.min() >= 0 and np.array_equal(kfl, vfl):
+            # both sides flush the same slots (a bulk prompt write): one launch
+            self._write_kivi_kv_quant_cache(gk[:nfk], gv[:nfv], k_fl, kfl.tolist())
+        else:
+            if nfk:
+                self._write_kivi_key_quant_cache(gk[:nfk], k_fl, _host_slots=kfl.tolist())
+            if nfv:
+                self._write_kivi_value_quant_cache(gv[:nfv], v_fl)
         kivi_window_scatter(rk, rv, k_wl, gk[nfk:], v_wl, gv[nfv:])
 
     def _kivi_set_plan_source(self, key: torch.Tensor, value: torch.Tensor) -> None:
@@ -471,6 +475,35 @@ class AscendKiviInt4AttentionBackendMixin:
         if not is_aligned_key_window(host_slots, self.kivi_group_size, block_size):
             raise RuntimeError("KIVI key flush requires contiguous aligned token groups.")
         self._launch_kivi_key_pack(key, slots)
+
+    def _write_kivi_kv_quant_cache(self, key: Any, value: Any, slot_mapping: Any, host_slots: list[int]) -> None:
+        """Key and value flush of the same (valid) slots, with both sides'
+        checks before the one launch (qkv_kivi_pack_kv)."""
+        self._check_kivi_cache_bound()
+        block_size = self._get_kivi_block_size()
+        g = self.kivi_group_size
+        if key.shape[-1] != self.head_size or value.shape[-1] != self.head_size:
+            raise RuntimeError(
+                f"KIVI INT4 key/value head_size must match attention head_size ({self.head_size})."
+            )
+        if key.shape[0] % g != 0:
+            raise RuntimeError(
+                f"KIVI key flush must contain whole token groups, got {key.shape[0]} tokens for group_size={g}."
+            )
+        if self.head_size % 8 != 0 or g % 8 != 0 or self.head_size % g != 0 or block_size % g != 0:
+            raise RuntimeError("KIVI INT4 packing geometry is invalid for this cache.")
+        if not is_aligned_key_window(host_slots, g, block_size):
+            raise RuntimeError("KIVI key flush requires contiguous aligned token groups.")
+        self._launch_kivi_kv_pack(key.contiguous(), value.contiguous(), slot_mapping.to(torch.long).contiguous())
+
+    def _launch_kivi_kv_pack(self, key: Any, value: Any, slots: Any) -> None:
+        """Kernel launch seam of the two-sided flush."""
+        from ...ops.kivi_pack import kivi_pack_kv_cache
+
+        kivi_pack_kv_cache(
+            key, value, slots, (self.k_quant_cache, self.k_scale_cache, self.k_mn_cache),
+            (self.v_quant_cache, self.v_scale_cache, self.v_mn_cache), self.kivi_group_size, validate_slots=False,
+        )
 
     def _launch_kivi_key_pack(self, key: Any, slots: Any) -> None:
         """Kernel launch seam (tests may replace it)."""

@@ -9,7 +9,7 @@ from .fp8 import fp8_dequant_gather, fp8_paged_decode, fp8_store
 from .int8 import int8_calc_scales, int8_dequant_gather, int8_paged_decode, int8_quant_store
 from .kivi_decode import kivi_paged_decode
 from .kivi_gather import kivi_dequant_gather
-from .kivi_pack import kivi_pack_key_cache, kivi_pack_value_cache
+from .kivi_pack import kivi_pack_key_cache, kivi_pack_kv_cache, kivi_pack_value_cache
 from .prefill import dense_prefill
 
 __all__ = [
@@ -23,6 +23,7 @@ __all__ = [
     "int8_quant_store",
     "kivi_dequant_gather",
     "kivi_pack_key_cache",
+    "kivi_pack_kv_cache",
     "kivi_pack_value_cache",
     "kivi_paged_decode",
 ]

@@ -55,6 +55,11 @@ SIGNATURES: dict[str, tuple] = {
         c_int,
         [c_vp, c_int, c_vp, c_int, c_i64, c_int, c_int, c_int, c_int, c_i64, c_vp, c_vp, c_vp, c_vp],
     ),
+    "qkv_kivi_pack_kv": (
+        c_int,
+        [c_vp, c_vp, c_int, c_vp, c_int, c_i64, c_int, c_int, c_int, c_int, c_i64,
+         c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
+    ),
     "qkv_kivi_pack_value": (
         c_int,
         [c_vp, c_int, c_vp, c_int, c_i64, c_int, c_int, c_int, c_int, c_i64, c_vp, c_vp, c_vp, c_vp],

@@ -120,4 +120,57 @@ def kivi_pack_key_cache(
     _lib.check(rc, "kivi_pack_key_cache")
 
 
-__all__ = ["kivi_pack_key_cache", "kivi_pack_value_cache"]
+def kivi_pack_kv_cache(
+    key: torch.Tensor,
+    value: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    k_caches: tuple,
+    v_caches: tuple,
+    group_size: int,
+    *,
+    validate_slots: bool = True,
+) -> None:
+    """``kivi_pack_key_cache(key, ...)`` then ``kivi_pack_value_cache(value,
+    ...)`` on the same slots, as one launch (``qkv_kivi_pack_kv``): the bulk
+    prompt write's flush of both sides. ``k_caches`` = (k_quant, k_scale,
+    k_mn), ``v_caches`` = (v_quant, v_scale, v_mn); the same validators and
+    messages as the two calls."""
+    num_tokens, num_kv_heads, head_size = key.shape
+    if num_tokens == 0:
+        return
+    if value.shape != key.shape or value.dtype != key.dtype:
+        raise RuntimeError("kivi_pack_kv_cache: key and value must have the same shape and dtype.")
+    assert group_size % 8 == 0
+    assert num_tokens % group_size == 0
+    assert head_size % group_size == 0
+    assert head_size % 8 == 0
+    k_quant, k_scale, k_mn = k_caches
+    v_quant, v_scale, v_mn = v_caches
+    for name, t in (("key", key), ("value", value), ("slot_mapping", slot_mapping), ("k_quant_cache", k_quant),
+                    ("k_scale_cache", k_scale), ("k_mn_cache", k_mn), ("v_quant_cache", v_quant),
+                    ("v_scale_cache", v_scale), ("v_mn_cache", v_mn)):
+        _check_contiguous(name, t)
+    for name, t in (("value", value), ("slot_mapping", slot_mapping), ("k_quant_cache", k_quant),
+                    ("k_scale_cache", k_scale), ("k_mn_cache", k_mn), ("v_quant_cache", v_quant),
+                    ("v_scale_cache", v_scale), ("v_mn_cache", v_mn)):
+        _check_same_device(name, t, key)
+    _check_slot_mapping(slot_mapping, num_tokens)
+    block_size = _check_key_cache_layout(
+        k_quant, k_scale, k_mn, num_kv_heads=num_kv_heads, head_size=head_size, group_size=group_size,
+    )
+    _check_value_cache_layout(
+        v_quant, v_scale, v_mn, num_kv_heads=num_kv_heads, head_size=head_size, group_size=group_size,
+    )
+    if validate_slots:
+        _check_key_slot_groups(slot_mapping, block_size=block_size, group_size=group_size)
+    require_cuda("kivi_pack_kv_cache", key, value)
+    lib = _lib.load()
+    rc = lib.qkv_kivi_pack_kv(
+        ptr(key), ptr(value), dtype_code(key), ptr(slot_mapping), index_code(slot_mapping),
+        num_tokens, num_kv_heads, head_size, group_size, block_size, k_quant.shape[0],
+        ptr(k_quant), ptr(k_scale), ptr(k_mn), ptr(v_quant), ptr(v_scale), ptr(v_mn), stream_handle(key.device),
+    )
+    _lib.check(rc, "kivi_pack_kv_cache")
+
+
+__all__ = ["kivi_pack_key_cache", "kivi_pack_kv_cache", "kivi_pack_value_cache"]
