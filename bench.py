@@ -938,15 +938,17 @@ def measured_peaks() -> dict:
     return {}
 
 
-def bench_pack(device, check=False):
+def bench_pack(device, check=False, tokens=None):
     """Pack GB/s (config 2's definition: 5248 B/token = 4096 bf16 in + 1152
-    out at KVH 8, D 128, g 128): keys and values of 8192 tokens."""
+    out at KVH 8, D 128, g 128): keys and values of 8192 tokens (or
+    ``tokens``), one bulk-prompt flush of both sides."""
     import torch
 
     from qkv_b200.ops import kivi_pack_kv_cache
 
     c = CONFIG2_PACK
     T, H, D, g, blk = c["tokens"], c["num_kv_heads"], c["head_size"], c["group_size"], c["block_size"]
+    T = tokens or T
     nb = T // blk
     k = torch.randn(T, H, D, device=device).to(torch.bfloat16)
     v = torch.randn(T, H, D, device=device).to(torch.bfloat16)
@@ -1180,7 +1182,10 @@ def main():
         print(json.dumps({"only": "config4", **run_config4_leg(device, args)}), flush=True)
         return
     if args.only == "pack":
-        print(json.dumps({"only": "pack", **bench_pack(device, check=args.check)}), flush=True)
+        res = bench_pack(device, check=args.check)
+        res["at_32768_tokens"] = {k: v for k, v in bench_pack(device, tokens=32768).items()
+                                  if k in ("gbs", "us_per_call", "tokens", "bytes_per_call")}
+        print(json.dumps({"only": "pack", **res}), flush=True)
         return
     if args.only == "small":
         print(json.dumps({"only": "small", **run_small_configs(device, args)}), flush=True)
@@ -1287,7 +1292,11 @@ def main():
     # grid), then the combine kernel when the plan has several splits
     launches_per_step = 2 if workspace_splits > 0 else 1
 
-    pack = bench_pack(device, check=world == 1 and args.check) if rank == 0 else None
+    pack = None
+    if rank == 0:
+        pack = bench_pack(device, check=world == 1 and args.check)
+        pack["at_32768_tokens"] = {k: v for k, v in bench_pack(device, tokens=32768).items()
+                                   if k in ("gbs", "us_per_call", "tokens", "bytes_per_call")}
     int8 = None
     if not args.no_int8:
         int8 = run_int8_leg(cfg3, rank, world, device, args)

@@ -340,11 +340,10 @@ pack_key_tiled_kernel(const T* __restrict__ key, const void* __restrict__ slots,
 // the reference's floor argument lies within 2.5 * 2^-20 < 2^-18.6 of
 // d * inv + 0.5, and e itself is within 2^-25 of d * inv - k: inside the band
 // that argument lies in (k, k + 1) and floor gives k. k lies in [0, 15]
-// because 0 <= d <= mx - mn. A word (8 codes) with any element outside the
-// band (within 2^-16 of a rounding tie, about 3e-5 of random inputs, or a
-// non-finite input: NaN fails every comparison) is recomputed with the
-// division sequence above. The fp32 pairs run as packed f32x2 instructions
-// (two lanes per instruction, Blackwell).
+// because 0 <= d <= mx - mn. An element outside the band (within 2^-16 of a
+// rounding tie, or a non-finite input: NaN fails every comparison) is
+// recomputed with the division sequence above. The fp32 pairs run as packed
+// f32x2 instructions (two lanes per instruction, Blackwell).
 namespace fastq {
 
 using u64 = unsigned long long;
@@ -383,18 +382,18 @@ __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w <<
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
 // Codes of the two bf16 values of w against per-lane (mn, inv): returned in
-// the low byte of r0 / r1; `ok` keeps its sign bit only while every element
-// so far lies inside the exact band.
-__device__ __forceinline__ void quant2(uint32_t w, u64 mn2, u64 inv2, uint32_t& r0, uint32_t& r1, uint32_t& ok) {
+// the low byte of r0 / r1. `ok` keeps its sign bit only while every element
+// so far lies inside the exact band; k0 / k1 (when asked for) carry each
+// element's own check (sign bit set: inside).
+__device__ __forceinline__ void quant2(uint32_t w, u64 mn2, u64 inv2, uint32_t& r0, uint32_t& r1, uint32_t& k0,
+                                       uint32_t& k1) {
   const u64 m2 = pack2(kMagic, kMagic);
   const u64 t2 = pack2(-kTie2, -kTie2);
   const u64 d = sub2(pack2(bf_lo(w), bf_hi(w)), mn2);
   const u64 r = fma2(d, inv2, m2);
   const u64 e = fma2(d, inv2, sub2(m2, r));  // d * inv - k
-  uint32_t c0, c1;
-  unpack2(fma2(e, e, t2), c0, c1);           // e^2 - band^2: negative inside
+  unpack2(fma2(e, e, t2), k0, k1);           // e^2 - band^2: negative inside
   unpack2(r, r0, r1);
-  ok &= c0 & c1;
 }
 
 // 8 codes (low bytes of c[0..7], each < 16) -> one int4 word, lane L at bits 4L.
@@ -404,33 +403,63 @@ __device__ __forceinline__ uint32_t pack8(const uint32_t (&c)[8]) {
   return e | (o << 4);
 }
 
+// The exact division sequence for one element, off the fast path: a real
+// call (not inlined), so the compiler branches around it instead of
+// predicating it into every element. Exact ties are common with bf16 inputs
+// (about 2e-3 of random N(0, 1) values: (x - mn) / s is a ratio of small
+// integers), so only the flagged elements of a word take it, one call each.
+__device__ __noinline__ uint32_t exact_code(float x, float mn, float sc) { return quantize_code(x, mn, sc); }
+
+// Replaces the codes of the elements of `word` whose check lies outside the
+// band (sign bit clear) with the exact ones; only called for a word whose
+// combined check failed (rare), so the checks are recomputed here rather than
+// kept live through the fast path. pair(i) is the bf16 pair holding elements
+// 2i and 2i + 1 of the word when `lanes_in_pairs`, else (keys) element l is
+// the lo / hi half (`hi`) of pair(l).
+template <bool kPairs, typename P>
+__device__ __noinline__ uint32_t patch_word(uint32_t word, P pair, bool hi, u64 mn2, u64 inv2, float mn, float sc) {
+#pragma unroll
+  for (int l = 0; l < 8; ++l) {
+    const uint32_t w = kPairs ? pair(l >> 1) : pair(l);
+    uint32_t r0, r1, k0, k1;
+    quant2(w, mn2, inv2, r0, r1, k0, k1);
+    const bool take_hi = kPairs ? (l & 1) : hi;
+    if (((take_hi ? k1 : k0) >> 31) == 0)
+      word = (word & ~(0xFu << (4 * l))) | (exact_code(take_hi ? bf_hi(w) : bf_lo(w), mn, sc) << (4 * l));
+  }
+  return word;
+}
+
 }  // namespace fastq
 
-// Keys: one CTA of 256 threads per (token group, head). Thread (warp w, lane)
-// owns the channel pair cp = 32 (w & 1) + lane and the token quarter
-// tc = w >> 1 of the group: it loads the pair for its G / 4 tokens (a warp's
-// loads are 128 contiguous bytes of a token row), reduces min / max in bf16
-// pairs (exact), the four quarters meet in shared memory, and each thread
-// quantises and stores its own G / 32 words per channel.
+// Keys: one CTA of 256 threads per (token group, head, channel half).
+// Thread (warp w, lane) owns the channel pair cp = 32 half + lane and the
+// token eighth w of the group: it loads the pair for its G / 8 tokens (a
+// warp's loads are 128 contiguous bytes of a token row), reduces min / max in
+// bf16 pairs (exact), the eight chunks meet in shared memory, and each thread
+// quantises and stores its own G / 64 words per channel.
 template <int G>
 __device__ __forceinline__ void pack_key_fast_tile(const __nv_bfloat16* __restrict__ key,
                                                    const void* __restrict__ slots, int slot_dtype, int kvh,
                                                    int block_size, int64_t num_blocks, int32_t* __restrict__ k_quant,
                                                    float* __restrict__ k_scale, float* __restrict__ k_mn, int* err,
-                                                   int64_t gi, int head) {
+                                                   int64_t gi, int head, int half) {
   using namespace fastq;
-  constexpr int kD = 128, kTok = G / 4, kWords = kTok / 8;
-  __shared__ uint32_t s_mn[4][64], s_mx[4][64];
+  constexpr int kD = 128, kChunks = 8, kTok = G / kChunks, kWords = kTok / 8;
+  __shared__ uint32_t s_mn[kChunks][32], s_mx[kChunks][32];
   const int64_t first_slot = load_index(slots, slot_dtype, gi * G);
   if (first_slot < 0) return;  // the reference kernel skips such groups
-  const int64_t blk = first_slot / block_size;
+  // (32-bit division whenever the slot fits: one per thread, on every lane)
+  const int64_t blk = first_slot < 0x7FFFFFFF
+                          ? static_cast<int64_t>(static_cast<uint32_t>(first_slot) / static_cast<uint32_t>(block_size))
+                          : first_slot / block_size;
   const int off = static_cast<int>(first_slot - blk * block_size);
   if (blk >= num_blocks || (off % G) != 0 || off + G > block_size) {
     if (threadIdx.x == 0) record_error(err, kErrSlot);
     return;
   }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int cp = 32 * (warp & 1) + lane, tc = warp >> 1;
+  const int tc = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cp = 32 * half + lane;
   const int64_t row_words = static_cast<int64_t>(kvh) * (kD / 2);
   const uint32_t* src =
       reinterpret_cast<const uint32_t*>(key) + (gi * G + tc * kTok) * row_words + head * (kD / 2) + cp;
@@ -443,13 +472,13 @@ __device__ __forceinline__ void pack_key_fast_tile(const __nv_bfloat16* __restri
     mn = bmin2(mn, v[i]);
     mx = bmax2(mx, v[i]);
   }
-  s_mn[tc][cp] = mn;
-  s_mx[tc][cp] = mx;
+  s_mn[tc][lane] = mn;
+  s_mx[tc][lane] = mx;
   __syncthreads();
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    mn = bmin2(mn, s_mn[j][cp]);
-    mx = bmax2(mx, s_mx[j][cp]);
+  for (int j = 0; j < kChunks; ++j) {
+    mn = bmin2(mn, s_mn[j][lane]);
+    mx = bmax2(mx, s_mx[j][lane]);
   }
   const float mn0 = bf_lo(mn), mn1 = bf_hi(mn);
   const float sc0 = group_scale(mn0, bf_lo(mx)), sc1 = group_scale(mn1, bf_hi(mx));
@@ -459,28 +488,34 @@ __device__ __forceinline__ void pack_key_fast_tile(const __nv_bfloat16* __restri
   for (int j = 0; j < kWords; ++j) {
     uint32_t c0[8], c1[8], ok = 0xFFFFFFFFu;
 #pragma unroll
-    for (int l = 0; l < 8; ++l) quant2(v[8 * j + l], mn2, inv2, c0[l], c1[l], ok);
+    for (int l = 0; l < 8; ++l) {
+      uint32_t k0, k1;
+      quant2(v[8 * j + l], mn2, inv2, c0[l], c1[l], k0, k1);
+      ok &= k0 & k1;
+    }
     w0[j] = pack8(c0);
     w1[j] = pack8(c1);
-    if ((ok >> 31) == 0) {  // an element near a tie: the exact sequence
-      w0[j] = w1[j] = 0;
-#pragma unroll
-      for (int l = 0; l < 8; ++l) {
-        w0[j] |= quantize_code(bf_lo(v[8 * j + l]), mn0, sc0) << (4 * l);
-        w1[j] |= quantize_code(bf_hi(v[8 * j + l]), mn1, sc1) << (4 * l);
-      }
+    if ((ok >> 31) == 0) {  // an element near a rounding tie (rare): exact codes for it
+      const uint4 a = make_uint4(v[8 * j], v[8 * j + 1], v[8 * j + 2], v[8 * j + 3]);
+      const uint4 b = make_uint4(v[8 * j + 4], v[8 * j + 5], v[8 * j + 6], v[8 * j + 7]);
+      const auto pair = [a, b](int l) {
+        const uint32_t t[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        return t[l];
+      };
+      w0[j] = patch_word<false>(w0[j], pair, false, mn2, inv2, mn0, sc0);
+      w1[j] = patch_word<false>(w1[j], pair, true, mn2, inv2, mn1, sc1);
     }
   }
   const int64_t chan0 = (blk * kvh + head) * static_cast<int64_t>(kD) + 2 * cp;
   const int64_t wpc = block_size >> 3;  // words per channel and page
   int32_t* dst0 = k_quant + chan0 * wpc + (off >> 3) + tc * kWords;
   int32_t* dst1 = dst0 + wpc;
-  if constexpr (kWords == 4) {
-    *reinterpret_cast<uint4*>(dst0) = make_uint4(w0[0], w0[1], w0[2], w0[3]);
-    *reinterpret_cast<uint4*>(dst1) = make_uint4(w1[0], w1[1], w1[2], w1[3]);
-  } else {
+  if constexpr (kWords == 2) {
     *reinterpret_cast<uint2*>(dst0) = make_uint2(w0[0], w0[1]);
     *reinterpret_cast<uint2*>(dst1) = make_uint2(w1[0], w1[1]);
+  } else {
+    *dst0 = static_cast<int32_t>(w0[0]);
+    *dst1 = static_cast<int32_t>(w1[0]);
   }
   if (tc == 0) {
     const int gpb = block_size / G;
@@ -498,27 +533,29 @@ pack_key_fast_kernel(const __nv_bfloat16* __restrict__ key, const void* __restri
                      int kvh, int block_size, int64_t num_blocks, int32_t* __restrict__ k_quant,
                      float* __restrict__ k_scale, float* __restrict__ k_mn, int* err) {
   pack_key_fast_tile<G>(key, slots, slot_dtype, kvh, block_size, num_blocks, k_quant, k_scale, k_mn, err,
-                        blockIdx.x, blockIdx.y);
+                        blockIdx.x, blockIdx.y >> 1, blockIdx.y & 1);
 }
 
-// Values: 8 threads per (token, head) row of 128 dims, 16 dims (two 16-byte
-// loads) each; a group of G dims is G / 16 threads, reduced with shuffles.
-// Each thread stores its two words (8 bytes; a row's 64 bytes contiguous).
+// Values: two threads per (token, head) row of 128 dims, 64 contiguous dims
+// (eight 16-byte loads) each, so a warp covers 16 rows; at group 128 the two
+// halves combine min / max with one shuffle. Each thread stores its eight
+// words (two 16-byte vectors). Index arithmetic is 32-bit: the launcher
+// guarantees num_tokens * kvh * 2 < 2^31.
 template <int G>
 __device__ __forceinline__ void pack_value_fast_rows(const __nv_bfloat16* __restrict__ value,
                                                      const void* __restrict__ slots, int slot_dtype,
-                                                     int64_t num_tokens, int kvh, int64_t num_slots,
+                                                     int num_rows, int kvh, int64_t num_slots,
                                                      int32_t* __restrict__ v_quant, float* __restrict__ v_scale,
                                                      float* __restrict__ v_mn, int* err,
-                                                     const RowSource<__nv_bfloat16>& rs, int64_t block) {
+                                                     const RowSource<__nv_bfloat16>& rs, unsigned block) {
   using namespace fastq;
-  constexpr int kD = 128, kTpg = G / 16;  // threads per group
-  const int64_t tid = block * blockDim.x + threadIdx.x;
-  const int64_t row = tid >> 3;  // token * kvh + head
-  const int part = static_cast<int>(tid & 7);
-  const bool in_range = row < num_tokens * kvh;
-  const int64_t token = in_range ? row / kvh : 0;
-  const int head = in_range ? static_cast<int>(row % kvh) : 0;
+  constexpr int kD = 128, kHalf = kD / 2;
+  const unsigned tid = block * blockDim.x + threadIdx.x;
+  const unsigned row = tid >> 1;  // token * kvh + head
+  const int part = static_cast<int>(tid & 1);
+  const bool in_range = row < static_cast<unsigned>(num_rows);
+  const unsigned token = in_range ? row / static_cast<unsigned>(kvh) : 0u;
+  const int head = static_cast<int>(row - token * static_cast<unsigned>(kvh));
   int64_t slot = -1;
   if (in_range) slot = load_index(slots, slot_dtype, token);
   bool valid = in_range && slot >= 0;
@@ -526,7 +563,7 @@ __device__ __forceinline__ void pack_value_fast_rows(const __nv_bfloat16* __rest
     record_error(err, kErrSlot);
     valid = false;
   }
-  const __nv_bfloat16* rowp = in_range ? value + row * kD : nullptr;
+  const __nv_bfloat16* rowp = in_range ? value + static_cast<int64_t>(row) * kD : nullptr;
   if (rs.src != nullptr && in_range) {
     const int64_t sidx = rs.src[token];
     const int64_t tok_row = static_cast<int64_t>(kvh) * kD;
@@ -540,69 +577,79 @@ __device__ __forceinline__ void pack_value_fast_rows(const __nv_bfloat16* __rest
       rowp = nullptr;
     }
   }
-  uint32_t v[8];
+  uint32_t v[kHalf / 2];
   if (rowp != nullptr) {
-    const uint4 a = __ldg(reinterpret_cast<const uint4*>(rowp) + 2 * part);
-    const uint4 b = __ldg(reinterpret_cast<const uint4*>(rowp) + 2 * part + 1);
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+#pragma unroll
+    for (int i = 0; i < kHalf / 8; ++i) {
+      const uint4 a = __ldg(reinterpret_cast<const uint4*>(rowp + kHalf * part) + i);
+      v[4 * i] = a.x;
+      v[4 * i + 1] = a.y;
+      v[4 * i + 2] = a.z;
+      v[4 * i + 3] = a.w;
+    }
   } else {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = 0u;
+    for (int i = 0; i < kHalf / 2; ++i) v[i] = 0u;
   }
   uint32_t mnp = v[0], mxp = v[0];
 #pragma unroll
-  for (int i = 1; i < 8; ++i) {
+  for (int i = 1; i < kHalf / 2; ++i) {
     mnp = bmin2(mnp, v[i]);
     mxp = bmax2(mxp, v[i]);
   }
   float mn = fminf(bf_lo(mnp), bf_hi(mnp)), mx = fmaxf(bf_lo(mxp), bf_hi(mxp));
-#pragma unroll
-  for (int o = 1; o < kTpg; o <<= 1) {
-    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if constexpr (G == kD) {  // the row is one group: combine the halves
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
   }
   if (!valid) return;
   const float sc = group_scale(mn, mx);
   const float inv = __frcp_rn(sc);
   const u64 mn2 = pack2(mn, mn), inv2 = pack2(inv, inv);
-  uint32_t w[2];
+  uint32_t w[kHalf / 8];
 #pragma unroll
-  for (int j = 0; j < 2; ++j) {
+  for (int j = 0; j < kHalf / 8; ++j) {
     uint32_t c[8], ok = 0xFFFFFFFFu;
 #pragma unroll
-    for (int l = 0; l < 4; ++l) quant2(v[4 * j + l], mn2, inv2, c[2 * l], c[2 * l + 1], ok);
+    for (int l = 0; l < 4; ++l) {
+      uint32_t k0, k1;
+      quant2(v[4 * j + l], mn2, inv2, c[2 * l], c[2 * l + 1], k0, k1);
+      ok &= k0 & k1;
+    }
     w[j] = pack8(c);
-    if ((ok >> 31) == 0) {
-      w[j] = 0;
-#pragma unroll
-      for (int l = 0; l < 4; ++l) {
-        w[j] |= quantize_code(bf_lo(v[4 * j + l]), mn, sc) << (8 * l);
-        w[j] |= quantize_code(bf_hi(v[4 * j + l]), mn, sc) << (8 * l + 4);
-      }
+    if ((ok >> 31) == 0) {  // an element near a rounding tie (rare): exact codes for it
+      const uint4 a = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      const auto pair = [a](int i) {
+        const uint32_t t[4] = {a.x, a.y, a.z, a.w};
+        return t[i];
+      };
+      w[j] = patch_word<true>(w[j], pair, false, mn2, inv2, mn, sc);
     }
   }
   const int64_t dst_row = slot * kvh + head;
-  *reinterpret_cast<uint2*>(v_quant + dst_row * (kD / 8) + 2 * part) = make_uint2(w[0], w[1]);
-  if (part % kTpg == 0) {
-    const int64_t s = dst_row * (kD / G) + part / kTpg;
-    v_scale[s] = sc;
-    v_mn[s] = mn;
+  uint4* dst = reinterpret_cast<uint4*>(v_quant + dst_row * (kD / 8) + part * (kHalf / 8));
+  dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  if (G == kD ? part == 0 : true) {
+    const int64_t sidx = dst_row * (kD / G) + (G == kD ? 0 : part);
+    v_scale[sidx] = sc;
+    v_mn[sidx] = mn;
   }
 }
 
 template <int G>
 __global__ void __launch_bounds__(256)
 pack_value_fast_kernel(const __nv_bfloat16* __restrict__ value, const void* __restrict__ slots, int slot_dtype,
-                       int64_t num_tokens, int kvh, int64_t num_slots, int32_t* __restrict__ v_quant,
+                       int num_rows, int kvh, int64_t num_slots, int32_t* __restrict__ v_quant,
                        float* __restrict__ v_scale, float* __restrict__ v_mn, int* err,
                        RowSource<__nv_bfloat16> rs) {
-  pack_value_fast_rows<G>(value, slots, slot_dtype, num_tokens, kvh, num_slots, v_quant, v_scale, v_mn, err, rs,
+  pack_value_fast_rows<G>(value, slots, slot_dtype, num_rows, kvh, num_slots, v_quant, v_scale, v_mn, err, rs,
                           blockIdx.x);
 }
 
-// Keys and values of the same tokens in one launch: CTAs [0, groups * kvh)
-// take the key tiles (group = x / kvh, head = x % kvh), the rest the value rows.
+// Keys and values of the same tokens in one launch: CTAs [0, 2 groups kvh)
+// take the key tiles (x / 2 = group * kvh + head, x % 2 = channel half), the
+// rest the value rows.
 template <int G>
 __global__ void __launch_bounds__(256)
 pack_kv_fast_kernel(const __nv_bfloat16* __restrict__ key, const __nv_bfloat16* __restrict__ value,
@@ -610,14 +657,18 @@ pack_kv_fast_kernel(const __nv_bfloat16* __restrict__ key, const __nv_bfloat16* 
                     int64_t num_blocks, int32_t* __restrict__ k_quant, float* __restrict__ k_scale,
                     float* __restrict__ k_mn, int32_t* __restrict__ v_quant, float* __restrict__ v_scale,
                     float* __restrict__ v_mn, int* err) {
-  const int64_t key_ctas = num_tokens / G * kvh;
-  const int64_t x = blockIdx.x;
-  if (x < key_ctas)
+  const unsigned key_ctas = static_cast<unsigned>(num_tokens / G * kvh * 2);
+  const unsigned x = blockIdx.x;
+  if (x < key_ctas) {
+    const unsigned gh = x >> 1;  // (group, head); x & 1 = channel half
     pack_key_fast_tile<G>(key, slots, slot_dtype, kvh, block_size, num_blocks, k_quant, k_scale, k_mn, err,
-                          x / kvh, static_cast<int>(x % kvh));
+                          gh / static_cast<unsigned>(kvh), static_cast<int>(gh % static_cast<unsigned>(kvh)),
+                          static_cast<int>(x & 1));
+  }
   else
-    pack_value_fast_rows<G>(value, slots, slot_dtype, num_tokens, kvh, num_blocks * block_size, v_quant, v_scale,
-                            v_mn, err, RowSource<__nv_bfloat16>{nullptr, nullptr, nullptr, 0, 0}, x - key_ctas);
+    pack_value_fast_rows<G>(value, slots, slot_dtype, static_cast<int>(num_tokens * kvh), kvh,
+                            num_blocks * block_size, v_quant, v_scale, v_mn, err,
+                            RowSource<__nv_bfloat16>{nullptr, nullptr, nullptr, 0, 0}, x - key_ctas);
 }
 
 template <typename T>
@@ -635,8 +686,8 @@ int launch_pack_key(const void* key, const void* slots, int slot_dtype,
     // bf16 at head 128, group 64 / 128: the division-free kernel
     const uintptr_t qa = reinterpret_cast<uintptr_t>(kq);
     if (head_size == 128 && (group_size == 64 || group_size == 128) &&
-        (reinterpret_cast<uintptr_t>(key) & 3u) == 0 && (qa & (group_size == 128 ? 15u : 7u)) == 0) {
-      dim3 fgrid(static_cast<unsigned>(groups), kvh);
+        (reinterpret_cast<uintptr_t>(key) & 3u) == 0 && (qa & 7u) == 0) {
+      dim3 fgrid(static_cast<unsigned>(groups), 2 * kvh);  // y = 2 head + channel half
       if (group_size == 128)
         pack_key_fast_kernel<128><<<fgrid, 256, 0, stream>>>(k, slots, slot_dtype, kvh, block_size, num_blocks,
                                                              kq, ks, km, err);
@@ -701,21 +752,23 @@ int launch_pack_key(const void* key, const void* slots, int slot_dtype,
 }
 
 // The division-free value kernel for bf16 rows at head 128, group 64 / 128
-// (rows 16-byte aligned, v_quant 8-byte aligned); false when it does not apply.
+// (rows and v_quant 16-byte aligned); false when it does not apply.
 bool launch_pack_value_fast(const __nv_bfloat16* v, const void* slots, int slot_dtype, int64_t num_tokens, int kvh,
                             int head_size, int group_size, int64_t num_slots, int32_t* vq, float* vs, float* vm,
                             RowSource<__nv_bfloat16> rs, cudaStream_t stream) {
   const auto al = [](const void* p, unsigned m) { return (reinterpret_cast<uintptr_t>(p) & m) == 0; };
-  if (head_size != 128 || (group_size != 64 && group_size != 128) || !al(vq, 7u)) return false;
+  if (head_size != 128 || (group_size != 64 && group_size != 128) || !al(vq, 15u)) return false;
   if (rs.src == nullptr ? !al(v, 15u) : (!al(rs.ring, 15u) || !al(rs.fresh, 15u))) return false;
-  const int64_t threads = num_tokens * kvh * 8;
+  const int64_t threads = num_tokens * kvh * 2;
+  if (threads >= (int64_t{1} << 31)) return false;
   const unsigned grid = static_cast<unsigned>((threads + 255) / 256);
+  const int rows = static_cast<int>(num_tokens * kvh);
   if (group_size == 128)
-    pack_value_fast_kernel<128><<<grid, 256, 0, stream>>>(v, slots, slot_dtype, num_tokens, kvh, num_slots, vq, vs,
-                                                          vm, device_error_ptr(), rs);
+    pack_value_fast_kernel<128><<<grid, 256, 0, stream>>>(v, slots, slot_dtype, rows, kvh, num_slots, vq, vs, vm,
+                                                          device_error_ptr(), rs);
   else
-    pack_value_fast_kernel<64><<<grid, 256, 0, stream>>>(v, slots, slot_dtype, num_tokens, kvh, num_slots, vq, vs,
-                                                         vm, device_error_ptr(), rs);
+    pack_value_fast_kernel<64><<<grid, 256, 0, stream>>>(v, slots, slot_dtype, rows, kvh, num_slots, vq, vs, vm,
+                                                         device_error_ptr(), rs);
   return true;
 }
 
@@ -896,8 +949,8 @@ int qkv_kivi_pack_kv(const void* key, const void* value, int dtype, const void* 
                 "qkv_kivi_pack_kv: null pointer");
   const auto al = [](const void* p, unsigned m) { return (reinterpret_cast<uintptr_t>(p) & m) == 0; };
   const bool fused = dtype == QKV_BF16 && head_size == 128 && (group_size == 64 || group_size == 128) &&
-                     al(key, 3u) && al(k_quant, group_size == 128 ? 15u : 7u) && al(value, 15u) && al(v_quant, 7u) &&
-                     num_tokens * num_kv_heads < (int64_t{1} << 40);
+                     al(key, 3u) && al(k_quant, 7u) && al(value, 15u) &&
+                     al(v_quant, 15u) && num_tokens * num_kv_heads * 2 < (int64_t{1} << 31);
   if (!fused) {
     rc = qkv_kivi_pack_key(key, dtype, slot_mapping, slot_dtype, num_tokens, num_kv_heads, head_size, group_size,
                            block_size, num_blocks, k_quant, k_scale, k_mn, stream);
@@ -905,8 +958,8 @@ int qkv_kivi_pack_kv(const void* key, const void* value, int dtype, const void* 
     return qkv_kivi_pack_value(value, dtype, slot_mapping, slot_dtype, num_tokens, num_kv_heads, head_size,
                                group_size, block_size, num_blocks, v_quant, v_scale, v_mn, stream);
   }
-  const int64_t key_ctas = num_tokens / group_size * num_kv_heads;
-  const int64_t value_ctas = (num_tokens * num_kv_heads * 8 + 255) / 256;
+  const int64_t key_ctas = num_tokens / group_size * num_kv_heads * 2;
+  const int64_t value_ctas = (num_tokens * num_kv_heads * 2 + 255) / 256;
   const int64_t grid = key_ctas + value_ctas;
   QKV_CHECK_ARG(grid < (int64_t{1} << 31), "qkv_kivi_pack_kv: too many tokens for one launch");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
