@@ -1,8 +1,9 @@
 """Generates the golden fixtures in tests/golden/ by running the REFERENCE.
 
 The reference plugin is pure Python/torch on CPU for everything these fixtures
-pin, so this script imports it read-only (``REFERENCE_ROOT``, default
-``/root/reference``) and records what its own code computes:
+pin, so this script imports it read-only from the checkout named by its one
+argument (or the ``REFERENCE_ROOT`` environment variable) and records what its
+own code computes:
 
 * ``int8.npz``      — ``AscendInt8AttentionBackendMixin._prepare_int8_scales``,
   ``_quantize_kv_to_runtime_int8`` and ``_dequant_int8_paged_kv_to_dense``
@@ -24,9 +25,9 @@ pin, so this script imports it read-only (``REFERENCE_ROOT``, default
   prefill writes, then decode steps that cross key-window flushes and value
   evictions, one finished request and one roll-back.
 
-Run it only where the reference exists (this repository's build container):
-``python tests/golden/make_golden.py``. The GPU box never runs it; the tests
-only read the .npz files it wrote.
+Run it where a checkout of the reference exists:
+``python tests/golden/make_golden.py <reference checkout> [--only fp8]``. The tests only
+read the .npz files it wrote.
 """
 
 from __future__ import annotations
@@ -42,7 +43,18 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REFERENCE_ROOT = Path(os.environ.get("REFERENCE_ROOT", "/root/reference"))
+REFERENCE_ROOT: Path | None = None
+
+
+def _reference_root() -> Path:
+    """The reference checkout: the first argument, else $REFERENCE_ROOT."""
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("REFERENCE_ROOT")
+    if not root:
+        raise SystemExit("usage: make_golden.py <reference checkout> (or set REFERENCE_ROOT)")
+    path = Path(root)
+    if not (path / "src").is_dir():
+        raise SystemExit(f"{path} does not look like a checkout of the reference (no src/)")
+    return path
 
 
 def _import_reference():
@@ -383,7 +395,15 @@ def make_fp8() -> dict:
 
 
 def main() -> None:
-    only = sys.argv[1:] and sys.argv[1] == "--only" and sys.argv[2:3]
+    global REFERENCE_ROOT
+    args = [a for a in sys.argv[1:]]
+    only = None
+    if "--only" in args:
+        i = args.index("--only")
+        only = args[i + 1:i + 2]
+        del args[i:i + 2]
+    sys.argv[1:] = args
+    REFERENCE_ROOT = _reference_root()
     if only and only[0] == "fp8":
         _import_reference()
         np.savez_compressed(HERE / "fp8.npz", **make_fp8())

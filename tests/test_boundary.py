@@ -1,6 +1,7 @@
-"""The reference-facing surface: dtype contract, method registry, dispatcher,
-bootstrap and the KIVI byte budget / six-view split — the behaviour the
-reference's tests/test_plugin.py and tests/test_kivi_int4.py:1205-1400 pin."""
+"""The reference-facing surface: dtype contract, KIVI geometry rules,
+bootstrap, the get_impl_cls dispatcher and the KIVI byte budget / six-view
+split — the behaviour the reference's tests/test_plugin.py and
+tests/test_kivi_int4.py:1205-1400 pin."""
 
 from __future__ import annotations
 
@@ -11,24 +12,13 @@ from types import SimpleNamespace
 import pytest
 import torch
 
-from qkv_b200 import KVQuantMode, bootstrap, kv_methods, resolve_layout
+from qkv_b200 import KVQuantMode, bootstrap, resolve_layout
 from qkv_b200.methods.kivi_int4.byte_cache import (
     KiviByteCacheLayout,
     kivi_byte_cache_layout,
     kivi_caches_from_byte_tensors,
 )
-from qkv_b200.methods.kivi_int4.geometry import validate_kivi_config
-from qkv_b200.methods.base import MethodConfig
-
-
-def test_methods_and_dtypes():
-    # the reference's methods package registers all three (methods/__init__.py)
-    assert kv_methods.list() == ["fp8_per_token_head", "int8_dynamic", "kivi_int4"]
-    assert kv_methods.describe("int8_dynamic")["dtype"] == "int8"
-    assert kv_methods.describe("kivi_int4")["dtype"] == "kivi_int4"
-    assert kv_methods.describe("fp8_per_token_head")["dtype"] == "fp8_per_token_head"
-    with pytest.raises(ValueError, match="unknown quantized KV method"):
-        kv_methods.get("fp8_e4m3")
+from qkv_b200.methods.kivi_int4.geometry import validate_kivi_config, validate_kivi_geometry
 
 
 def test_layout_contract():
@@ -36,6 +26,7 @@ def test_layout_contract():
     lay = resolve_layout("kivi_int4", 128)
     assert lay.storage_dtype == "uint8" and lay.packed_last_dim == 64
     assert lay.quant_mode is KVQuantMode.KIVI_INT4
+    assert resolve_layout("fp8_per_token_head", 128).storage_dtype == "uint8"
     with pytest.raises(ValueError, match="positive even"):
         resolve_layout("kivi_int4", 127)
     with pytest.raises(ValueError, match="not a registered"):
@@ -56,31 +47,36 @@ def test_geometry_rejects(overrides, match):
     kw = dict(head_size=32, group_size=8, residual_length=16, block_size=16)
     kw.update(overrides)
     with pytest.raises(ValueError, match=match):
-        validate_kivi_config(MethodConfig(**kw))
+        validate_kivi_geometry(**kw)
     with pytest.raises(ValueError, match=match):
-        kv_methods.get("kivi_int4", **kw)
+        validate_kivi_config(SimpleNamespace(**kw))
+    # a live impl carries the kivi_* names
+    impl = SimpleNamespace(head_size=kw["head_size"], kivi_group_size=kw["group_size"],
+                           kivi_residual_length=kw["residual_length"], block_size=kw["block_size"])
+    with pytest.raises(ValueError, match=match):
+        validate_kivi_config(impl)
 
 
 def test_import_needs_no_torch():
-    code = "import sys; import qkv_b200; qkv_b200.kv_methods.list(); print('torch' in sys.modules)"
+    code = "import sys; import qkv_b200, qkv_b200.bootstrap, qkv_b200.methods; print('torch' in sys.modules)"
     out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
                          env={"PYTHONPATH": ":".join(sys.path)})
     assert out.stdout.strip() == "False", out.stderr
 
 
 def test_bootstrap_noop_without_host(monkeypatch):
-    monkeypatch.setattr(bootstrap, "detect_host", lambda: None)
+    monkeypatch.setattr(bootstrap, "host_stack_present", lambda: False)
     assert bootstrap.register_plugins() == []
 
 
-def test_bootstrap_registers_both(monkeypatch):
+def test_bootstrap_installs_the_dispatcher(monkeypatch):
     calls = []
-    monkeypatch.setattr(bootstrap, "detect_host", lambda: bootstrap.VLLM_ASCEND_HUST)
-    import qkv_b200.core.activation as activation
+    monkeypatch.setattr(bootstrap, "host_stack_present", lambda: True)
+    import qkv_b200.adapters.vllm_ascend_hust.backend as backend
 
-    monkeypatch.setattr(activation, "activate", lambda name, host: calls.append((name, host)) or {})
+    monkeypatch.setattr(backend, "install_kv_impl_dispatch", lambda: calls.append("install"))
     assert bootstrap.register_plugins() == ["int8_dynamic", "kivi_int4"]
-    assert calls == [("int8_dynamic", "vllm_ascend_hust"), ("kivi_int4", "vllm_ascend_hust")]
+    assert calls == ["install"]
 
 
 @pytest.fixture
@@ -124,18 +120,16 @@ def host_stack(monkeypatch):
     utils.enable_cp = lambda: False
     from qkv_b200.adapters.vllm_ascend_hust import backend
 
-    backend._build_kivi_impl_cls.cache_clear()
-    backend._build_int8_impl_cls.cache_clear()
-    yield SimpleNamespace(backend=HostBackend, impl=HostImpl, cc=cc, utils=utils)
-    backend._build_kivi_impl_cls.cache_clear()
-    backend._build_int8_impl_cls.cache_clear()
+    backend.impl_class.cache_clear()
+    yield SimpleNamespace(backend=HostBackend, impl=HostImpl, cc=cc, utils=utils, install=backend.install_kv_impl_dispatch)
+    backend.impl_class.cache_clear()
 
 
 def test_dispatch_selects_plugin_only_for_quantized_dtypes(host_stack):
-    info = kv_methods.activate("kivi_int4", host="vllm_ascend_hust")
-    assert info["integration"] == "host_get_impl_cls_dispatch"
-    assert "--kv-cache-dtype kivi_int4" in info["usage"]
     be = host_stack.backend
+    assert host_stack.install() is be
+    assert be._quantized_kv_plugin_dispatch_installed
+    assert be._quantized_kv_original_get_impl_cls() is host_stack.impl
     assert be.get_impl_cls() is host_stack.impl
     host_stack.cc.cache_dtype = "kivi_int4"
     cls = be.get_impl_cls()
@@ -154,13 +148,14 @@ def test_dispatch_selects_plugin_only_for_quantized_dtypes(host_stack):
 
     assert issubclass(be.get_impl_cls(), AscendFp8PerTokenHeadAttentionBackendMixin)
     # idempotent install
-    kv_methods.activate("int8_dynamic", host="vllm_ascend_hust")
+    wrapped = be.get_impl_cls
+    assert host_stack.install() is be and be.get_impl_cls is wrapped
     host_stack.cc.cache_dtype = "auto"
     assert be.get_impl_cls() is host_stack.impl
 
 
 def test_dispatch_refuses_context_parallel(host_stack):
-    kv_methods.activate("kivi_int4", host="vllm_ascend_hust")
+    host_stack.install()
     host_stack.utils.enable_cp = lambda: True
     host_stack.cc.cache_dtype = "kivi_int4"
     with pytest.raises(NotImplementedError, match="does not support context parallel"):

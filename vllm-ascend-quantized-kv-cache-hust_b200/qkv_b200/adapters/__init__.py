@@ -1,5 +1,1 @@
-"""Host adapters (vllm-ascend-hust)."""
-
-from .base import HostAdapter
-
-__all__ = ["HostAdapter"]
+"""Host integration (vllm-ascend-hust): the ``get_impl_cls`` dispatcher."""

@@ -1,5 +1,6 @@
-"""vllm-ascend-hust host adapter."""
+"""vllm-ascend-hust host: ``install_kv_impl_dispatch`` routes the quantized
+cache dtypes of ``AscendAttentionBackend.get_impl_cls`` to this package."""
 
-from .register import BACKEND_CLASS_PATH_BY_DTYPE, AscendHustAdapter
+from .backend import install_kv_impl_dispatch
 
-__all__ = ["AscendHustAdapter", "BACKEND_CLASS_PATH_BY_DTYPE"]
+__all__ = ["install_kv_impl_dispatch"]

@@ -1,5 +1,4 @@
-"""Quantisation methods; importing this package registers their metadata only."""
-
-from . import fp8_per_token_head, int8_dynamic, kivi_int4  # noqa: F401  (registration side effect)
-
-__all__ = ["fp8_per_token_head", "int8_dynamic", "kivi_int4"]
+"""The quantized KV cache methods: ``int8_dynamic`` (``--kv-cache-dtype
+int8``), ``kivi_int4`` and ``fp8_per_token_head``; each package holds the
+attention mixin and its layout rules. Importing this package imports none of
+them (and no torch)."""
