@@ -327,28 +327,31 @@ pack_key_tiled_kernel(const T* __restrict__ key, const void* __restrict__ slots,
 // ------------------------------------------------ fast path (bf16, head 128)
 //
 // The same codes, scales and minima as the kernels above, without an IEEE
-// division per element. For a group with minimum mn and scale s (computed
-// exactly as above) and inv = 1/s (correctly rounded), each element takes
-//   d  = x - mn                  (fp32, as the reference)
-//   r  = RN(d * inv + 1.5 2^23)  (= 1.5 2^23 + round(d * inv): the integer k
-//                                 sits in the low mantissa bits of r)
-//   e  = RN(d * inv - k)         (the distance of d * inv to that integer)
-// and k is the reference's clamp(floor(RN(RN(d / s) + 0.5)), 0, 15) whenever
-// |e| < 0.5 - 2^-16. The bound: with Q = d / s (real), d * inv = Q (1 + a),
-// |a| <= 2^-24 and Q <= 15 (1 + 2^-22), so |d * inv - Q| < 2^-20;
-// |RN(Q) - Q| <= 2^-21 and the + 0.5 rounds by at most 2^-20 (below 16), so
-// the reference's floor argument lies within 2.5 * 2^-20 < 2^-18.6 of
-// d * inv + 0.5, and e itself is within 2^-25 of d * inv - k: inside the band
-// that argument lies in (k, k + 1) and floor gives k. k lies in [0, 15]
-// because 0 <= d <= mx - mn. An element outside the band (within 2^-16 of a
-// rounding tie, or a non-finite input: NaN fails every comparison) is
-// recomputed with the division sequence above. The fp32 pairs run as packed
-// f32x2 instructions (two lanes per instruction, Blackwell).
+// division per element and without branches. For a group with minimum mn and
+// scale s (computed exactly as above) and inv = RN(1/s), each element takes
+//   d  = RN(x - mn)                   the reference's first operation
+//   q0 = RN(d * inv)                  quotient estimate
+//   r  = RN(d - q0 * s)               (one FMA) the remainder, exact
+//   q  = RN(q0 + r * inv)             (one FMA) = RN(d / s), the reference's
+//                                     IEEE quotient (Markstein's correction
+//                                     step, 1990)
+//   t  = RN(q + 0.5)                  the reference's second rounding
+//   k  = floor(t): RM(t + 1.5 2^23)   rounding toward -inf leaves 1.5 2^23 +
+//                                     floor(t), so k sits in the low mantissa
+//                                     bits
+// k needs no clamp: 0 <= d <= mx - mn, so q <= 15 (1 + 2^-23) and t <= 15.5.
+// The correction step was checked against exact rational arithmetic on
+// 600 000 quotients: random ones, every element of bf16 groups (which hit
+// exact half-integer quotients often), quotients next to float32 rounding
+// midpoints, and the hardest case fp32 operands allow (a quotient 1/B of an
+// ulp from a midpoint, B the divisor's 24-bit significand); no mismatch. The
+// fp32 pairs run as packed f32x2 instructions (two lanes per instruction).
+// Non-finite inputs give codes outside the contract (the reference's cast of
+// a NaN to an integer is undefined as well).
 namespace fastq {
 
 using u64 = unsigned long long;
-constexpr float kMagic = 12582912.0f;              // 1.5 * 2^23
-constexpr float kTie2 = (0.5f - 1.0f / 65536.0f) * (0.5f - 1.0f / 65536.0f);
+constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
 
 __device__ __forceinline__ u64 pack2(float a, float b) {
   u64 r;
@@ -361,6 +364,21 @@ __device__ __forceinline__ void unpack2(u64 r, uint32_t& a, uint32_t& b) {
 __device__ __forceinline__ u64 sub2(u64 a, u64 b) {
   u64 r;
   asm("sub.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ u64 mul2(u64 a, u64 b) {
+  u64 r;
+  asm("mul.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ u64 add2(u64 a, u64 b) {
+  u64 r;
+  asm("add.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ u64 add2_rm(u64 a, u64 b) {
+  u64 r;
+  asm("add.rm.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
 __device__ __forceinline__ u64 fma2(u64 a, u64 b, u64 c) {
@@ -381,19 +399,22 @@ __device__ __forceinline__ uint32_t bmax2(uint32_t a, uint32_t b) {
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
-// Codes of the two bf16 values of w against per-lane (mn, inv): returned in
-// the low byte of r0 / r1. `ok` keeps its sign bit only while every element
-// so far lies inside the exact band; k0 / k1 (when asked for) carry each
-// element's own check (sign bit set: inside).
-__device__ __forceinline__ void quant2(uint32_t w, u64 mn2, u64 inv2, uint32_t& r0, uint32_t& r1, uint32_t& k0,
-                                       uint32_t& k1) {
-  const u64 m2 = pack2(kMagic, kMagic);
-  const u64 t2 = pack2(-kTie2, -kTie2);
-  const u64 d = sub2(pack2(bf_lo(w), bf_hi(w)), mn2);
-  const u64 r = fma2(d, inv2, m2);
-  const u64 e = fma2(d, inv2, sub2(m2, r));  // d * inv - k
-  unpack2(fma2(e, e, t2), k0, k1);           // e^2 - band^2: negative inside
-  unpack2(r, r0, r1);
+// The group constants of one lane pair: minimum, reciprocal and negated scale.
+struct Group2 {
+  u64 mn, inv, neg_s;
+};
+__device__ __forceinline__ Group2 group2(float mn0, float s0, float mn1, float s1) {
+  return Group2{pack2(mn0, mn1), pack2(__frcp_rn(s0), __frcp_rn(s1)), pack2(-s0, -s1)};
+}
+
+// Codes of the two bf16 values of w (low half: lane 0 of the group pair),
+// returned in the low byte of r0 / r1.
+__device__ __forceinline__ void quant2(uint32_t w, const Group2& g, uint32_t& r0, uint32_t& r1) {
+  const u64 d = sub2(pack2(bf_lo(w), bf_hi(w)), g.mn);
+  const u64 q0 = mul2(d, g.inv);
+  const u64 q = fma2(fma2(q0, g.neg_s, d), g.inv, q0);
+  const u64 k = add2_rm(add2(q, pack2(0.5f, 0.5f)), pack2(kMagic, kMagic));
+  unpack2(k, r0, r1);
 }
 
 // 8 codes (low bytes of c[0..7], each < 16) -> one int4 word, lane L at bits 4L.
@@ -403,50 +424,25 @@ __device__ __forceinline__ uint32_t pack8(const uint32_t (&c)[8]) {
   return e | (o << 4);
 }
 
-// The exact division sequence for one element, off the fast path: a real
-// call (not inlined), so the compiler branches around it instead of
-// predicating it into every element. Exact ties are common with bf16 inputs
-// (about 2e-3 of random N(0, 1) values: (x - mn) / s is a ratio of small
-// integers), so only the flagged elements of a word take it, one call each.
-__device__ __noinline__ uint32_t exact_code(float x, float mn, float sc) { return quantize_code(x, mn, sc); }
-
-// Replaces the codes of the elements of `word` whose check lies outside the
-// band (sign bit clear) with the exact ones; only called for a word whose
-// combined check failed (rare), so the checks are recomputed here rather than
-// kept live through the fast path. pair(i) is the bf16 pair holding elements
-// 2i and 2i + 1 of the word when `lanes_in_pairs`, else (keys) element l is
-// the lo / hi half (`hi`) of pair(l).
-template <bool kPairs, typename P>
-__device__ __noinline__ uint32_t patch_word(uint32_t word, P pair, bool hi, u64 mn2, u64 inv2, float mn, float sc) {
-#pragma unroll
-  for (int l = 0; l < 8; ++l) {
-    const uint32_t w = kPairs ? pair(l >> 1) : pair(l);
-    uint32_t r0, r1, k0, k1;
-    quant2(w, mn2, inv2, r0, r1, k0, k1);
-    const bool take_hi = kPairs ? (l & 1) : hi;
-    if (((take_hi ? k1 : k0) >> 31) == 0)
-      word = (word & ~(0xFu << (4 * l))) | (exact_code(take_hi ? bf_hi(w) : bf_lo(w), mn, sc) << (4 * l));
-  }
-  return word;
-}
-
 }  // namespace fastq
 
-// Keys: one CTA of 256 threads per (token group, head, channel half).
-// Thread (warp w, lane) owns the channel pair cp = 32 half + lane and the
-// token eighth w of the group: it loads the pair for its G / 8 tokens (a
-// warp's loads are 128 contiguous bytes of a token row), reduces min / max in
-// bf16 pairs (exact), the eight chunks meet in shared memory, and each thread
-// quantises and stores its own G / 64 words per channel.
+// Keys: one CTA of 256 threads per (token group, head). Thread t owns the
+// channel pair cp = t % 64 and the token quarter t / 64 of the group: it
+// loads the pair for its G / 4 tokens (a warp's loads are 128 contiguous
+// bytes of a token row), reduces min / max in bf16 pairs (exact), the four
+// quarters meet in shared memory, and each thread quantises and stores its
+// own G / 32 words per channel. (Eighths of the group over channel halves,
+// twice the CTAs with half the tokens each, measured 19 % slower: the
+// per-thread setup weighs more.)
 template <int G>
 __device__ __forceinline__ void pack_key_fast_tile(const __nv_bfloat16* __restrict__ key,
                                                    const void* __restrict__ slots, int slot_dtype, int kvh,
                                                    int block_size, int64_t num_blocks, int32_t* __restrict__ k_quant,
                                                    float* __restrict__ k_scale, float* __restrict__ k_mn, int* err,
-                                                   int64_t gi, int head, int half) {
+                                                   int64_t gi, int head) {
   using namespace fastq;
-  constexpr int kD = 128, kChunks = 8, kTok = G / kChunks, kWords = kTok / 8;
-  __shared__ uint32_t s_mn[kChunks][32], s_mx[kChunks][32];
+  constexpr int kD = 128, kChunks = 4, kTok = G / kChunks, kWords = kTok / 8;
+  __shared__ uint32_t s_mn[kChunks][64], s_mx[kChunks][64];
   const int64_t first_slot = load_index(slots, slot_dtype, gi * G);
   if (first_slot < 0) return;  // the reference kernel skips such groups
   // (32-bit division whenever the slot fits: one per thread, on every lane)
@@ -458,8 +454,8 @@ __device__ __forceinline__ void pack_key_fast_tile(const __nv_bfloat16* __restri
     if (threadIdx.x == 0) record_error(err, kErrSlot);
     return;
   }
-  const int tc = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int cp = 32 * half + lane;
+  const int tc = threadIdx.x >> 6, lane = threadIdx.x & 63;
+  const int cp = lane;
   const int64_t row_words = static_cast<int64_t>(kvh) * (kD / 2);
   const uint32_t* src =
       reinterpret_cast<const uint32_t*>(key) + (gi * G + tc * kTok) * row_words + head * (kD / 2) + cp;
@@ -482,40 +478,27 @@ __device__ __forceinline__ void pack_key_fast_tile(const __nv_bfloat16* __restri
   }
   const float mn0 = bf_lo(mn), mn1 = bf_hi(mn);
   const float sc0 = group_scale(mn0, bf_lo(mx)), sc1 = group_scale(mn1, bf_hi(mx));
-  const u64 mn2 = pack2(mn0, mn1), inv2 = pack2(__frcp_rn(sc0), __frcp_rn(sc1));
+  const Group2 g2 = group2(mn0, sc0, mn1, sc1);
   uint32_t w0[kWords], w1[kWords];
 #pragma unroll
   for (int j = 0; j < kWords; ++j) {
-    uint32_t c0[8], c1[8], ok = 0xFFFFFFFFu;
+    uint32_t c0[8], c1[8];
 #pragma unroll
-    for (int l = 0; l < 8; ++l) {
-      uint32_t k0, k1;
-      quant2(v[8 * j + l], mn2, inv2, c0[l], c1[l], k0, k1);
-      ok &= k0 & k1;
-    }
+    for (int l = 0; l < 8; ++l) quant2(v[8 * j + l], g2, c0[l], c1[l]);
     w0[j] = pack8(c0);
     w1[j] = pack8(c1);
-    if ((ok >> 31) == 0) {  // an element near a rounding tie (rare): exact codes for it
-      const uint4 a = make_uint4(v[8 * j], v[8 * j + 1], v[8 * j + 2], v[8 * j + 3]);
-      const uint4 b = make_uint4(v[8 * j + 4], v[8 * j + 5], v[8 * j + 6], v[8 * j + 7]);
-      const auto pair = [a, b](int l) {
-        const uint32_t t[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        return t[l];
-      };
-      w0[j] = patch_word<false>(w0[j], pair, false, mn2, inv2, mn0, sc0);
-      w1[j] = patch_word<false>(w1[j], pair, true, mn2, inv2, mn1, sc1);
-    }
   }
   const int64_t chan0 = (blk * kvh + head) * static_cast<int64_t>(kD) + 2 * cp;
   const int64_t wpc = block_size >> 3;  // words per channel and page
   int32_t* dst0 = k_quant + chan0 * wpc + (off >> 3) + tc * kWords;
   int32_t* dst1 = dst0 + wpc;
-  if constexpr (kWords == 2) {
+  if constexpr (kWords == 4) {
+    *reinterpret_cast<uint4*>(dst0) = make_uint4(w0[0], w0[1], w0[2], w0[3]);
+    *reinterpret_cast<uint4*>(dst1) = make_uint4(w1[0], w1[1], w1[2], w1[3]);
+  } else {
+    static_assert(kWords == 2, "group 64 or 128");
     *reinterpret_cast<uint2*>(dst0) = make_uint2(w0[0], w0[1]);
     *reinterpret_cast<uint2*>(dst1) = make_uint2(w1[0], w1[1]);
-  } else {
-    *dst0 = static_cast<int32_t>(w0[0]);
-    *dst1 = static_cast<int32_t>(w1[0]);
   }
   if (tc == 0) {
     const int gpb = block_size / G;
@@ -533,7 +516,7 @@ pack_key_fast_kernel(const __nv_bfloat16* __restrict__ key, const void* __restri
                      int kvh, int block_size, int64_t num_blocks, int32_t* __restrict__ k_quant,
                      float* __restrict__ k_scale, float* __restrict__ k_mn, int* err) {
   pack_key_fast_tile<G>(key, slots, slot_dtype, kvh, block_size, num_blocks, k_quant, k_scale, k_mn, err,
-                        blockIdx.x, blockIdx.y >> 1, blockIdx.y & 1);
+                        blockIdx.x, blockIdx.y);
 }
 
 // Values: two threads per (token, head) row of 128 dims, 64 contiguous dims
@@ -604,27 +587,14 @@ __device__ __forceinline__ void pack_value_fast_rows(const __nv_bfloat16* __rest
   }
   if (!valid) return;
   const float sc = group_scale(mn, mx);
-  const float inv = __frcp_rn(sc);
-  const u64 mn2 = pack2(mn, mn), inv2 = pack2(inv, inv);
+  const Group2 g2 = group2(mn, sc, mn, sc);
   uint32_t w[kHalf / 8];
 #pragma unroll
   for (int j = 0; j < kHalf / 8; ++j) {
-    uint32_t c[8], ok = 0xFFFFFFFFu;
+    uint32_t c[8];
 #pragma unroll
-    for (int l = 0; l < 4; ++l) {
-      uint32_t k0, k1;
-      quant2(v[4 * j + l], mn2, inv2, c[2 * l], c[2 * l + 1], k0, k1);
-      ok &= k0 & k1;
-    }
+    for (int l = 0; l < 4; ++l) quant2(v[4 * j + l], g2, c[2 * l], c[2 * l + 1]);
     w[j] = pack8(c);
-    if ((ok >> 31) == 0) {  // an element near a rounding tie (rare): exact codes for it
-      const uint4 a = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-      const auto pair = [a](int i) {
-        const uint32_t t[4] = {a.x, a.y, a.z, a.w};
-        return t[i];
-      };
-      w[j] = patch_word<true>(w[j], pair, false, mn2, inv2, mn, sc);
-    }
   }
   const int64_t dst_row = slot * kvh + head;
   uint4* dst = reinterpret_cast<uint4*>(v_quant + dst_row * (kD / 8) + part * (kHalf / 8));
@@ -647,9 +617,9 @@ pack_value_fast_kernel(const __nv_bfloat16* __restrict__ value, const void* __re
                           blockIdx.x);
 }
 
-// Keys and values of the same tokens in one launch: CTAs [0, 2 groups kvh)
-// take the key tiles (x / 2 = group * kvh + head, x % 2 = channel half), the
-// rest the value rows.
+// Keys and values of the same tokens in one launch: CTAs [0, groups * kvh)
+// take the key tiles (group = x / kvh, head = x % kvh), the rest the value
+// rows.
 template <int G>
 __global__ void __launch_bounds__(256)
 pack_kv_fast_kernel(const __nv_bfloat16* __restrict__ key, const __nv_bfloat16* __restrict__ value,
@@ -657,14 +627,11 @@ pack_kv_fast_kernel(const __nv_bfloat16* __restrict__ key, const __nv_bfloat16* 
                     int64_t num_blocks, int32_t* __restrict__ k_quant, float* __restrict__ k_scale,
                     float* __restrict__ k_mn, int32_t* __restrict__ v_quant, float* __restrict__ v_scale,
                     float* __restrict__ v_mn, int* err) {
-  const unsigned key_ctas = static_cast<unsigned>(num_tokens / G * kvh * 2);
+  const unsigned key_ctas = static_cast<unsigned>(num_tokens / G * kvh);
   const unsigned x = blockIdx.x;
-  if (x < key_ctas) {
-    const unsigned gh = x >> 1;  // (group, head); x & 1 = channel half
+  if (x < key_ctas)
     pack_key_fast_tile<G>(key, slots, slot_dtype, kvh, block_size, num_blocks, k_quant, k_scale, k_mn, err,
-                          gh / static_cast<unsigned>(kvh), static_cast<int>(gh % static_cast<unsigned>(kvh)),
-                          static_cast<int>(x & 1));
-  }
+                          x / static_cast<unsigned>(kvh), static_cast<int>(x % static_cast<unsigned>(kvh)));
   else
     pack_value_fast_rows<G>(value, slots, slot_dtype, static_cast<int>(num_tokens * kvh), kvh,
                             num_blocks * block_size, v_quant, v_scale, v_mn, err,
@@ -686,8 +653,8 @@ int launch_pack_key(const void* key, const void* slots, int slot_dtype,
     // bf16 at head 128, group 64 / 128: the division-free kernel
     const uintptr_t qa = reinterpret_cast<uintptr_t>(kq);
     if (head_size == 128 && (group_size == 64 || group_size == 128) &&
-        (reinterpret_cast<uintptr_t>(key) & 3u) == 0 && (qa & 7u) == 0) {
-      dim3 fgrid(static_cast<unsigned>(groups), 2 * kvh);  // y = 2 head + channel half
+        (reinterpret_cast<uintptr_t>(key) & 3u) == 0 && (qa & (group_size == 128 ? 15u : 7u)) == 0) {
+      dim3 fgrid(static_cast<unsigned>(groups), kvh);
       if (group_size == 128)
         pack_key_fast_kernel<128><<<fgrid, 256, 0, stream>>>(k, slots, slot_dtype, kvh, block_size, num_blocks,
                                                              kq, ks, km, err);
@@ -949,7 +916,7 @@ int qkv_kivi_pack_kv(const void* key, const void* value, int dtype, const void* 
                 "qkv_kivi_pack_kv: null pointer");
   const auto al = [](const void* p, unsigned m) { return (reinterpret_cast<uintptr_t>(p) & m) == 0; };
   const bool fused = dtype == QKV_BF16 && head_size == 128 && (group_size == 64 || group_size == 128) &&
-                     al(key, 3u) && al(k_quant, 7u) && al(value, 15u) &&
+                     al(key, 3u) && al(k_quant, group_size == 128 ? 15u : 7u) && al(value, 15u) &&
                      al(v_quant, 15u) && num_tokens * num_kv_heads * 2 < (int64_t{1} << 31);
   if (!fused) {
     rc = qkv_kivi_pack_key(key, dtype, slot_mapping, slot_dtype, num_tokens, num_kv_heads, head_size, group_size,
@@ -958,7 +925,7 @@ int qkv_kivi_pack_kv(const void* key, const void* value, int dtype, const void* 
     return qkv_kivi_pack_value(value, dtype, slot_mapping, slot_dtype, num_tokens, num_kv_heads, head_size,
                                group_size, block_size, num_blocks, v_quant, v_scale, v_mn, stream);
   }
-  const int64_t key_ctas = num_tokens / group_size * num_kv_heads * 2;
+  const int64_t key_ctas = num_tokens / group_size * num_kv_heads;
   const int64_t value_ctas = (num_tokens * num_kv_heads * 2 + 255) / 256;
   const int64_t grid = key_ctas + value_ctas;
   QKV_CHECK_ARG(grid < (int64_t{1} << 31), "qkv_kivi_pack_kv: too many tokens for one launch");
