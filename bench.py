@@ -74,6 +74,9 @@ def parse():
                          "parity check of sampled requests)")
     ap.add_argument("--no-int8", action="store_true", help="skip the config-3 INT8 leg")
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 chunked-prefill leg")
+    ap.add_argument("--shard", type=int, default=None,
+                    help="with --only kivi: build rank 0's share of an N-way KV-head shard on this one GPU "
+                         "(the per-GPU decode of an N-GPU run)")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the request count (small cases for ncu captures)")
     ap.add_argument("--only", choices=("kivi", "int8", "config4", "fp8", "small", "pack"), default=None,
@@ -1195,7 +1198,10 @@ def main():
         if rank == 0:
             print(json.dumps({"only": "fp8", **res}), flush=True)
         return
-    w = build_workload(cfg, rank, world, device)
+    if args.only == "kivi" and args.shard:
+        w = build_workload(cfg, 0, args.shard, device)
+    else:
+        w = build_workload(cfg, rank, world, device)
     out = torch.empty(w.B, w.Hql, w.D, dtype=torch.bfloat16, device=device)
     peer = None
     if world > 1:
@@ -1220,7 +1226,7 @@ def main():
 
     if args.only == "kivi":
         decode_ms = time_loop(decode, args.steps, args.warmup, device)
-        print(json.dumps({"only": "kivi", "batch": w.B, "decode_ms": decode_ms,
+        print(json.dumps({"only": "kivi", "batch": w.B, "kv_heads": w.Hl, "decode_ms": decode_ms,
                           "gbs": algorithmic_bytes(w) / (decode_ms * 1e-3) / 1e9}), flush=True)
         return
     # warm-up on a side stream (allocator, NCCL communicators, kernel

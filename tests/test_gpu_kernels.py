@@ -10,8 +10,9 @@ where bf16 cannot resolve 1e-2 (|want| >= 2: the outputs are bf16), the
 ``attention_error`` rule of the oracle. The INT8 kernels reproduce the
 reference's bf16 ``code * aq`` exactly; the KIVI decode kernel uses the
 exact ``code * scale + min`` (the rounding to bf16 would cost it several
-instructions per code), so KIVI outputs are also held to the same bound
-against the fp32-dequantised variant."""
+instructions per code), so KIVI outputs are held to the bound against the
+fp32-dequantised variant, and against the bf16-cast one wherever the two
+reference variants agree within the bound (``assert_kivi_close``)."""
 
 from __future__ import annotations
 
@@ -30,6 +31,19 @@ def assert_attention_close(got: np.ndarray, want: np.ndarray, atol: float = O.AT
     e = O.attention_error(got, want, atol)
     assert e["within_bound"], e
     return e["max_abs"]
+
+
+def assert_kivi_close(got: np.ndarray, want_cast: np.ndarray, want_fp32: np.ndarray) -> None:
+    """KIVI decode outputs: within the bound of the fp32-dequantised result
+    (the arithmetic the kernel performs), and of the reference's bf16-cast
+    result wherever the two reference variants agree within the bound
+    themselves. On short contexts with x10 outlier keys the cast alone moves
+    the reference by more than 1e-2 (0.016 on the 3..129-token case, 0.014
+    on the 2000-token GQA-8 case); the benchmarked configs 2, 4 and 5 are
+    held to the bf16-cast result outright (tests/test_gpu_configs.py)."""
+    assert_attention_close(got, want_fp32)
+    if O.attention_error(O.bf16_round(want_fp32), want_cast)["within_bound"]:
+        assert_attention_close(got, want_cast)
 
 
 def dev():
@@ -369,8 +383,8 @@ def test_kivi_paged_decode_vs_oracle(lens, k_res, v_res, Hq, H, D, g, blk, cap):
     kw = [[res_k[state[b, 0], (state[b, 1] + i) % cap] for i in range(k_res[b])] or None for b in range(B)]
     vw = [[res_v[state[b, 0], (state[b, 3] + i) % cap] for i in range(v_res[b])] or None for b in range(B)]
     got = to_np(out)
-    for cast in (True, False):
-        assert_attention_close(got, O.kivi_decode_reference(views, bt, lens, kw, vw, q, g, scale, target_bf16=cast))
+    assert_kivi_close(got, *(O.kivi_decode_reference(views, bt, lens, kw, vw, q, g, scale, target_bf16=cast)
+                             for cast in (True, False)))
     assert_no_device_error()
 
 
@@ -388,9 +402,8 @@ def test_kivi_decode_without_window_vs_oracle():
     kivi_paged_decode(bf16_tensor(q), tv, None, None, torch.from_numpy(bt).to(dev()),
                       torch.tensor(lens, dtype=torch.int32, device=dev()), None, g, D ** -0.5, out, max(lens))
     # keys past the last whole group stay zero codes in both views and oracle
-    for cast in (True, False):
-        want = O.kivi_decode_reference(views, bt, lens, [None] * B, [None] * B, q, g, D ** -0.5, target_bf16=cast)
-        assert_attention_close(to_np(out), want)
+    assert_kivi_close(to_np(out), *(O.kivi_decode_reference(views, bt, lens, [None] * B, [None] * B, q, g,
+                                                              D ** -0.5, target_bf16=cast) for cast in (True, False)))
     assert_no_device_error()
 
 
