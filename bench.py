@@ -1284,6 +1284,10 @@ def main():
     ke.record()
     torch.cuda.synchronize(device)
     decode_ms = ks.elapsed_time(ke) / args.steps
+    if peer is None:
+        # on one GPU the step IS the decode call (same graph work): one
+        # measurement for both, so the kernel time cannot exceed the step's
+        decode_ms = ms
     # graphs holding NCCL work are released before the process group goes
     del step_graph, decode_graph
     t = torch.tensor([ms, decode_ms], dtype=torch.float64, device=device)

@@ -85,6 +85,8 @@ struct __align__(1024) PageShared {
   PageStage<NG> st[kStages];
   uint4 qf[2][NG][kWarps][32];     // Q' B fragments: [buffer][group][k-step pair][lane]
   float cmn[2][NG][kWarps][kHeads];  // partial sum_d q k_mn: [buffer][group][k-step pair][head]
+  float vsv[2][kBlk * NG];           // the page's value scales / minima, copied out of the
+  float vmv[2][kBlk * NG];           // stage so it can refill while the page is computed
   unsigned long long full[kStages];
   int pid[kMaxPages];
 };
@@ -332,10 +334,17 @@ static_assert(sizeof(float) * (kTailBlock * (kTailLd + kD + kHeads) + 3 * kHeads
 
 // ------------------------------------------------------------ the kernel
 
-// 5 CTAs per SM for group 128; group 64 fits 4 (shared memory), which leaves
-// its larger register state room
-template <int NG>
-__global__ void __launch_bounds__(kThreads, NG == 1 ? 5 : 4)
+// Two schedules of the same page pipeline:
+//  kEarly = false (large decodes): 5 CTAs per SM for group 128 (4 for group
+//   64, shared memory); a page's stage refills after the page is computed,
+//   so one page is in flight while another is computed.
+//  kEarly = true (small decodes, where one page in flight per CTA leaves DRAM
+//   idle): 4 CTAs per SM; a page's code fragments go to registers (ldmatrix)
+//   and its value scales to a small side buffer before the CTA barrier, so
+//   its stage refills at once and both stages are in flight while the page
+//   is computed (32 more registers per thread).
+template <int NG, bool kEarly>
+__global__ void __launch_bounds__(kThreads, (NG == 1 && !kEarly) ? 5 : 4)
 kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tmap_k,
                        const __grid_constant__ CUtensorMap tmap_v) {
   extern __shared__ unsigned char smem_dyn[];
@@ -418,8 +427,9 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
     }
   };
 
+  constexpr int kAhead = kEarly ? kStages : kStages - 1;  // pages issued before the loop
 #pragma unroll
-  for (int i = 0; i < kStages - 1; ++i)
+  for (int i = 0; i < kAhead; ++i)
     if (i < n_pages) issue(i);
 
   // ---- per-warp running state: heads 2t, 2t+1 of this thread
@@ -458,7 +468,25 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
     const PageStage<NG>& st = sh.st[s];
     const int pg = sh.pid[i];
     const int qb = i & 1;
+    // the page's key / value code fragments of this lane: matrices m = 0..3
+    // of key block kp are channels 32 kp + 8 m .. + 7 (rows) x token quads
+    // (columns); value block db is tokens {4r + d} x 32 dims of dim block db
+    uint32_t kx[4][4], vx[4][4];
+    const auto load_frags = [&]() {
+#pragma unroll
+      for (int kp = 0; kp < 4; ++kp) {
+        ldsm_x4_t(kx[kp], reinterpret_cast<const unsigned char*>(&st.k[0][0]) + kro[kp]);
+        ldsm_x4_t(vx[kp], reinterpret_cast<const unsigned char*>(&st.v[0][0]) + vro[kp]);
+      }
+    };
     if (pg >= 0 && ok) {
+      if constexpr (kEarly) {
+        load_frags();
+        for (int e = tid; e < kBlk * NG; e += kThreads) {
+          sh.vsv[qb][e] = st.vs[e];
+          sh.vmv[qb][e] = st.vm[e];
+        }
+      }
       // Q' entries of k-steps 2 warp, 2 warp + 1 (lane = fragment owner)
 #pragma unroll
       for (int gq = 0; gq < NG; ++gq) {
@@ -489,7 +517,9 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
       break;
     }
     consumed = i + 1;
-    if (i + kStages - 1 < n_pages) issue(i + kStages - 1);
+    // early: every warp holds page i in registers, so its stage refills now;
+    // otherwise the stage of page i - 1 does
+    if (i + kAhead < n_pages) issue(i + kAhead);
     if (pg < 0) continue;
     const int pos0 = t0 + i * kBlk;
     const int valid = min(kBlk, t1 - pos0) - kTokW * warp;  // live tokens of this warp
@@ -524,13 +554,12 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
     for (int j = 0; j < 2; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
 #pragma unroll
     for (int kp = 0; kp < 4; ++kp) {
-      // matrices m = 0..3: channels 32 kp + 8 m .. + 7 (rows), token quads (columns)
-      uint32_t kx[4];
-      ldsm_x4_t(kx, reinterpret_cast<const unsigned char*>(&st.k[0][0]) + kro[kp]);
+      if constexpr (!kEarly)  // late schedule: fragments straight from the stage, next to their use
+        ldsm_x4_t(kx[kp], reinterpret_cast<const unsigned char*>(&st.k[0][0]) + kro[kp]);
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int kk = 2 * kp + e;
-        const uint32_t x0 = kx[2 * e], x1 = kx[2 * e + 1];
+        const uint32_t x0 = kx[kp][2 * e], x1 = kx[kp][2 * e + 1];
         mma16816(sc[0], nib_lo_sub(x0), nib_hi_sub(x0), nib_lo_sub(x1), nib_hi_sub(x1), bq[kk][0], bq[kk][1]);
         const uint32_t y0 = prmt(x0, x0, 0x0301u), y1 = prmt(x1, x1, 0x0301u);
         mma16816(sc[1], nib_lo_sub(y0), nib_hi_sub(y0), nib_lo_sub(y1), nib_hi_sub(y1), bq[kk][0], bq[kk][1]);
@@ -594,8 +623,8 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
 
     // ---- probabilities -> P'^T B fragments (per value group), v_mn terms
     uint32_t pb[2][NG][2];
-    const float* vsw = &st.vs[kTokW * warp * NG];
-    const float* vmw = &st.vm[kTokW * warp * NG];
+    const float* vsw = kEarly ? &sh.vsv[qb][kTokW * warp * NG] : &st.vs[kTokW * warp * NG];
+    const float* vmw = kEarly ? &sh.vmv[qb][kTokW * warp * NG] : &st.vm[kTokW * warp * NG];
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       float pr[4];
@@ -649,12 +678,11 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
     // dims 32 db + 4g + 2s and + 1.
 #pragma unroll
     for (int db = 0; db < 4; ++db) {
-      uint32_t vx[4];
-      ldsm_x4_t(vx, reinterpret_cast<const unsigned char*>(&st.v[0][0]) + vro[db]);
+      if constexpr (!kEarly) ldsm_x4_t(vx[db], reinterpret_cast<const unsigned char*>(&st.v[0][0]) + vro[db]);
       const int gg = NG == 2 ? (db >> 1) : 0;
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        const uint32_t x0 = vx[2 * j], x1 = vx[2 * j + 1];
+        const uint32_t x0 = vx[db][2 * j], x1 = vx[db][2 * j + 1];
         mma16816(o[2 * db], nib_lo_sub(x0), nib_hi_sub(x0), nib_lo_sub(x1), nib_hi_sub(x1), pb[j][gg][0],
                  pb[j][gg][1]);
         const uint32_t y0 = prmt(x0, x0, 0x0301u), y1 = prmt(x1, x1, 0x0301u);
@@ -667,7 +695,7 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
   if (aborted) {
     // let the copies still in flight land before the shared memory is reused
     if (tid == 0)
-      for (int i = consumed; i < min(n_pages, consumed + kStages - 1); ++i)
+      for (int i = consumed; i < min(n_pages, consumed + kAhead); ++i)
         (void)mbar_wait(&sh.full[i % kStages], static_cast<uint32_t>((i / kStages) & 1));
   }
   __syncthreads();
@@ -767,14 +795,14 @@ int encode_maps(const DecodeParams& p, CUtensorMap* tk, CUtensorMap* tv) {
   return QKV_OK;
 }
 
-template <int NG>
+template <int NG, bool kEarly>
 int set_smem_attr() {
   int dev = 0;
   cudaGetDevice(&dev);
   static std::atomic<uint64_t> done{0};
   const uint64_t bit = 1ull << (dev & 63);
   if ((done.load() & bit) == 0) {
-    const cudaError_t e = cudaFuncSetAttribute(kivi_decode_tma_kernel<NG>,
+    const cudaError_t e = cudaFuncSetAttribute(kivi_decode_tma_kernel<NG, kEarly>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                static_cast<int>(kivi_smem_bytes<NG>()));
     if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(kivi_decode_tma_kernel)");
@@ -797,13 +825,21 @@ bool kivi_tma_supported(const DecodeParams& p) {
          al(p.km, 16) && al(p.vs, 8) && al(p.vm, 8);
 }
 
+// Unit-pages (requests x kv heads x pages per request) up to which the early
+// refill schedule runs: measured on config 5's shapes, it wins at 8192
+// (0.049 vs 0.053 ms) and 16384 (0.087 vs 0.088) and loses at 32768 (0.156
+// vs 0.148) and 65536 (0.283 vs 0.267).
+constexpr long long kEarlyMaxUnitPages = 16384;
+
+bool kivi_early(long long units, long long pages) { return units * pages <= kEarlyMaxUnitPages; }
+
 // CTAs of the page-pipelined kernel resident per SM: the launch bounds (5 for
-// group 128, 4 for group 64) or shared memory, whichever is lower.
-int kivi_tma_ctas_per_sm(int group) {
+// group 128 on the late schedule, else 4) or shared memory, whichever is lower.
+int kivi_tma_ctas_per_sm(int group, bool early) {
   constexpr int kSmemPerSm = 228 * 1024, kReservedPerCta = 1024;
   const int per = static_cast<int>(group == 128 ? kivi_smem_bytes<1>() : kivi_smem_bytes<2>()) +
                   kReservedPerCta;
-  const int by_smem = kSmemPerSm / per, by_regs = group == 128 ? 5 : 4;
+  const int by_smem = kSmemPerSm / per, by_regs = (group == 128 && !early) ? 5 : 4;
   return by_smem < by_regs ? by_smem : by_regs;
 }
 
@@ -815,7 +851,7 @@ SplitPlan plan_kivi_tma(int batch, int kvh, int group, int max_seq_len, int sms)
   SplitPlan plan;
   const int pages = max_seq_len > 0 ? (max_seq_len + kBlk - 1) / kBlk : 1;
   const int units = batch * kvh > 0 ? batch * kvh : 1;
-  const int resident = sms * kivi_tma_ctas_per_sm(group);
+  const int resident = sms * kivi_tma_ctas_per_sm(group, kivi_early(units, pages));
   const int s_min = (pages + kMaxPages - 1) / kMaxPages;
   int s_max = (8 * resident + units - 1) / units;
   s_max = s_max < s_min ? s_min : s_max;
@@ -851,13 +887,20 @@ int launch_kivi_tma(const DecodeParams& p0, cudaStream_t stream, bool combine, i
   int rc = encode_maps(p, &tk, &tv);
   if (rc != QKV_OK) return rc;
   dim3 grid(p.splits_total, p.kvh, p.batch);
+  // the plan's pages per request: history splits x pages per split
+  const bool early = kivi_early(static_cast<long long>(p.batch) * p.kvh,
+                                static_cast<long long>(p.num_hist_splits) * (p.split_tokens / kBlk));
+#define QKV_KIVI_LAUNCH(NG, EARLY)                                                      \
+  do {                                                                                  \
+    if ((rc = set_smem_attr<NG, EARLY>()) != QKV_OK) return rc;                         \
+    kivi_decode_tma_kernel<NG, EARLY><<<grid, kThreads, kivi_smem_bytes<NG>(), stream>>>(p, tk, tv); \
+  } while (0)
   if (p.group == 128) {
-    if ((rc = set_smem_attr<1>()) != QKV_OK) return rc;
-    kivi_decode_tma_kernel<1><<<grid, kThreads, kivi_smem_bytes<1>(), stream>>>(p, tk, tv);
+    if (early) QKV_KIVI_LAUNCH(1, true); else QKV_KIVI_LAUNCH(1, false);
   } else {
-    if ((rc = set_smem_attr<2>()) != QKV_OK) return rc;
-    kivi_decode_tma_kernel<2><<<grid, kThreads, kivi_smem_bytes<2>(), stream>>>(p, tk, tv);
+    if (early) QKV_KIVI_LAUNCH(2, true); else QKV_KIVI_LAUNCH(2, false);
   }
+#undef QKV_KIVI_LAUNCH
   QKV_CHECK_LAUNCH("kivi_decode_tma_kernel");
   if (p.splits_total > 1 && combine) {
     launch_combine(p, stream);
