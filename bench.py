@@ -310,9 +310,10 @@ def run_reference(args):
         "data": "synthetic",
         "config": workload_config(cfg, args.gpus),
         "cpu_baseline": {
-            "value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+            "value": value, "unit": UNIT, "kind": "port",
             "sample": "one request of the workload per step (context 32768, 64 q / 8 kv heads); the CPU path is "
                       "linear in requests, so tokens/s/layer of the sample is that of the full batch",
+            **cpu_info(),
         },
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
