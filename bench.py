@@ -633,7 +633,7 @@ def run_small_configs(device, args):
     out["config1"] = {"workload": "BASELINE config 1: INT8, 4 requests at 512/1024/1536/2048, Hq 32 / KVH 8",
                       "ms_per_step": ms, "tokens_per_s_per_layer": len(lens) / (ms * 1e-3), "bytes_per_launch": by,
                       "hbm_gbs": by / (ms * 1e-3) / 1e9, "frac_of_measured_hbm": by / (ms * 1e-3) / 1e9 / peak,
-                      "l2": "256 MB buffer written before every timed step", "parity": parity1}
+                      "l2": "flushed: 256 MB written, then another 256 MB read, before every timed step", "parity": parity1}
     # ---- config 2
     c2 = build_config2(device)
     o = torch.empty_like(c2.q)
@@ -650,7 +650,7 @@ def run_small_configs(device, args):
                       "lens": c2.lens, "ms_per_step": ms, "tokens_per_s_per_layer": len(c2.lens) / (ms * 1e-3),
                       "bytes_per_launch": by, "hbm_gbs": by / (ms * 1e-3) / 1e9,
                       "frac_of_measured_hbm": by / (ms * 1e-3) / 1e9 / peak,
-                      "l2": "256 MB buffer written before every timed step", "parity": parity2}
+                      "l2": "flushed: 256 MB written, then another 256 MB read, before every timed step", "parity": parity2}
     return out
 
 
@@ -783,11 +783,17 @@ def time_loop(fn, steps, warmup, device):
 
 def time_loop_flushed(fn, steps, warmup, device):
     """ms per call of ``fn`` for workloads that fit in L2: before every timed
-    replay a 256 MB buffer (twice the 126 MB L2) is written, and only the
-    replay itself sits between that step's CUDA events."""
+    replay a 256 MB buffer (twice the 126 MB L2) is written and a second
+    256 MB buffer is read, and only the replay itself sits between that
+    step's CUDA events. The read evicts the written lines, so their write-back
+    to HBM happens before the timed replay and the L2 it starts from holds
+    clean lines of neither the workload nor the flush (the state ncu's cache
+    control gives a profiled launch); with the write alone, up to 126 MB of
+    dirty flush lines would be written back during the timed replay."""
     import torch
 
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    clean = torch.zeros(32 << 20, dtype=torch.int64, device=device)
     side = torch.cuda.Stream(device)
     side.wait_stream(torch.cuda.current_stream(device))
     with torch.cuda.stream(side):
@@ -803,6 +809,7 @@ def time_loop_flushed(fn, steps, warmup, device):
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     for s, e in ev:
         flush.zero_()
+        clean.sum()
         s.record()
         graph.replay()
         e.record()

@@ -292,6 +292,44 @@ def test_kivi_pack_kv_equals_the_two_packs(group, dtype):
     assert_no_device_error()
 
 
+@pytest.mark.parametrize(
+    "group,H,groups,slot_dtype",
+    [(128, 8, 64, np.int64), (64, 3, 7, np.int32), (128, 1, 3, np.int64), (64, 8, 50, np.int64),
+     (128, 5, 301, np.int32)],
+)
+def test_kivi_pack_kv_fused_kernel_matches_oracle(group, H, groups, slot_dtype):
+    """The one-launch pack of both sides (bf16, head 128) against the oracle's
+    packers, bit for bit: a ragged last value CTA (tokens x heads not a
+    multiple of 128 rows), padding groups (every slot -1: the key group and
+    its value rows are skipped; the host validator, which rejects them, is
+    bypassed), int32 and int64 slot maps, and grids of up to 3000 CTAs."""
+    from qkv_b200.ops import kivi_pack_kv_cache
+
+    rng = np.random.default_rng(group * 31 + H * 7 + groups)
+    D, blk = 128, 128
+    T = groups * group
+    key = kv_data(rng, T, H, D, 0.02, 10.0)
+    value = kv_data(rng, T, H, D, 0.0, 1.0)
+    gpb = blk // group
+    nb = (groups + gpb - 1) // gpb + 3
+    gslots = rng.permutation(nb * gpb)[:groups]  # group-aligned destinations, pages shuffled
+    gslots[rng.random(groups) < 0.15] = -1  # padding groups
+    slots = np.where(gslots[np.arange(T) // group] < 0, -1,
+                     gslots[np.arange(T) // group] * group + np.arange(T) % group).astype(slot_dtype)
+    views = _empty_views(nb, blk, H, D, group, 3.0)
+    kivi_pack_kv_cache(torch.from_numpy(key).to(dev()).to(torch.bfloat16),
+                       torch.from_numpy(value).to(dev()).to(torch.bfloat16), torch.from_numpy(slots).to(dev()),
+                       views[:3], views[3:], group, validate_slots=False)
+    torch.cuda.synchronize()
+    ov = [x.cpu().numpy() for x in _empty_views(nb, blk, H, D, group, 3.0)]
+    O.kivi_pack_key(key, slots, ov[0], ov[1], ov[2], group)
+    O.kivi_pack_value(value, slots, ov[3], ov[4], ov[5], group)
+    names = ("k_quant", "k_scale", "k_mn", "v_quant", "v_scale", "v_mn")
+    for n, v, o in zip(names, views, ov):
+        assert np.array_equal(v.cpu().numpy().view(np.uint32), o.view(np.uint32)), n
+    assert_no_device_error()
+
+
 def test_kivi_pack_value_skips_padding_and_rejects_misaligned_keys():
     from qkv_b200.ops import kivi_pack_key_cache, kivi_pack_value_cache
 
