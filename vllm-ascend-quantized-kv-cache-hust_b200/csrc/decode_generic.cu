@@ -272,36 +272,79 @@ decode_generic_kernel(const DecodeParams p) {
   }
 }
 
-// grid (num_heads, batch), one thread per channel.
-__global__ void combine_kernel(const DecodeParams p) {
-  const int hq = blockIdx.x, b = blockIdx.y;
-  const int S = p.splits_total;
-  const int64_t row0 = (static_cast<int64_t>(b) * p.num_heads + hq) * S;
+// Warp per (request, head) row, 8 rows per CTA. The lanes read the row's
+// (max, sum) pairs together and stage the split weights w = exp2(m - max) in
+// shared memory; lane l then merges dims 4 l + 128 k .. + 3 with the
+// partials of 8 splits in flight, in split order: num += w acc, den += w l,
+// out = num / den (splits with m = -inf are skipped: their partial sums may
+// never have been written). kVec: 16-byte loads of the partial sums (the
+// workspace 16-byte aligned).
+constexpr int kCombineRows = 8;
+constexpr int kCombineStaged = 128;  // splits whose weights a warp stages
+template <bool kVec>
+__global__ void __launch_bounds__(kCombineRows * 32) combine_kernel(const DecodeParams p) {
+  __shared__ float wts[kCombineRows][kCombineStaged];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kCombineRows + warp;
+  if (row >= static_cast<int64_t>(p.batch) * p.num_heads) return;
+  const int b = static_cast<int>(row / p.num_heads), hq = static_cast<int>(row % p.num_heads);
+  const int S = p.splits_total, D = p.head_size;
+  const float* ml = p.ws_ml + row * S * 2;
+  const float* acc = p.ws_acc + row * S * D;
   float M = kNegInf;
-  for (int s = 0; s < S; ++s) M = fmaxf(M, p.ws_ml[(row0 + s) * 2]);
-  for (int d = threadIdx.x; d < p.head_size; d += blockDim.x) {
-    float num = 0.0f, den = 0.0f;
+  for (int s = lane; s < S; s += 32) M = fmaxf(M, ml[2 * s]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  const bool staged = S <= kCombineStaged;
+  if (staged)
+    for (int s = lane; s < S; s += 32) {
+      const float m = ml[2 * s];
+      wts[warp][s] = (M == kNegInf || m == kNegInf) ? 0.0f : exp2f(m - M);
+    }
+  __syncwarp();
+  __nv_bfloat16* out = p.out + static_cast<int64_t>(b) * p.out_stride + static_cast<int64_t>(hq) * D;
+  for (int d0 = 4 * lane; d0 < D; d0 += 128) {
+    float num[4] = {0.0f, 0.0f, 0.0f, 0.0f}, den = 0.0f;
     if (M != kNegInf) {
-      for (int s = 0; s < S; ++s) {
-        const float m = p.ws_ml[(row0 + s) * 2];
-        if (m == kNegInf) continue;
-        const float w = exp2f(m - M);
-        num += w * p.ws_acc[(row0 + s) * p.head_size + d];
-        den += w * p.ws_ml[(row0 + s) * 2 + 1];
+      for (int s0 = 0; s0 < S; s0 += 8) {
+        float4 v[8];
+        float l[8], m[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int s = s0 + k < S ? s0 + k : S - 1;  // in range: the extra lanes of the batch are unused
+          m[k] = ml[2 * s];
+          l[k] = ml[2 * s + 1];
+          const float* a = acc + static_cast<int64_t>(s) * D + d0;
+          v[k] = kVec ? *reinterpret_cast<const float4*>(a) : make_float4(a[0], a[1], a[2], a[3]);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if (s0 + k >= S || m[k] == kNegInf) continue;
+          const float w = staged ? wts[warp][s0 + k] : exp2f(m[k] - M);
+          num[0] = fmaf(w, v[k].x, num[0]);
+          num[1] = fmaf(w, v[k].y, num[1]);
+          num[2] = fmaf(w, v[k].z, num[2]);
+          num[3] = fmaf(w, v[k].w, num[3]);
+          den = fmaf(w, l[k], den);
+        }
       }
     }
-    p.out[static_cast<int64_t>(b) * p.out_stride +
-          static_cast<int64_t>(hq) * p.head_size + d] =
-        __float2bfloat16_rn(den > 0.0f ? num / den : 0.0f);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) out[d0 + k] = __float2bfloat16_rn(den > 0.0f ? num[k] / den : 0.0f);
   }
 }
 
 }  // namespace
 
+// head_size is a multiple of 8 on every decode entry point, so a 16-byte
+// aligned workspace gives 16-byte aligned partial rows.
 void launch_combine(const DecodeParams& p, cudaStream_t stream) {
-  dim3 grid(p.num_heads, p.batch);
-  const int threads = p.head_size < 128 ? 128 : (p.head_size > 256 ? 256 : p.head_size);
-  combine_kernel<<<grid, threads, 0, stream>>>(p);
+  const int64_t rows = static_cast<int64_t>(p.batch) * p.num_heads;
+  const unsigned grid = static_cast<unsigned>((rows + kCombineRows - 1) / kCombineRows);
+  if ((reinterpret_cast<uintptr_t>(p.ws_acc) & 15u) == 0)
+    combine_kernel<true><<<grid, kCombineRows * 32, 0, stream>>>(p);
+  else
+    combine_kernel<false><<<grid, kCombineRows * 32, 0, stream>>>(p);
 }
 
 size_t generic_smem_bytes(int gqa, int head_size) {

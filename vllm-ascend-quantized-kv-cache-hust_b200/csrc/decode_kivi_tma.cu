@@ -189,6 +189,18 @@ __device__ __forceinline__ float4 tail_value4(const DecodeParams& p, const TailS
 
 constexpr int kTailLd = kD + 4;  // padded fp32 row of the staged keys
 
+// A split with nothing to attend writes only the (max, sum) = (-inf, 0) of
+// its rows: the combine skips such a split without reading its sums. (With
+// a single split the output itself is written by the full path.)
+__device__ __forceinline__ void empty_split(const DecodeParams& p, int b, int h, int split) {
+  const int G = p.gqa;
+  if (static_cast<int>(threadIdx.x) < G) {
+    const int64_t row = (static_cast<int64_t>(b) * p.num_heads + h * G + threadIdx.x) * p.splits_total + split;
+    p.ws_ml[row * 2] = -CUDART_INF_F;
+    p.ws_ml[row * 2 + 1] = 0.0f;
+  }
+}
+
 // One tail CTA: positions [body_end, L) in blocks of kTailBlock, blocks
 // c, c + n_tail, ...; its partial softmax state is split num_hist_splits + c.
 // Each block's K and V rows are staged in shared memory (fp32) with
@@ -207,6 +219,10 @@ __device__ __forceinline__ void window_tail(const DecodeParams& p, int c, int n_
   const int L = max(p.seq_lens[b], 0);
   const TailState ts = load_tail_state(p, b, L);
   const int body_end = min(ts.k_begin, ts.v_begin);
+  if (body_end + kTailBlock * c >= L && p.splits_total > 1) {  // no block for this CTA
+    empty_split(p, b, h, p.num_hist_splits + c);
+    return;
+  }
 
   // q * scale * log2(e), channels 4 lane .. 4 lane + 3 of every head
   float q[kHeads][4];
@@ -370,6 +386,10 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
   const int t0 = split * p.split_tokens;
   const int t1 = min(body_end, t0 + p.split_tokens);
   const int n_pages = t1 > t0 ? min((t1 - t0 + kBlk - 1) / kBlk, kMaxPages) : 0;
+  if (n_pages == 0 && p.splits_total > 1) {  // the request ends before this split
+    empty_split(p, b, h, split);
+    return;
+  }
 
   for (int i = tid; i < n_pages; i += kThreads)
     sh.pid[i] = static_cast<int>(page_of(p, b, t0 + i * kBlk));
