@@ -481,6 +481,9 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
 
   int consumed = 0;
   bool aborted = false;
+  // late schedule: two pages per unrolled iteration make the stage and
+  // buffer indices constants (2.4 % faster on config 5)
+#pragma unroll(kEarly ? 1 : 2)
   for (int i = 0; i < n_pages; ++i) {
     const int s = i % kStages;
     const uint32_t parity = static_cast<uint32_t>((i / kStages) & 1);
