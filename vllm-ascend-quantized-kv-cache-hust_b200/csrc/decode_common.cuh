@@ -164,6 +164,20 @@ __device__ __forceinline__ void store_partial(const DecodeParams& p, int b,
   }
 }
 
+// A split with nothing to attend writes only the (max, sum) = (-inf, 0) of
+// its rows (kv head h's G query heads): the combine skips such a split
+// without reading its sums. Only for plans of several splits (with one, the
+// output itself is written by the full path).
+__device__ __forceinline__ void empty_split(const DecodeParams& p, int b, int h, int split) {
+  const int G = p.gqa;
+  if (static_cast<int>(threadIdx.x) < G) {
+    const int64_t row =
+        (static_cast<int64_t>(b) * p.num_heads + static_cast<int64_t>(h) * G + threadIdx.x) * p.splits_total + split;
+    p.ws_ml[row * 2] = -__int_as_float(0x7f800000);
+    p.ws_ml[row * 2 + 1] = 0.0f;
+  }
+}
+
 void launch_combine(const DecodeParams& p, cudaStream_t stream);
 
 }  // namespace qkv

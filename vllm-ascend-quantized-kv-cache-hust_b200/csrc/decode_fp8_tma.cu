@@ -86,6 +86,10 @@ fp8_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap 
   const int t0 = split * p.split_tokens;
   const int t1 = min(L, t0 + p.split_tokens);
   const int n_pages = t1 > t0 ? min((t1 - t0 + kBlk - 1) / kBlk, kMaxPages) : 0;
+  if (n_pages == 0 && p.splits_total > 1) {  // the request ends before this split
+    empty_split(p, b, h, split);
+    return;
+  }
 
   for (int i = tid; i < n_pages; i += kThreads)
     sh.pid[i] = static_cast<int>(page_of(p, b, t0 + i * kBlk));

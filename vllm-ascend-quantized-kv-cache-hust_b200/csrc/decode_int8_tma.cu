@@ -94,6 +94,10 @@ int8_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
   const int t0 = split * p.split_tokens;
   const int t1 = min(L, t0 + p.split_tokens);
   const int n_pages = t1 > t0 ? min((t1 - t0 + kBlk - 1) / kBlk, kMaxPages) : 0;
+  if (n_pages == 0 && p.splits_total > 1) {  // the request ends before this split
+    empty_split(p, b, h, split);
+    return;
+  }
   const int n_steps = t1 > t0 ? min((t1 - t0 + kStageTok - 1) / kStageTok, kMaxPages * kHalves) : 0;
 
   for (int i = tid; i < n_pages; i += kThreads)

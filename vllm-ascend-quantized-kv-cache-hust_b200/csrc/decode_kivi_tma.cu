@@ -189,17 +189,6 @@ __device__ __forceinline__ float4 tail_value4(const DecodeParams& p, const TailS
 
 constexpr int kTailLd = kD + 4;  // padded fp32 row of the staged keys
 
-// A split with nothing to attend writes only the (max, sum) = (-inf, 0) of
-// its rows: the combine skips such a split without reading its sums. (With
-// a single split the output itself is written by the full path.)
-__device__ __forceinline__ void empty_split(const DecodeParams& p, int b, int h, int split) {
-  const int G = p.gqa;
-  if (static_cast<int>(threadIdx.x) < G) {
-    const int64_t row = (static_cast<int64_t>(b) * p.num_heads + h * G + threadIdx.x) * p.splits_total + split;
-    p.ws_ml[row * 2] = -CUDART_INF_F;
-    p.ws_ml[row * 2 + 1] = 0.0f;
-  }
-}
 
 // One tail CTA: positions [body_end, L) in blocks of kTailBlock, blocks
 // c, c + n_tail, ...; its partial softmax state is split num_hist_splits + c.
