@@ -23,8 +23,9 @@
 // register, i.e. the (row, k) / (row, k + 1) pair of an A fragment; masking
 // nibble i of both halves (one AND) makes fp16 subnormals n * 2^-24 (16 n *
 // 2^-24 for nibble 1), which the MMA takes exactly. Nibbles 2 and 3 first
-// move down a byte (one PRMT per register). Scales fold into the other
-// operand:
+// move down a byte with zeros above (one PRMT per register); nibble 3's rows
+// then take the whole byte n2 + 16 n3 unmasked and lose the n2 part
+// afterwards (hi_bytes). Scales fold into the other operand:
 //     K: S = S' / f + sum_d q[h][d] k_mn[d][group]
 //     V: P'[t][h] = p[t][h] * v_scale[t][group],
 //        O = O' / f + sum_t p[t][h] v_mn[t][group]
@@ -68,6 +69,12 @@ constexpr float kUnsub = 16777216.0f;        // 2^24: low-nibble rows
 constexpr float kUnsubHi = 1048576.0f;       // 2^20: high-nibble rows (2^24 / 16)
 __device__ __forceinline__ uint32_t nib_lo_sub(uint32_t x) { return x & 0x000F000Fu; }
 __device__ __forceinline__ uint32_t nib_hi_sub(uint32_t x) { return x & 0x00F000F0u; }
+// Bytes 1 and 3 of x moved down to bytes 0 and 2, zeros above: each half is
+// the whole byte n2 + 16 n3 as an fp16 subnormal, (n2 + 16 n3) * 2^-24. As the
+// operand of the rows that want nibble 3 it saves their AND; the n2 part is
+// taken off the accumulator afterwards (the rows that want nibble 2 hold
+// exactly it, in the same lane and column).
+__device__ __forceinline__ uint32_t hi_bytes(uint32_t x) { return __byte_perm(x, 0u, 0x4341u); }
 constexpr float kLazy = 4.0f;  // log2 headroom of the running max
 
 template <int NG>
@@ -573,10 +580,13 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
         const int kk = 2 * kp + e;
         const uint32_t x0 = kx[kp][2 * e], x1 = kx[kp][2 * e + 1];
         mma16816(sc[0], nib_lo_sub(x0), nib_hi_sub(x0), nib_lo_sub(x1), nib_hi_sub(x1), bq[kk][0], bq[kk][1]);
-        const uint32_t y0 = prmt(x0, x0, 0x0301u), y1 = prmt(x1, x1, 0x0301u);
-        mma16816(sc[1], nib_lo_sub(y0), nib_hi_sub(y0), nib_lo_sub(y1), nib_hi_sub(y1), bq[kk][0], bq[kk][1]);
+        const uint32_t y0 = hi_bytes(x0), y1 = hi_bytes(x1);
+        mma16816(sc[1], nib_lo_sub(y0), y0, nib_lo_sub(y1), y1, bq[kk][0], bq[kk][1]);
       }
     }
+    // m-tile 1's rows g + 8 took whole bytes (n2 + 16 n3): remove the n2 part
+    sc[1][2] -= sc[1][0];
+    sc[1][3] -= sc[1][1];
     // scores in log2 units: [j][0..1] low-nibble token, heads 2t, 2t+1; [j][2..3] its +1
 #pragma unroll
     for (int j = 0; j < 2; ++j)
@@ -697,8 +707,8 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
         const uint32_t x0 = vx[db][2 * j], x1 = vx[db][2 * j + 1];
         mma16816(o[2 * db], nib_lo_sub(x0), nib_hi_sub(x0), nib_lo_sub(x1), nib_hi_sub(x1), pb[j][gg][0],
                  pb[j][gg][1]);
-        const uint32_t y0 = prmt(x0, x0, 0x0301u), y1 = prmt(x1, x1, 0x0301u);
-        mma16816(o[2 * db + 1], nib_lo_sub(y0), nib_hi_sub(y0), nib_lo_sub(y1), nib_hi_sub(y1), pb[j][gg][0],
+        const uint32_t y0 = hi_bytes(x0), y1 = hi_bytes(x1);
+        mma16816(o[2 * db + 1], nib_lo_sub(y0), y0, nib_lo_sub(y1), y1, pb[j][gg][0],
                  pb[j][gg][1]);
       }
     }
@@ -729,6 +739,10 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
   for (int mt = 0; mt < 8; ++mt) {
     const int d_lo = 32 * (mt >> 1) + 4 * g + 2 * (mt & 1);
     const int gg = NG == 2 ? (mt >> 2) : 0;
+    if (mt & 1) {  // rows g + 8 of the odd m-tiles took whole bytes (n2 + 16 n3)
+      o[mt][2] -= o[mt][0];
+      o[mt][3] -= o[mt][1];
+    }
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int head = 2 * t + e;
