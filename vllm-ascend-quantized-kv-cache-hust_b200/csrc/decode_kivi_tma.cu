@@ -506,27 +506,59 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
           sh.vmv[qb][e] = st.vm[e];
         }
       }
-      // Q' entries of k-steps 2 warp, 2 warp + 1 (lane = fragment owner)
+      // Q' entries of k-steps 2 warp, 2 warp + 1 (lane = fragment owner):
+      // channels qch(r) = 2t, 2t + 1, 2t + 8, 2t + 9 are two adjacent pairs,
+      // so each pair's scales (and minima) of both groups come in one load
+      float c[NG];
+      uint32_t f[NG][4];
 #pragma unroll
-      for (int gq = 0; gq < NG; ++gq) {
-        float c = 0.0f;
-        uint32_t f[4];
+      for (int gq = 0; gq < NG; ++gq) c[gq] = 0.0f;
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
+      for (int e = 0; e < 2; ++e) {
+        const int ch0 = 16 * (2 * warp + e) + 2 * t;
+        float ks_[4][NG], km_[4][NG];  // [r][group]
+#pragma unroll
+        for (int hp = 0; hp < 2; ++hp) {
+          const int ch = ch0 + 8 * hp;
+          if constexpr (NG == 1) {
+            const float2 a = *reinterpret_cast<const float2*>(&st.ks[ch]);
+            const float2 m = *reinterpret_cast<const float2*>(&st.km[ch]);
+            ks_[2 * hp][0] = a.x;
+            ks_[2 * hp + 1][0] = a.y;
+            km_[2 * hp][0] = m.x;
+            km_[2 * hp + 1][0] = m.y;
+          } else {
+            const float4 a = *reinterpret_cast<const float4*>(&st.ks[ch * NG]);
+            const float4 m = *reinterpret_cast<const float4*>(&st.km[ch * NG]);
+            ks_[2 * hp][0] = a.x;
+            ks_[2 * hp][NG - 1] = a.y;
+            ks_[2 * hp + 1][0] = a.z;
+            ks_[2 * hp + 1][NG - 1] = a.w;
+            km_[2 * hp][0] = m.x;
+            km_[2 * hp][NG - 1] = m.y;
+            km_[2 * hp + 1][0] = m.z;
+            km_[2 * hp + 1][NG - 1] = m.w;
+          }
+        }
+#pragma unroll
+        for (int gq = 0; gq < NG; ++gq) {
           float qq[4];
 #pragma unroll
           for (int r = 0; r < 4; ++r) {
-            const int ch = 16 * (2 * warp + e) + qch(r);
-            qq[r] = qv[4 * e + r] * st.ks[ch * NG + gq];
-            c = fmaf(qv[4 * e + r], st.km[ch * NG + gq], c);
+            qq[r] = qv[4 * e + r] * ks_[r][gq];
+            c[gq] = fmaf(qv[4 * e + r], km_[r][gq], c[gq]);
           }
-          f[2 * e] = pack_half2(qq[0], qq[1]);
-          f[2 * e + 1] = pack_half2(qq[2], qq[3]);
+          f[gq][2 * e] = pack_half2(qq[0], qq[1]);
+          f[gq][2 * e + 1] = pack_half2(qq[2], qq[3]);
         }
-        sh.qf[qb][gq][warp][lane] = make_uint4(f[0], f[1], f[2], f[3]);
-        c += __shfl_xor_sync(0xffffffffu, c, 1);
-        c += __shfl_xor_sync(0xffffffffu, c, 2);
-        if (t == 0) sh.cmn[qb][gq][warp][g] = c;
+      }
+#pragma unroll
+      for (int gq = 0; gq < NG; ++gq) {
+        sh.qf[qb][gq][warp][lane] = make_uint4(f[gq][0], f[gq][1], f[gq][2], f[gq][3]);
+        float cc = c[gq];
+        cc += __shfl_xor_sync(0xffffffffu, cc, 1);
+        cc += __shfl_xor_sync(0xffffffffu, cc, 2);
+        if (t == 0) sh.cmn[qb][gq][warp][g] = cc;
       }
     }
     if (!__syncthreads_and(ok ? 1 : 0)) {  // uniform: every thread leaves here
