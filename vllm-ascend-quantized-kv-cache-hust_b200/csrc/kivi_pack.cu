@@ -361,11 +361,6 @@ __device__ __forceinline__ u64 pack2(float a, float b) {
 __device__ __forceinline__ void unpack2(u64 r, uint32_t& a, uint32_t& b) {
   asm("mov.b64 {%0, %1}, %2;\n" : "=r"(a), "=r"(b) : "l"(r));
 }
-__device__ __forceinline__ u64 sub2(u64 a, u64 b) {
-  u64 r;
-  asm("sub.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
 __device__ __forceinline__ u64 mul2(u64 a, u64 b) {
   u64 r;
   asm("mul.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
@@ -399,18 +394,30 @@ __device__ __forceinline__ uint32_t bmax2(uint32_t a, uint32_t b) {
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
-// The group constants of one lane pair: minimum, reciprocal and negated scale.
+// The group constants of one lane pair: minima, reciprocal and negated scale.
 struct Group2 {
-  u64 mn, inv, neg_s;
+  float mn0, mn1;
+  u64 inv, neg_s;
 };
 __device__ __forceinline__ Group2 group2(float mn0, float s0, float mn1, float s1) {
-  return Group2{pack2(mn0, mn1), pack2(__frcp_rn(s0), __frcp_rn(s1)), pack2(-s0, -s1)};
+  return Group2{mn0, mn1, pack2(__frcp_rn(s0), __frcp_rn(s1)), pack2(-s0, -s1)};
+}
+
+// RN(x - mn) for the bf16 halves of w in one mixed-precision subtraction
+// each (the bf16 operand enters exactly; one rounding, as x.float() - mn).
+__device__ __forceinline__ u64 sub_bf16x2(uint32_t w, float mn0, float mn1) {
+  float d0, d1;
+  asm("{\n .reg .b16 lo, hi;\n mov.b32 {lo, hi}, %2;\n"
+      " sub.rn.f32.bf16 %0, lo, %3;\n sub.rn.f32.bf16 %1, hi, %4;\n}\n"
+      : "=f"(d0), "=f"(d1)
+      : "r"(w), "f"(mn0), "f"(mn1));
+  return pack2(d0, d1);
 }
 
 // Codes of the two bf16 values of w (low half: lane 0 of the group pair),
 // returned in the low byte of r0 / r1.
 __device__ __forceinline__ void quant2(uint32_t w, const Group2& g, uint32_t& r0, uint32_t& r1) {
-  const u64 d = sub2(pack2(bf_lo(w), bf_hi(w)), g.mn);
+  const u64 d = sub_bf16x2(w, g.mn0, g.mn1);
   const u64 q0 = mul2(d, g.inv);
   const u64 q = fma2(fma2(q0, g.neg_s, d), g.inv, q0);
   const u64 k = add2_rm(add2(q, pack2(0.5f, 0.5f)), pack2(kMagic, kMagic));
