@@ -884,10 +884,11 @@ bool kivi_tma_supported(const DecodeParams& p) {
 }
 
 // Unit-pages (requests x kv heads x pages per request) up to which the early
-// refill schedule runs: measured on config 5's shapes, it wins at 8192
-// (0.049 vs 0.053 ms) and 16384 (0.087 vs 0.088) and loses at 32768 (0.156
-// vs 0.148) and 65536 (0.283 vs 0.267).
-constexpr long long kEarlyMaxUnitPages = 16384;
+// refill schedule runs: measured on config 5's shapes with the current page
+// loop (late: unrolled by two), it wins at 8192 (0.0469 vs 0.0490 ms) and on
+// config 2 (3968; 35.1 vs 36.9 us), and loses at 16384 (0.0800 vs 0.0780) and
+// 32768 (0.149 vs 0.137).
+constexpr long long kEarlyMaxUnitPages = 12288;
 
 bool kivi_early(long long units, long long pages) { return units * pages <= kEarlyMaxUnitPages; }
 
