@@ -19,6 +19,22 @@ __device__ __forceinline__ float kivi_value(uint32_t code, float scale, float mn
   return __fadd_rn(__fmul_rn(static_cast<float>(code), scale), mn);
 }
 
+// The same value without an int -> float conversion: `field` holds the code
+// at bits 19..22, so f = 16 + code exactly (1.0 * 2^4 plus code ulps of
+// 2^-19), and fma(f, scale, -16 scale) = RN(code * scale): the product f *
+// scale is exact inside the FMA and -16 scale is exact, so the sum is code *
+// scale exactly before its one rounding. Valid while 16 |scale| is finite
+// (|scale| < 2^124); callers take kivi_value beyond kBigScale.
+constexpr float kBigScale = 0x1p120f;
+__device__ __forceinline__ float kivi_value_field(uint32_t field, float scale, float neg16_scale, float mn) {
+  const float f = __uint_as_float((field & 0x00780000u) | 0x41800000u);
+  return __fadd_rn(__fmaf_rn(f, scale, neg16_scale), mn);
+}
+// rotates the nibble at bits 4 k .. 4 k + 3 of w to bits 19..22
+__device__ __forceinline__ uint32_t nibble_field(uint32_t w, int k) {
+  return __funnelshift_l(w, w, (19 - 4 * k) & 31);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&v);
@@ -110,8 +126,13 @@ __global__ void kivi_gather_kernel(const DecodeParams p, const int32_t* cu_k, in
 // token row. Values are token-major already and are read directly. `ch`
 // divides the block size and is a multiple or a divisor of the group, so a
 // chunk lies in one page and its groups do not straddle chunks.
-__global__ void __launch_bounds__(256) kivi_gather_tiled_kernel(const DecodeParams p, const int32_t* cu_k, int ch,
+// kD / kG / kCh: the head size, group and chunk as constants (0: from the
+// arguments), so the per-element index arithmetic is shifts.
+template <int kD, int kG, int kCh>
+__global__ void __launch_bounds__(256) kivi_gather_tiled_kernel(const DecodeParams p, const int32_t* cu_k, int ch_arg,
                                                                 __nv_bfloat16* dense_k, __nv_bfloat16* dense_v) {
+  const int ch = kCh ? kCh : ch_arg;
+  const int group = kG ? kG : p.group;
   extern __shared__ __align__(16) uint32_t gsm[];
   // ---- chunk -> (request, first position): chunks never straddle requests
   int b = -1, t0 = 0;
@@ -131,16 +152,17 @@ __global__ void __launch_bounds__(256) kivi_gather_tiled_kernel(const DecodePara
   const int h = blockIdx.y;
   const int L = max(p.seq_lens[b], 0);
   const int n = min(ch, L - t0);
-  const int D = p.head_size, kvh = p.kvh, words = D >> 3;
+  const int D = kD ? kD : p.head_size, kvh = p.kvh, words = D >> 3;
   const int cw = ch >> 3, pitch = D + 4;
-  const int ng = ch >= p.group ? ch / p.group : 1;
+  const int ng = ch >= group ? ch / group : 1;
   uint32_t* codes = gsm;                                          // [cw][pitch]
   float* gscale = reinterpret_cast<float*>(gsm + cw * pitch);     // [ng][D]
   float* gmin = gscale + ng * D;
+  float* gneg = gmin + ng * D;                                    // -16 x scale
   const TailState ts = load_tail_state(p, b, L);
   const int64_t page = t0 < ts.k_begin || t0 < ts.v_begin ? page_of(p, b, t0) : -1;
   const int off0 = t0 % p.blk;
-  const int g0 = off0 / p.group;
+  const int g0 = off0 / group;
   if (page >= 0 && t0 < ts.k_begin) {
     const int wpb = p.blk >> 3;
     const int32_t* src = p.kq + (page * kvh + h) * static_cast<int64_t>(D) * wpb + (off0 >> 3);
@@ -148,11 +170,13 @@ __global__ void __launch_bounds__(256) kivi_gather_tiled_kernel(const DecodePara
       const int d = i / cw, w = i - d * cw;
       codes[w * pitch + d] = static_cast<uint32_t>(__ldg(src + static_cast<int64_t>(d) * wpb + w));
     }
-    const int ngk = p.blk / p.group;
+    const int ngk = p.blk / group;
     const int64_t sb = (page * kvh + h) * static_cast<int64_t>(D) * ngk + g0;
     for (int i = threadIdx.x; i < D * ng; i += blockDim.x) {
       const int d = i / ng, gi = i - d * ng;
-      gscale[gi * D + d] = __ldg(p.ks + sb + static_cast<int64_t>(d) * ngk + gi);
+      const float sc = __ldg(p.ks + sb + static_cast<int64_t>(d) * ngk + gi);
+      gscale[gi * D + d] = sc;
+      gneg[gi * D + d] = fabsf(sc) < kBigScale ? __fmul_rn(-16.0f, sc) : __int_as_float(0x7fffffff);
       gmin[gi * D + d] = __ldg(p.km + sb + static_cast<int64_t>(d) * ngk + gi);
     }
   }
@@ -174,19 +198,34 @@ __global__ void __launch_bounds__(256) kivi_gather_tiled_kernel(const DecodePara
       const uint32_t* cr = codes + (tl >> 3) * pitch + 8 * c;
       const uint4 w0 = *reinterpret_cast<const uint4*>(cr);
       const uint4 w1 = *reinterpret_cast<const uint4*>(cr + 4);
-      const int gi = (off0 + tl) / p.group - g0;
+      const int gi = (off0 + tl) / group - g0;
       const float4 s0 = *reinterpret_cast<const float4*>(gscale + gi * D + 8 * c);
       const float4 s1 = *reinterpret_cast<const float4*>(gscale + gi * D + 8 * c + 4);
       const float4 m0 = *reinterpret_cast<const float4*>(gmin + gi * D + 8 * c);
       const float4 m1 = *reinterpret_cast<const float4*>(gmin + gi * D + 8 * c + 4);
-      const int sh = 4 * (tl & 7);
+      const float4 n0 = *reinterpret_cast<const float4*>(gneg + gi * D + 8 * c);
+      const float4 n1 = *reinterpret_cast<const float4*>(gneg + gi * D + 8 * c + 4);
+      const int k = tl & 7;
       const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
       const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
       const float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+      const float nv[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+      // a NaN -16 x scale marks a scale beyond kBigScale (or not finite)
+      const bool fast = !(isnan(nv[0]) || isnan(nv[1]) || isnan(nv[2]) || isnan(nv[3]) || isnan(nv[4]) ||
+                          isnan(nv[5]) || isnan(nv[6]) || isnan(nv[7]));
+      if (fast) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        ok[j] = pack_bf16x2(kivi_value((wv[2 * j] >> sh) & 0xFu, sv[2 * j], mv[2 * j]),
-                            kivi_value((wv[2 * j + 1] >> sh) & 0xFu, sv[2 * j + 1], mv[2 * j + 1]));
+        for (int j = 0; j < 4; ++j)
+          ok[j] = pack_bf16x2(kivi_value_field(nibble_field(wv[2 * j], k), sv[2 * j], nv[2 * j], mv[2 * j]),
+                              kivi_value_field(nibble_field(wv[2 * j + 1], k), sv[2 * j + 1], nv[2 * j + 1],
+                                               mv[2 * j + 1]));
+      } else {
+        const int sh = 4 * k;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          ok[j] = pack_bf16x2(kivi_value((wv[2 * j] >> sh) & 0xFu, sv[2 * j], mv[2 * j]),
+                              kivi_value((wv[2 * j + 1] >> sh) & 0xFu, sv[2 * j + 1], mv[2 * j + 1]));
+      }
     }
     // ---- value (token-major in the pages)
     if (t >= ts.v_begin) {
@@ -199,12 +238,20 @@ __global__ void __launch_bounds__(256) kivi_gather_tiled_kernel(const DecodePara
     } else {
       const int64_t vrow = (page * p.blk + off0 + tl) * kvh + h;
       const uint32_t word = static_cast<uint32_t>(__ldg(p.vq + vrow * words + c));
-      const int64_t si = vrow * (D / p.group) + (8 * c) / p.group;
+      const int64_t si = vrow * (D / group) + (8 * c) / group;
       const float sc = __ldg(p.vs + si), mn = __ldg(p.vm + si);
+      if (fabsf(sc) < kBigScale) {
+        const float n16 = __fmul_rn(-16.0f, sc);
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        ov[j] = pack_bf16x2(kivi_value((word >> (8 * j)) & 0xFu, sc, mn),
-                            kivi_value((word >> (8 * j + 4)) & 0xFu, sc, mn));
+        for (int j = 0; j < 4; ++j)
+          ov[j] = pack_bf16x2(kivi_value_field(nibble_field(word, 2 * j), sc, n16, mn),
+                              kivi_value_field(nibble_field(word, 2 * j + 1), sc, n16, mn));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          ov[j] = pack_bf16x2(kivi_value((word >> (8 * j)) & 0xFu, sc, mn),
+                              kivi_value((word >> (8 * j + 4)) & 0xFu, sc, mn));
+      }
     }
     const int64_t o = ((row0 + tl) * kvh + h) * D + 8 * c;
     *reinterpret_cast<uint4*>(dense_k + o) = make_uint4(ok[0], ok[1], ok[2], ok[3]);
@@ -228,12 +275,17 @@ int launch_kivi_gather(const DecodeParams& p, const int32_t* cu_k, int total_k, 
   if (threads <= 0) return QKV_OK;
   const int ch = tiled_chunk(p.blk, p.group);
   const int ng = ch >= p.group ? ch / p.group : 1;
-  const size_t smem = ch > 0 ? (static_cast<size_t>(ch / 8) * (p.head_size + 4) + 2 * ng * p.head_size) * 4 : 0;
+  const size_t smem = ch > 0 ? (static_cast<size_t>(ch / 8) * (p.head_size + 4) + 3 * ng * p.head_size) * 4 : 0;
   if (ch > 0 && smem <= 48 * 1024) {
     const int64_t chunks = (static_cast<int64_t>(total_k) + ch - 1) / ch + p.num_reqs;  // upper bound
     if (chunks > 0x7FFFFFFFll) return set_error(QKV_ERR_INVALID, "qkv_kivi_dequant_gather: too many chunks");
-    kivi_gather_tiled_kernel<<<dim3(static_cast<unsigned>(chunks), p.kvh), 256, smem, stream>>>(
-        p, cu_k, ch, dense_k, dense_v);
+    const dim3 grid(static_cast<unsigned>(chunks), p.kvh);
+    if (p.head_size == 128 && ch == 64 && p.group == 64)
+      kivi_gather_tiled_kernel<128, 64, 64><<<grid, 256, smem, stream>>>(p, cu_k, ch, dense_k, dense_v);
+    else if (p.head_size == 128 && ch == 64 && p.group == 128)
+      kivi_gather_tiled_kernel<128, 128, 64><<<grid, 256, smem, stream>>>(p, cu_k, ch, dense_k, dense_v);
+    else
+      kivi_gather_tiled_kernel<0, 0, 0><<<grid, 256, smem, stream>>>(p, cu_k, ch, dense_k, dense_v);
     QKV_CHECK_LAUNCH("kivi_gather_tiled_kernel");
     return QKV_OK;
   }
