@@ -375,11 +375,18 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
   const int G = p.gqa;
   const int kvh = p.kvh;
 
-  // ---- the split's history range [t0, t1): positions before the window
+  // ---- the split's history range [t0, t1): positions before the window.
+  // The block-table entry of page tid of the split is read alongside the
+  // request's length and window state (it does not depend on them; kMaxPages
+  // <= kThreads), and checked once the page count is known.
+  static_assert(kMaxPages <= kThreads, "one block-table entry per thread");
+  const int t0 = split * p.split_tokens;
+  const int col = t0 / kBlk + tid;
+  const int32_t pg_raw =
+      tid < kMaxPages && col < p.bt_stride ? p.bt[static_cast<int64_t>(b) * p.bt_stride + col] : -1;
   const int L = max(p.seq_lens[b], 0);
   const TailState ts = load_tail_state(p, b, L);
   const int body_end = min(ts.k_begin, ts.v_begin);
-  const int t0 = split * p.split_tokens;
   const int t1 = min(body_end, t0 + p.split_tokens);
   const int n_pages = t1 > t0 ? min((t1 - t0 + kBlk - 1) / kBlk, kMaxPages) : 0;
   if (n_pages == 0 && p.splits_total > 1) {  // the request ends before this split
@@ -387,8 +394,17 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
     return;
   }
 
-  for (int i = tid; i < n_pages; i += kThreads)
-    sh.pid[i] = static_cast<int>(page_of(p, b, t0 + i * kBlk));
+  if (tid < n_pages) {  // page_of's checks and errors on the entry read above
+    int pg = -1;
+    if (col >= p.bt_stride) {
+      record_error(p.err, kErrBlock);
+    } else if (pg_raw < 0 || pg_raw >= p.num_blocks) {
+      record_error(p.err, pg_raw < 0 ? kErrNegativeBlock : kErrBlock);
+    } else {
+      pg = static_cast<int>(pg_raw);
+    }
+    sh.pid[tid] = pg;
+  }
   if (tid == 0) {
 #pragma unroll
     for (int s = 0; s < kStages; ++s) mbar_init(&sh.full[s], 32 + 1);
@@ -790,28 +806,43 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
     }
   }
   __syncthreads();
+  // per head: the maximum over the warps, each warp's weight exp2(m_w - M)
+  // (-1: the warp saw nothing) and the weighted sum of l, once
+  float* mw8 = ml + kWarps * kHeads;  // [warp][head] weights
+  float* hmax = mw8 + kWarps * kHeads;
+  float* hsum = hmax + kHeads;
+  if (tid < kHeads) {
+    float M = -CUDART_INF_F;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, mm[w * kHeads + tid]);
+    float l = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float mw = mm[w * kHeads + tid];
+      const bool live = M != -CUDART_INF_F && mw != -CUDART_INF_F;
+      const float sc = live ? exp2f(mw - M) : -1.0f;
+      mw8[w * kHeads + tid] = sc;
+      if (live) l = fmaf(sc, ml[w * kHeads + tid], l);
+    }
+    hmax[tid] = M;
+    hsum[tid] = l;
+  }
+  __syncthreads();
   for (int idx = tid; idx < kHeads * kD; idx += kThreads) {
     const int head = idx / kD, d = idx % kD;
     if (head >= G) continue;
-    float M = -CUDART_INF_F;
+    float acc = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, mm[w * kHeads + head]);
-    float acc = 0.0f, l = 0.0f;
-    if (M != -CUDART_INF_F) {
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
-        const float mw = mm[w * kHeads + head];
-        if (mw == -CUDART_INF_F) continue;
-        const float sc = exp2f(mw - M);
-        acc = fmaf(sc, mo[(w * kHeads + head) * kD + d], acc);
-        l = fmaf(sc, ml[w * kHeads + head], l);
-      }
+    for (int w = 0; w < kWarps; ++w) {
+      const float sc = mw8[w * kHeads + head];
+      if (sc >= 0.0f) acc = fmaf(sc, mo[(w * kHeads + head) * kD + d], acc);
     }
-    store_partial(p, b, h * G + head, split, d, acc, M, l);
+    store_partial(p, b, h * G + head, split, d, acc, hmax[head], hsum[head]);
   }
 }
 
-static_assert(sizeof(PageStage<1>) * kStages >= sizeof(float) * (kWarps * kHeads * kD + 2 * kWarps * kHeads),
+static_assert(sizeof(PageStage<1>) * kStages >=
+                  sizeof(float) * (kWarps * kHeads * kD + 3 * kWarps * kHeads + 2 * kHeads),
               "merge buffers must fit in the stage memory");
 
 // ------------------------------------------------------------ host side
