@@ -382,8 +382,12 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
   static_assert(kMaxPages <= kThreads, "one block-table entry per thread");
   const int t0 = split * p.split_tokens;
   const int col = t0 / kBlk + tid;
-  const int32_t pg_raw =
-      tid < kMaxPages && col < p.bt_stride ? p.bt[static_cast<int64_t>(b) * p.bt_stride + col] : -1;
+  // past the table row: INT32_MAX, which fails the block-range check below
+  // with the same error as an entry past the last block (this kernel takes
+  // num_blocks * kvh * 128 < 2^31)
+  const int32_t pg_raw = tid >= kMaxPages      ? -1
+                         : col < p.bt_stride   ? p.bt[static_cast<int64_t>(b) * p.bt_stride + col]
+                                               : 0x7fffffff;
   const int L = max(p.seq_lens[b], 0);
   const TailState ts = load_tail_state(p, b, L);
   const int body_end = min(ts.k_begin, ts.v_begin);
@@ -396,9 +400,7 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
 
   if (tid < n_pages) {  // page_of's checks and errors on the entry read above
     int pg = -1;
-    if (col >= p.bt_stride) {
-      record_error(p.err, kErrBlock);
-    } else if (pg_raw < 0 || pg_raw >= p.num_blocks) {
+    if (pg_raw < 0 || pg_raw >= p.num_blocks) {
       record_error(p.err, pg_raw < 0 ? kErrNegativeBlock : kErrBlock);
     } else {
       pg = static_cast<int>(pg_raw);
