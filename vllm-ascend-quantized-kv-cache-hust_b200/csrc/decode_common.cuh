@@ -50,6 +50,7 @@ struct DecodeParams {
   int split_tokens;  // tokens per history split (multiple of blk)
   int splits_total;  // history splits (+1 tail split for KIVI)
   int split_base;    // blockIdx.x + split_base = split index of a CTA
+  int split_mid;     // KIVI page-pipelined grid: 0 (kv head, request, split), 1 (kv head, split, request)
   float* ws_acc;     // [B, Hq, splits_total, D]   (unnormalised)
   float* ws_ml;      // [B, Hq, splits_total, 2]   (running max, sum)
   __nv_bfloat16* out;

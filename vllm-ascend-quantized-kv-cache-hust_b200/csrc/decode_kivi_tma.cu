@@ -364,9 +364,12 @@ kivi_decode_tma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
   unsigned char* smem_raw = smem_dyn + (((raw + 1023u) & ~1023u) - raw);
   PageShared<NG>& sh = *reinterpret_cast<PageShared<NG>*>(smem_raw);
   const int n_tail = p.splits_total - p.num_hist_splits;  // window CTAs come first
-  // grid (kv head, request, split): the heads of one (request, split) are
-  // consecutive CTAs, the split index the slowest-moving (see the launch)
-  const int h = blockIdx.x, b = blockIdx.y, xs = blockIdx.z;
+  // grid (kv head, request, split) or, with split_mid (early schedule only),
+  // (kv head, split, request): the heads of one (request, split) are
+  // consecutive CTAs (see the launch)
+  const bool mid = kEarly && p.split_mid;
+  const int h = blockIdx.x;
+  const int b = mid ? blockIdx.z : blockIdx.y, xs = mid ? blockIdx.y : blockIdx.z;
   if (xs < n_tail) {
     window_tail(p, xs, n_tail, h, b, smem_raw);
     return;
@@ -972,6 +975,8 @@ SplitPlan plan_kivi_tma(int batch, int kvh, int group, int max_seq_len, int sms)
   return plan;
 }
 
+constexpr int kSplitMidBatch = 8;
+
 int launch_kivi_tma(const DecodeParams& p0, cudaStream_t stream, bool combine, int* splits_used) {
   DecodeParams p = p0;
   // window CTAs only when there is a window; the partial count shrinks to match
@@ -983,11 +988,16 @@ int launch_kivi_tma(const DecodeParams& p0, cudaStream_t stream, bool combine, i
   // the split index moves slowest, so the CTAs an SM receives come from
   // different splits rather than neighbouring splits of few requests (config
   // 5 0.245 -> 0.240 ms, one GPU's N = 8 share 0.0468 -> 0.0450, config 4's
-  // decode rows 0.104 -> 0.100; config 2 0.036 -> 0.037)
-  dim3 grid(p.kvh, p.batch, p.splits_total);
-  // the plan's pages per request: history splits x pages per split
+  // decode rows 0.104 -> 0.100). Batches of up to kSplitMidBatch requests
+  // order (kv head, split, request) instead: config 2 (8 requests) 0.0367 ->
+  // 0.0329-0.0344 ms, where that order costs config 4's rows (30 requests)
+  // and the N = 8 share (32) 3-4 %.
+  // (the late schedule keeps the first order: its kernel reads no flag).
+  // The plan's pages per request: history splits x pages per split.
   const bool early = kivi_early(static_cast<long long>(p.batch) * p.kvh,
                                 static_cast<long long>(p.num_hist_splits) * (p.split_tokens / kBlk));
+  p.split_mid = early && p.batch <= kSplitMidBatch ? 1 : 0;
+  const dim3 grid = p.split_mid ? dim3(p.kvh, p.splits_total, p.batch) : dim3(p.kvh, p.batch, p.splits_total);
 #define QKV_KIVI_LAUNCH(NG, EARLY)                                                      \
   do {                                                                                  \
     if ((rc = set_smem_attr<NG, EARLY>()) != QKV_OK) return rc;                         \
