@@ -193,7 +193,8 @@ int kivi_decode(
     const int32_t* res_state, int batch, int num_heads, int num_kv_heads,
     int head_size, int group_size, int block_size, int64_t num_blocks,
     int max_seq_len, float scale, void* workspace, size_t workspace_bytes_,
-    void* out, int64_t out_stride, qkv_stream_t stream, bool combine, int* splits_used) {
+    void* out, int64_t out_stride, qkv_stream_t stream, bool combine, int* splits_used,
+    bool after_ring_write = false) {
   if (splits_used != nullptr) *splits_used = 1;
   int rc = check_decode_args("qkv_kivi_paged_decode", batch, num_heads,
                              num_kv_heads, head_size, block_size, num_blocks,
@@ -240,6 +241,7 @@ int kivi_decode(
   p.out = static_cast<__nv_bfloat16*>(out);
   p.out_stride = out_stride;
   p.err = device_error_ptr();
+  p.after_ring_write = after_ring_write ? 1 : 0;
   const SplitPlan plan = plan_for(p, true, max_seq_len);
   p.num_hist_splits = plan.hist_splits;
   p.split_tokens = plan.split_tokens;
@@ -264,6 +266,21 @@ int kivi_decode(
 }
 
 }  // namespace
+
+// (C++ linkage, declared in qkv_common.cuh: not part of the C ABI)
+extern "C++" int kivi_paged_decode_after_ring_write(
+    const void* query, int64_t q_stride, const int32_t* k_quant, const float* k_scale, const float* k_mn,
+    const int32_t* v_quant, const float* v_scale, const float* v_mn, const void* res_key, const void* res_value,
+    int res_rows, int res_capacity, const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
+    const int32_t* res_state, int batch, int num_heads, int num_kv_heads, int head_size, int group_size,
+    int block_size, int64_t num_blocks, int max_seq_len, float scale, void* workspace, size_t workspace_bytes_,
+    void* out, int64_t out_stride, qkv_stream_t stream) {
+  return kivi_decode(query, q_stride, k_quant, k_scale, k_mn, v_quant, v_scale, v_mn, res_key, res_value, res_rows,
+                     res_capacity, block_table, bt_stride, seq_lens, res_state, batch, num_heads, num_kv_heads,
+                     head_size, group_size, block_size, num_blocks, max_seq_len, scale, workspace, workspace_bytes_,
+                     out, out_stride, stream, true, nullptr, true);
+}
+
 }  // namespace qkv
 
 int qkv_kivi_paged_decode(

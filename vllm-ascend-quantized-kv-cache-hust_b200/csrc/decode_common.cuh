@@ -51,6 +51,10 @@ struct DecodeParams {
   int splits_total;  // history splits (+1 tail split for KIVI)
   int split_base;    // blockIdx.x + split_base = split index of a CTA
   int split_mid;     // KIVI page-pipelined grid: 0 (kv head, request, split), 1 (kv head, split, request)
+  // the launch before the decode wrote only the bf16 residual rings: the
+  // decode may start before it ends (programmatic dependent launch), its
+  // window CTAs waiting for it
+  int after_ring_write;
   float* ws_acc;     // [B, Hq, splits_total, D]   (unnormalised)
   float* ws_ml;      // [B, Hq, splits_total, 2]   (running max, sum)
   __nv_bfloat16* out;
@@ -178,6 +182,29 @@ __device__ __forceinline__ void empty_split(const DecodeParams& p, int b, int h,
     p.ws_ml[row * 2 + 1] = 0.0f;
   }
 }
+
+// Waits until the grid this one was launched behind with programmatic
+// stream serialisation has completed and its writes are visible; returns at
+// once for a grid launched without it.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
+// Launch attributes of a programmatic dependent launch (the grid may start
+// before the previous one on the stream ends; it calls grid_dependency_wait
+// before reading what that grid wrote).
+struct PdlConfig {
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  PdlConfig(dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl) {
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+};
 
 void launch_combine(const DecodeParams& p, cudaStream_t stream);
 

@@ -284,6 +284,7 @@ constexpr int kCombineStaged = 128;  // splits whose weights a warp stages
 template <bool kVec>
 __global__ void __launch_bounds__(kCombineRows * 32) combine_kernel(const DecodeParams p) {
   __shared__ float wts[kCombineRows][kCombineStaged];
+  grid_dependency_wait();  // launched behind the decode that wrote the partials
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kCombineRows + warp;
   if (row >= static_cast<int64_t>(p.batch) * p.num_heads) return;
@@ -341,10 +342,14 @@ __global__ void __launch_bounds__(kCombineRows * 32) combine_kernel(const Decode
 void launch_combine(const DecodeParams& p, cudaStream_t stream) {
   const int64_t rows = static_cast<int64_t>(p.batch) * p.num_heads;
   const unsigned grid = static_cast<unsigned>((rows + kCombineRows - 1) / kCombineRows);
+  // a programmatic dependent launch: the combine's launch overlaps the end
+  // of the decode it follows, and its CTAs wait for that decode
+  // (a failed launch shows in the callers' launch check)
+  PdlConfig c(dim3(grid), dim3(kCombineRows * 32), 0, stream, true);
   if ((reinterpret_cast<uintptr_t>(p.ws_acc) & 15u) == 0)
-    combine_kernel<true><<<grid, kCombineRows * 32, 0, stream>>>(p);
+    (void)cudaLaunchKernelEx(&c.cfg, combine_kernel<true>, p);
   else
-    combine_kernel<false><<<grid, kCombineRows * 32, 0, stream>>>(p);
+    (void)cudaLaunchKernelEx(&c.cfg, combine_kernel<false>, p);
 }
 
 size_t generic_smem_bytes(int gqa, int head_size) {

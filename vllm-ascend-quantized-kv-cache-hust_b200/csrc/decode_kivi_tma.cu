@@ -204,6 +204,7 @@ constexpr int kTailLd = kD + 4;  // padded fp32 row of the staged keys
 // CUDA-core math (the window is < 1% of the bytes).
 __device__ __forceinline__ void window_tail(const DecodeParams& p, int c, int n_tail, int h, int b,
                                             unsigned char* smem) {
+  grid_dependency_wait();  // the rings may still be written by the launch before (after_ring_write)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = p.gqa;
   float* kt = reinterpret_cast<float*>(smem);  // [kTailBlock][kTailLd]
@@ -1001,7 +1002,9 @@ int launch_kivi_tma(const DecodeParams& p0, cudaStream_t stream, bool combine, i
 #define QKV_KIVI_LAUNCH(NG, EARLY)                                                      \
   do {                                                                                  \
     if ((rc = set_smem_attr<NG, EARLY>()) != QKV_OK) return rc;                         \
-    kivi_decode_tma_kernel<NG, EARLY><<<grid, kThreads, kivi_smem_bytes<NG>(), stream>>>(p, tk, tv); \
+    PdlConfig c_(grid, dim3(kThreads), kivi_smem_bytes<NG>(), stream, p.after_ring_write != 0); \
+    const cudaError_t le_ = cudaLaunchKernelEx(&c_.cfg, kivi_decode_tma_kernel<NG, EARLY>, p, tk, tv); \
+    if (le_ != cudaSuccess) return cuda_error(le_, "kivi_decode_tma_kernel");                          \
   } while (0)
   if (p.group == 128) {
     if (early) QKV_KIVI_LAUNCH(1, true); else QKV_KIVI_LAUNCH(1, false);

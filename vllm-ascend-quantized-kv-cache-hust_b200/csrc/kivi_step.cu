@@ -292,6 +292,15 @@ QKV_API int qkv_kivi_decode_step(
     rc = scatter_new_tokens(res_key, res_value, ring_lanes, dk_lan, dk_src + nf[0], nw[0], dv_lan, dv_src + nf[1],
                             nw[1], new_key, new_value, batch, row_bytes, st);
     if (rc != QKV_OK) return rc;
+    // when the scatter launched (ring writes exist), it is the last launch
+    // and wrote only the rings (the pack and the staged metadata are
+    // complete): the decode may overlap it
+    if (nw[0] + nw[1] > 0)
+      return kivi_paged_decode_after_ring_write(
+          query, q_stride, k_quant, k_scale, k_mn, v_quant, v_scale, v_mn, res_key, res_value, w->rows, cap,
+          stage_table ? d32 + 7 * batch : block_table, stage_table ? table_cols : bt_stride, d32 + 6 * batch, d32,
+          batch, num_heads, num_kv_heads, head_size, group_size, block_size, num_blocks, std::max(max_len, 1), scale,
+          workspace, workspace_bytes, out, out_stride, stream);
     return qkv_kivi_paged_decode(query, q_stride, k_quant, k_scale, k_mn, v_quant, v_scale, v_mn, res_key,
                                  res_value, w->rows, cap, stage_table ? d32 + 7 * batch : block_table,
                                  stage_table ? table_cols : bt_stride, d32 + 6 * batch, d32, batch, num_heads,

@@ -84,4 +84,17 @@ __device__ __forceinline__ int64_t load_index(const void* p, int dtype,
                           : static_cast<int64_t>(static_cast<const int32_t*>(p)[i]);
 }
 
+// qkv_kivi_paged_decode for a caller whose last launch on `stream` wrote only
+// the bf16 residual rings (the one-call decode step's ring scatter): the
+// page-pipelined kernel starts before that launch ends, its history CTAs read
+// pages and metadata written by earlier launches, and its window CTAs wait
+// for the rings.
+int kivi_paged_decode_after_ring_write(
+    const void* query, int64_t q_stride, const int32_t* k_quant, const float* k_scale, const float* k_mn,
+    const int32_t* v_quant, const float* v_scale, const float* v_mn, const void* res_key, const void* res_value,
+    int res_rows, int res_capacity, const int32_t* block_table, int64_t bt_stride, const int32_t* seq_lens,
+    const int32_t* res_state, int batch, int num_heads, int num_kv_heads, int head_size, int group_size,
+    int block_size, int64_t num_blocks, int max_seq_len, float scale, void* workspace, size_t workspace_bytes,
+    void* out, int64_t out_stride, qkv_stream_t stream);
+
 }  // namespace qkv
