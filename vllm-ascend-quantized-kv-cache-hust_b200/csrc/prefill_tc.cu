@@ -10,9 +10,10 @@
 // an MMA. Per 128-key tile j and q-tile t:
 //     S_t[128 x 128] = Q_t . K_j^T   tcgen05.mma kind::f16, A and B from
 //                                    shared memory, fp32 in tensor memory
-//     P_t = softmax row pieces       one thread per row (TMEM lane = row);
-//                                    bf16 P written back over the first 64
-//                                    columns of S_t
+//     P_t = softmax row pieces       one thread per row (TMEM lane = row):
+//                                    the row max over the whole tile first,
+//                                    then bf16 P written back over the upper
+//                                    64 columns of S_t
 //     O_t[128 x 128] += P_t . V_j    A = P_t from TENSOR memory, B = V_j
 //                                    (MN-major) from shared memory
 // Keeping P in tensor memory leaves the tensor core only Q, K and V to read
@@ -24,10 +25,12 @@
 // issues the MMAs, ping-ponging: while warpgroup 1 turns S_1(j) into P_1(j),
 // the tensor core runs P_0(j).V_j and S_0(j+1), and the other way round. A
 // CTA's MMAs execute in issue order, so S_t(j+1) may overwrite the columns
-// P_t(j).V_j reads. The running max moves lazily (8 log2 units); O is
-// rescaled in TMEM only then. tcgen05.commit arrives on mbarriers; every wait
-// is bounded, and a wait that gives up ends the CTA's loops, drains what is
-// in flight, frees TMEM, skips the store and records device error 5.
+// P_t(j).V_j reads. P of keys 64-127 is handed over first, so their P.V runs
+// while the warpgroup finishes keys 0-63. The running max moves lazily (8 log2
+// units); O is rescaled in TMEM only then, before any P of the tile exists.
+// tcgen05.commit arrives on mbarriers; every wait is bounded, and a wait that
+// gives up ends the CTA's loops, drains what is in flight, frees TMEM, skips
+// the store and records device error 5.
 #include <math_constants.h>
 
 #include <atomic>
@@ -59,7 +62,7 @@ struct __align__(1024) PrefillSmem {
   __nv_bfloat16 v[kStages][2][kKTile][64];  // [stage][64-dim block][key][dims]
   unsigned long long q_full;
   unsigned long long k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
-  unsigned long long s_full[2], p_ready[2], o_done[2];
+  unsigned long long s_full[2], p_hi[2], p_ready[2], o_done[2];  // p_hi: P of keys 64-127 written
   uint32_t tmem_base;
 };
 constexpr size_t kPrefillSmem = sizeof(PrefillSmem) + 1024;
@@ -95,6 +98,96 @@ __device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsig
   unsigned long long r;
   asm("fma.rn.f32x2 %0, %1, %2, %3;\n" : "=l"(r) : "l"(a), "l"(b), "l"(c));
   return r;
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long f2_mul(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long f2_sub(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("sub.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// max of three (one instruction on sm_100)
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;\n" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for a pair of scores on the FMA pipe instead of the SFU. x = n + f with
+// n = rint(x): adding 1.5 * 2^23 leaves n in the low mantissa bits of t, and
+// f = x - (t - 1.5 * 2^23) lies in [-1/2, 1/2]. 2^f is a cubic in Horner form,
+// and n goes into the exponent field as (bits of t) << 23 (the shift constant's
+// own bits vanish in that shift). The cubic is a relative-error minimax fit of
+// 2^f on [-1/2, 1/2] by Lawson's iteratively reweighted least squares
+// (exp2_poly_fit.py beside this file prints these float32 coefficients); its
+// largest relative error evaluated in fp32 is 7.5e-5, under the 2^-9 of the bf16
+// rounding P goes through next. Inputs are clamped to -126 so that adding n to
+// the exponent field cannot wrap: a masked score (-inf) gives about 2^-126
+// (1e-38) instead of 0, which no sum of this kernel can notice (each row's sum
+// is at least 1: the score that set the running max contributes 2^0).
+constexpr float kExp2C0 = 0.99992806f, kExp2C1 = 0.69326097f, kExp2C2 = 0.24261114f, kExp2C3 = 0.055171669f;
+__device__ __forceinline__ void exp2_fma2(unsigned long long x2, float& p0, float& p1) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  float x0, x1;
+  f2_unpack(x2, x0, x1);
+  x2 = f2_pack(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
+  const unsigned long long rnd = f2_pack(kRound, kRound);
+  const unsigned long long t = f2_add(x2, rnd);
+  const unsigned long long f = f2_sub(x2, f2_sub(t, rnd));
+  unsigned long long q = f2_fma(f2_pack(kExp2C3, kExp2C3), f, f2_pack(kExp2C2, kExp2C2));
+  q = f2_fma(q, f, f2_pack(kExp2C1, kExp2C1));
+  q = f2_fma(q, f, f2_pack(kExp2C0, kExp2C0));
+  float q0, q1, t0, t1;
+  f2_unpack(q, q0, q1);
+  f2_unpack(t, t0, t1);
+  p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
+  p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
+}
+
+// Scores at columns >= lim of a 32-column chunk become -inf (causal mask).
+__device__ __forceinline__ void mask_scores(uint32_t (&sv)[32], int lim) {
+#pragma unroll
+  for (int c = 0; c < 32; ++c)
+    if (c >= lim) sv[c] = __float_as_uint(-CUDART_INF_F);
+}
+// Running maxima of a chunk: 4 chains of 3-input maxima, two scores per step.
+__device__ __forceinline__ void max_scores(float (&cm)[4], const uint32_t (&sv)[32]) {
+#pragma unroll
+  for (int c = 0; c < 32; c += 2)
+    cm[(c >> 1) & 3] = max3f(cm[(c >> 1) & 3], __uint_as_float(sv[c]), __uint_as_float(sv[c + 1]));
+}
+// p = 2^(s * scale * log2(e) - m) for a 32-score chunk, the scaling as one
+// f32x2 FMA per pair. The SFU's ex2 takes 15 of the 16 pairs and the FMA pipe
+// (exp2_fma2) the last, whose result then does not wait behind the SFU queue
+// (measured on config 4: 1168 TFLOP/s against 1140 with every pair on the SFU,
+// 1113-1134 with a quarter and 1036-1067 with a half or more on the FMA pipe).
+// Sums go to ps2, bf16 pairs to pk.
+__device__ __forceinline__ void exp_scores(const uint32_t (&sv)[32], unsigned long long sc2, unsigned long long nm2,
+                                           unsigned long long (&ps2)[4], uint32_t (&pk)[16]) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const unsigned long long x2 =
+        f2_fma(f2_pack(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1])), sc2, nm2);
+    float p0, p1;
+    if (i == 15) {
+      exp2_fma2(x2, p0, p1);
+    } else {
+      float x0, x1;
+      f2_unpack(x2, x0, x1);
+      p0 = fast_exp2(x0);
+      p1 = fast_exp2(x1);
+    }
+    ps2[i & 3] = f2_add(ps2[i & 3], f2_pack(p0, p1));
+    pk[i] = pack_bf16x2(p0, p1);
+  }
 }
 
 __device__ __forceinline__ void mbar_arrive_local(unsigned long long* bar) {
@@ -158,6 +251,7 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmap_
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&sm.s_full[t], 1);
+      mbar_init(&sm.p_hi[t], kSoftmaxThreads / 2);
       mbar_init(&sm.p_ready[t], kSoftmaxThreads / 2);
       mbar_init(&sm.o_done[t], 1);
     }
@@ -222,13 +316,17 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmap_
                        (kb | ks) != 0 ? 1u : 0u);
         tc::mma_commit(&sm.s_full[t]);
       };
-      auto issue_pv = [&](int t, int j) {
+      // P.V over keys 64-127 (hi) or 0-63; the hi half is issued first, so
+      // its first step starts O at tile 0
+      auto issue_pv = [&](int t, int j, bool hi) {
         const uint32_t v_addr = smem_u32(&sm.v[j % kStages][0][0][0]);
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks)  // 16 keys per step: 8 columns of packed bf16 P
-          tc::mma_ts(tbase + o_col(t), tbase + s_col(t) + 8 * ks,
+        for (int k4 = 0; k4 < 4; ++k4) {  // 16 keys per step: 8 columns of packed bf16 P
+          const int ks = hi ? 4 + k4 : k4;
+          tc::mma_ts(tbase + o_col(t), tbase + s_col(t) + 64 + 8 * ks,
                      tc::smem_desc_sw128(v_addr + ks * 16 * 128, 16384, 1024), id_pv,
-                     (j > 0 || ks > 0) ? 1u : 0u);
+                     (j > 0 || ks != 4) ? 1u : 0u);
+        }
       };
       bool ok = mbar_wait(&sm.q_full, 0) && mbar_wait(&sm.k_full[0], 0);
       tc::fence_after_sync();
@@ -240,9 +338,12 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmap_
         const bool next = j + 1 < n_tiles;
         if (!(ok = mbar_wait(&sm.v_full[j % kStages], static_cast<uint32_t>((j / kStages) & 1)))) break;
         // q-tile 0: P_0(j).V_j, then S_0(j + 1) while warpgroup 1 works
+        if (!(ok = mbar_wait(&sm.p_hi[0], static_cast<uint32_t>(j & 1)))) break;
+        tc::fence_after_sync();
+        issue_pv(0, j, true);  // while warpgroup 0 turns keys 0-63 into P
         if (!(ok = mbar_wait(&sm.p_ready[0], static_cast<uint32_t>(j & 1)))) break;
         tc::fence_after_sync();
-        issue_pv(0, j);
+        issue_pv(0, j, false);
         if (next) {
           const int s1 = (j + 1) % kStages;
           if (!(ok = mbar_wait(&sm.k_full[s1], static_cast<uint32_t>(((j + 1) / kStages) & 1)))) break;
@@ -250,9 +351,12 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmap_
           issue_s(0, j + 1);
         }
         if (has1) {
+          if (!(ok = mbar_wait(&sm.p_hi[1], static_cast<uint32_t>(j & 1)))) break;
+          tc::fence_after_sync();
+          issue_pv(1, j, true);
           if (!(ok = mbar_wait(&sm.p_ready[1], static_cast<uint32_t>(j & 1)))) break;
           tc::fence_after_sync();
-          issue_pv(1, j);
+          issue_pv(1, j, false);
         }
         tc::mma_commit(&sm.v_empty[j % kStages]);  // V_j read by both P.V MMAs
         if (next) {
@@ -279,88 +383,88 @@ prefill_tc_kernel(const PrefillArgs a, const __grid_constant__ CUtensorMap tmap_
         break;
       }
       tc::fence_after_sync();
-      // One pass over S_t in 32-column chunks, the next chunk's load in
-      // flight while this one is turned into P. A chunk whose max passes the
-      // running max by more than kLazyMax (log2 units) rescales O (earlier
-      // tiles) and the P chunks of this tile already written; after the first
-      // chunks of a row that is rare. Only a tile that reaches past some row's
-      // causal end masks.
+      // Two phases over S_t. (1) The row max over the tile's 128 scores:
+      // chunks 0-1, then chunks 2-3, which stay in registers. A row whose max
+      // passes the running max by more than kLazyMax (log2 units) rescales O
+      // (earlier tiles), once per tile and before any P of the tile exists;
+      // after the first tiles of a row that is rare. (2) P for chunks 2-3, then
+      // for chunks 0-1 loaded again. bf16 P goes to S_t's upper 64 columns (key
+      // k at column 64 + k / 2), whose scores are in registers by then. Only a
+      // tile that reaches past some row's causal end masks.
       const bool full_tile = __all_sync(0xffffffffu, (j + 1) * kKTile <= row_end);
+      const int lim = row_end - j * kKTile;  // scores at columns >= lim are masked
+      const uint32_t s_addr = t_row + s_col(t);
+      uint32_t sa[32], sb[32];
+      float cm[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F};
+      tc::tmem_ld32_async(s_addr, sa);
+      tc::tmem_ld32_async(s_addr + 32, sb);
+      tc::tmem_wait_ld_into(sa);
+      tc::tmem_wait_ld_into(sb);
+      if (!full_tile) {
+        mask_scores(sa, lim);
+        mask_scores(sb, lim - 32);
+      }
+      max_scores(cm, sa);
+      max_scores(cm, sb);
+      tc::tmem_ld32_async(s_addr + 64, sa);
+      tc::tmem_ld32_async(s_addr + 96, sb);
+      tc::tmem_wait_ld_into(sa);
+      tc::tmem_wait_ld_into(sb);
+      if (!full_tile) {
+        mask_scores(sa, lim - 64);
+        mask_scores(sb, lim - 96);
+      }
+      max_scores(cm, sa);
+      max_scores(cm, sb);
+      const float cmax = fmaxf(max3f(cm[0], cm[1], cm[2]), cm[3]) * a.scale_log2;
+      const bool grow = cmax > m_run + kLazyMax;
+      if (__any_sync(0xffffffffu, grow)) {
+        // m_run = -inf (nothing seen yet) gives alpha = 0: nothing to keep
+        const float alpha = grow ? fast_exp2(m_run - cmax) : 1.0f;
+        // S_t(j) is complete, so is every earlier MMA of this q-tile: O_t
+        // is free to touch
+        if (j > 0) {
+#pragma unroll
+          for (int cb = 0; cb < 4; ++cb) {
+            uint32_t ov[32];
+            tc::tmem_ld32(t_row + o_col(t) + 32 * cb, ov);
+#pragma unroll
+            for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
+            tc::tmem_st32(t_row + o_col(t) + 32 * cb, ov);
+          }
+        }
+        l_run *= alpha;
+        if (grow) m_run = cmax;
+      }
+      const float neg_m = m_run == -CUDART_INF_F ? 0.0f : -m_run;
+      const unsigned long long sc2 = f2_pack(a.scale_log2, a.scale_log2), nm2 = f2_pack(neg_m, neg_m);
+      // row sums as 4 packed pairs (one f32x2 add per pair of scores)
+      unsigned long long ps2[4] = {0ull, 0ull, 0ull, 0ull};
+      uint32_t pk[16];
+      exp_scores(sa, sc2, nm2, ps2, pk);
+      tc::tmem_st16(s_addr + 96, pk);
+      tc::tmem_ld32_async(s_addr, sa);  // chunk 0 again (its columns never hold P)
+      exp_scores(sb, sc2, nm2, ps2, pk);
+      tc::tmem_st16(s_addr + 112, pk);
+      tc::tmem_ld32_async(s_addr + 32, sb);
+      tc::tmem_wait_ld_into(sa);
+      tc::tmem_wait_ld_into(sb);
+      if (!full_tile) {
+        mask_scores(sa, lim);
+        mask_scores(sb, lim - 32);
+      }
+      exp_scores(sa, sc2, nm2, ps2, pk);
+      // P of keys 64-127 (and any O rescale) is in tensor memory: the MMA
+      // warp starts their P.V while this thread finishes keys 0-63
+      tc::tmem_wait_st();
+      tc::fence_before_sync();
+      mbar_arrive_local(&sm.p_hi[t]);
+      tc::tmem_st16(s_addr + 64, pk);
+      exp_scores(sb, sc2, nm2, ps2, pk);
+      tc::tmem_st16(s_addr + 80, pk);
       float ps[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) ps[i] = 0.0f;
-      uint32_t buf[2][32];
-      tc::tmem_ld32_async(t_row + s_col(t), buf[0]);
-      tc::tmem_wait_ld_into(buf[0]);
-#pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        uint32_t(&sv)[32] = buf[ch & 1];
-        if (ch < 3) tc::tmem_ld32_async(t_row + s_col(t) + 32 * (ch + 1), buf[(ch + 1) & 1]);
-        float cm[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F};
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          float v = __uint_as_float(sv[c]);
-          if (!full_tile && j * kKTile + 32 * ch + c >= row_end) v = -CUDART_INF_F;
-          sv[c] = __float_as_uint(v);
-          cm[c & 3] = fmaxf(cm[c & 3], v);
-        }
-        const float cmax = fmaxf(fmaxf(cm[0], cm[1]), fmaxf(cm[2], cm[3])) * a.scale_log2;
-        const bool grow = cmax > m_run + kLazyMax;
-        if (__any_sync(0xffffffffu, grow)) {
-          // m_run = -inf (nothing seen yet) gives alpha = 0: nothing to keep
-          const float alpha = grow ? fast_exp2(m_run - cmax) : 1.0f;
-          // S_t(j) is complete, so is every earlier MMA of this q-tile: O_t
-          // is free to touch
-          if (j > 0) {
-#pragma unroll
-            for (int cb = 0; cb < 4; ++cb) {
-              uint32_t ov[32];
-              tc::tmem_ld32(t_row + o_col(t) + 32 * cb, ov);
-#pragma unroll
-              for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
-              tc::tmem_st32(t_row + o_col(t) + 32 * cb, ov);
-            }
-          }
-          if (ch > 0) {
-            tc::tmem_wait_st();
-            for (int pc = 0; pc < ch; ++pc) {
-              uint32_t pw[16];
-              tc::tmem_ld16(t_row + s_col(t) + 16 * pc, pw);
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&pw[i]);
-                pw[i] = pack_bf16x2(__low2float(b2) * alpha, __high2float(b2) * alpha);
-              }
-              tc::tmem_st16(t_row + s_col(t) + 16 * pc, pw);
-            }
-          }
-          tc::tmem_wait_st();
-#pragma unroll
-          for (int i = 0; i < 8; ++i) ps[i] *= alpha;
-          l_run *= alpha;
-          if (grow) m_run = cmax;
-        }
-        // p = 2^(s * scale * log2(e) - m): one ex2 per score, the scaling as
-        // one f32x2 FMA per pair (moving a quarter of the ex2s to the FMA pipe
-        // as a cubic measured slower, 834 vs 851 TFLOP/s: the pass is not
-        // bound by the SFU); bf16 pairs go back over S_t's first 64 columns (this row's own
-        // lane; chunk ch lands on columns 16 ch.., read two chunks ago)
-        const float neg_m = m_run == -CUDART_INF_F ? 0.0f : -m_run;
-        const unsigned long long sc2 = f2_pack(a.scale_log2, a.scale_log2), nm2 = f2_pack(neg_m, neg_m);
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const unsigned long long x2 =
-              f2_fma(f2_pack(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1])), sc2, nm2);
-          float x0, x1;
-          f2_unpack(x2, x0, x1);
-          const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
-          ps[i & 7] += p0 + p1;
-          pk[i] = pack_bf16x2(p0, p1);
-        }
-        tc::tmem_st16(t_row + s_col(t) + 16 * ch, pk);
-        if (ch < 3) tc::tmem_wait_ld_into(buf[(ch + 1) & 1]);
-      }
+      for (int i = 0; i < 4; ++i) f2_unpack(ps2[i], ps[2 * i], ps[2 * i + 1]);
       l_run += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
       tc::tmem_wait_st();
       tc::fence_before_sync();
