@@ -520,6 +520,32 @@ def test_dense_prefill_tensor_core_vs_oracle(q_lens, kv_lens, Hq, H, causal):
     assert_no_device_error()
 
 
+def test_dense_prefill_tensor_core_rows_without_keys_are_zero():
+    """A request with fewer keys than queries (causal, aligned to the end of
+    the keys): its first rows see no key. The oracle's softmax over an empty
+    row is NaN; the kernel writes 0 there, including in a q-tile pair whose
+    other rows do see keys (every exponential of an all-masked row, on the SFU
+    or the FMA pipe, is 0). The other rows match the oracle."""
+    from qkv_b200.ops import dense_prefill
+
+    q_lens, kv_lens, Hq, H, D = [200, 64], [100, 64], 32, 8, 128
+    rng = np.random.default_rng(200)
+    q = O.bf16_round(rng.standard_normal((sum(q_lens), Hq, D)).astype(np.float32))
+    k = kv_data(rng, sum(kv_lens), H, D, 0.02, 5.0)
+    v = kv_data(rng, sum(kv_lens), H, D, 0.0, 1.0)
+    scale = D ** -0.5
+    out = torch.full((sum(q_lens), Hq, D), float("nan"), dtype=torch.bfloat16, device=dev())
+    dense_prefill(bf16_tensor(q), bf16_tensor(k), bf16_tensor(v), q_lens, kv_lens, scale, out, causal=True)
+    with np.errstate(invalid="ignore"):
+        want = O.dense_attention(q, k, v, q_lens, kv_lens, scale, causal=True)
+    empty = q_lens[0] - kv_lens[0]  # rows 0 .. 99 of request 0 see no key
+    assert np.isnan(want[:empty]).all() and not np.isnan(want[empty:]).any()
+    got = to_np(out)
+    assert (got[:empty] == 0.0).all()
+    assert_attention_close(got[empty:], want[empty:])
+    assert_no_device_error()
+
+
 def test_dense_prefill_tensor_core_is_deterministic_at_config4_scale():
     """The config-4 chunk shape (512-token chunks over 16k keys, GQA 4): two
     runs give identical bits, rows of a request with the same prefix of keys

@@ -129,16 +129,16 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
 // 2^f on [-1/2, 1/2] by Lawson's iteratively reweighted least squares
 // (exp2_poly_fit.py beside this file prints these float32 coefficients); its
 // largest relative error evaluated in fp32 is 7.5e-5, under the 2^-9 of the bf16
-// rounding P goes through next. Inputs are clamped to -126 so that adding n to
-// the exponent field cannot wrap: a masked score (-inf) gives about 2^-126
-// (1e-38) instead of 0, which no sum of this kernel can notice (each row's sum
-// is at least 1: the score that set the running max contributes 2^0).
+// rounding P goes through next. The softmax's arguments are at most a few
+// units above 0 (the lazy running max), so n + 127 stays below 255; below -126
+// (masked scores: -inf) the exponent field would wrap, and the result is
+// selected to 0 there, as the SFU's flush-to-zero ex2 gives: a row that sees
+// no key keeps a zero sum.
 constexpr float kExp2C0 = 0.99992806f, kExp2C1 = 0.69326097f, kExp2C2 = 0.24261114f, kExp2C3 = 0.055171669f;
 __device__ __forceinline__ void exp2_fma2(unsigned long long x2, float& p0, float& p1) {
   constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
   float x0, x1;
   f2_unpack(x2, x0, x1);
-  x2 = f2_pack(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
   const unsigned long long rnd = f2_pack(kRound, kRound);
   const unsigned long long t = f2_add(x2, rnd);
   const unsigned long long f = f2_sub(x2, f2_sub(t, rnd));
@@ -148,8 +148,8 @@ __device__ __forceinline__ void exp2_fma2(unsigned long long x2, float& p0, floa
   float q0, q1, t0, t1;
   f2_unpack(q, q0, q1);
   f2_unpack(t, t0, t1);
-  p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
-  p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
+  p0 = x0 >= -126.0f ? __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23)) : 0.0f;
+  p1 = x1 >= -126.0f ? __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23)) : 0.0f;
 }
 
 // Scores at columns >= lim of a 32-column chunk become -inf (causal mask).
