@@ -182,6 +182,91 @@ __global__ void __launch_bounds__(256) kivi_gather_tiled_kernel(const DecodePara
   }
   __syncthreads();
   const int64_t row0 = static_cast<int64_t>(cu_k[b]) + t0;
+  if constexpr (kD > 0 && kCh > 0 && kG >= kCh) {
+    // Constant geometry with one key group per chunk: a thread keeps the same
+    // 8 channels (word c) for all its tokens, so their key scales, minima and
+    // -16 x scales, and the choice of the fast form, are loop constants, and
+    // the row addresses advance by a fixed stride.
+    constexpr int kWords = kD / 8;
+    static_assert(256 % kWords == 0, "a block covers whole token rows");
+    const int c = threadIdx.x % kWords, tl0 = threadIdx.x / kWords;
+    constexpr int kStep = 256 / kWords;  // tokens per pass of the block
+    float sv[8], mv[8], nv[8];
+    bool fast = true;
+    const bool staged = page >= 0 && t0 < ts.k_begin;  // the key scales were staged above
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      sv[j] = staged ? gscale[8 * c + j] : 0.0f;
+      mv[j] = staged ? gmin[8 * c + j] : 0.0f;
+      nv[j] = staged ? gneg[8 * c + j] : 0.0f;
+      fast = fast && !isnan(nv[j]);  // a NaN -16 x scale marks a scale beyond kBigScale
+    }
+    const int64_t ostride = static_cast<int64_t>(kStep) * kvh * kD;
+    int64_t o = ((row0 + tl0) * kvh + h) * kD + 8 * c;
+    // value row of token tl: (page * blk + off0 + tl) * kvh + h
+    int64_t vrow = page >= 0 ? (page * p.blk + off0 + tl0) * kvh + h : 0;
+    const int vcg = (8 * c) / kG;  // value group of this thread's 8 dims
+    for (int tl = tl0; tl < n; tl += kStep, o += ostride, vrow += static_cast<int64_t>(kStep) * kvh) {
+      const int t = t0 + tl;
+      uint32_t ok[4], ov[4];
+      // ---- key
+      if (t >= ts.k_begin) {
+        const int slot = (ts.k_start + (t - ts.k_begin)) % p.res_cap;
+        const uint4 raw = *reinterpret_cast<const uint4*>(
+            p.rk + ((static_cast<int64_t>(ts.row) * p.res_cap + slot) * kvh + h) * kD + 8 * c);
+        ok[0] = raw.x; ok[1] = raw.y; ok[2] = raw.z; ok[3] = raw.w;
+      } else if (page < 0) {
+        ok[0] = ok[1] = ok[2] = ok[3] = 0u;
+      } else {
+        const uint32_t* cr = codes + (tl >> 3) * pitch + 8 * c;
+        const uint4 w0 = *reinterpret_cast<const uint4*>(cr);
+        const uint4 w1 = *reinterpret_cast<const uint4*>(cr + 4);
+        const int k = tl & 7;
+        const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        if (fast) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            ok[j] = pack_bf16x2(kivi_value_field(nibble_field(wv[2 * j], k), sv[2 * j], nv[2 * j], mv[2 * j]),
+                                kivi_value_field(nibble_field(wv[2 * j + 1], k), sv[2 * j + 1], nv[2 * j + 1],
+                                                 mv[2 * j + 1]));
+        } else {
+          const int sh = 4 * k;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            ok[j] = pack_bf16x2(kivi_value((wv[2 * j] >> sh) & 0xFu, sv[2 * j], mv[2 * j]),
+                                kivi_value((wv[2 * j + 1] >> sh) & 0xFu, sv[2 * j + 1], mv[2 * j + 1]));
+        }
+      }
+      // ---- value (token-major in the pages)
+      if (t >= ts.v_begin) {
+        const int slot = (ts.v_start + (t - ts.v_begin)) % p.res_cap;
+        const uint4 raw = *reinterpret_cast<const uint4*>(
+            p.rv + ((static_cast<int64_t>(ts.row) * p.res_cap + slot) * kvh + h) * kD + 8 * c);
+        ov[0] = raw.x; ov[1] = raw.y; ov[2] = raw.z; ov[3] = raw.w;
+      } else if (page < 0) {
+        ov[0] = ov[1] = ov[2] = ov[3] = 0u;
+      } else {
+        const uint32_t word = static_cast<uint32_t>(__ldg(p.vq + vrow * kWords + c));
+        const int64_t si = vrow * (kD / kG) + vcg;
+        const float sc = __ldg(p.vs + si), mn = __ldg(p.vm + si);
+        if (fabsf(sc) < kBigScale) {
+          const float n16 = __fmul_rn(-16.0f, sc);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            ov[j] = pack_bf16x2(kivi_value_field(nibble_field(word, 2 * j), sc, n16, mn),
+                                kivi_value_field(nibble_field(word, 2 * j + 1), sc, n16, mn));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            ov[j] = pack_bf16x2(kivi_value((word >> (8 * j)) & 0xFu, sc, mn),
+                                kivi_value((word >> (8 * j + 4)) & 0xFu, sc, mn));
+        }
+      }
+      *reinterpret_cast<uint4*>(dense_k + o) = make_uint4(ok[0], ok[1], ok[2], ok[3]);
+      *reinterpret_cast<uint4*>(dense_v + o) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
+    }
+    return;
+  }
   for (int i = threadIdx.x; i < n * words; i += blockDim.x) {
     const int tl = i / words, c = i - tl * words;
     const int t = t0 + tl;
