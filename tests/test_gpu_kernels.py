@@ -504,7 +504,7 @@ def test_dense_prefill_vs_oracle(q_lens, kv_lens, Hq, H, D, causal):
 ])
 def test_dense_prefill_tensor_core_vs_oracle(q_lens, kv_lens, Hq, H, causal):
     """Head 128 with 1, 2, 4 or 8 query heads per KV head runs the tcgen05
-    kernel (S and O in tensor memory, P in bf16 through shared memory)."""
+    kernel (S, P and O in tensor memory)."""
     from qkv_b200.ops import dense_prefill
 
     rng = np.random.default_rng(sum(q_lens) + sum(kv_lens))
